@@ -1,0 +1,369 @@
+"""Benchmark: Screening Attention fwd+bwd on B200 (BASELINE.json metric).
+
+Workload (cfg3 of BASELINE.json): isolated ScreeningAttention, d_model=1024,
+16 heads x 64, causal, batch 8 per GPU, T=4096, bf16, x ~ N(0,1), r_h ~ U[1,2],
+w_h ~ U[256,4096] (seeded).  One step = module forward + backward (q/k/v/out
+projections on cuBLAS, the screening core on this repo's kernels); with N>1
+GPUs every rank runs its own batch of 8 (weak scaling, batch sharding) and the
+projection-weight gradients are all-reduced over NCCL, as data-parallel
+training does.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  `--impl reference` times the reference
+algorithm's CPU implementation (the oracle restatement of
+multiscreen/attention.py, fp32, all host threads) on a bounded sample of the
+same workload (one sequence of T=4096 with all 16 heads per step).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+PKG = "pytorch-implementation-of-screening-attention_b200"
+
+D_MODEL, HEADS, HEAD_DIM, BATCH, SEQ = 1024, 16, 64, 8, 4096
+METRIC = "screening-attn fwd+bwd tokens/s (ScreeningAttention d=1024 H=16 D=64 causal T=4096, bf16)"
+WORKLOAD = ("cfg3: isolated ScreeningAttention d_model=1024, 16 heads x 64, causal, batch 8/GPU, "
+            "T=4096, bf16, r~U[1,2], w~U[256,4096], fwd+bwd")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def head_params(seed=0):
+    g = torch.Generator().manual_seed(seed)
+    r = 1.0 + torch.rand(HEADS, generator=g)
+    w = 256.0 + (4096.0 - 256.0) * torch.rand(HEADS, generator=g)
+    return r, w
+
+
+def windowed_pairs(w: torch.Tensor, T: int, causal=True) -> float:
+    """sum over heads of #(i, j) with j in the causal window of i."""
+    tot = 0
+    for wh in w.tolist():
+        d = max(-1, math.ceil(wh) - 1)
+        n = d + 1
+        if n >= T:
+            tot += T * (T + 1) // 2
+        else:
+            tot += n * (n + 1) // 2 + (T - n) * n
+    return float(tot)
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[3]) if v.lower() == "active"})
+        loaded = [r[0] for r in rows if r[2] > 200.0] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+def cpu_reference_sample(threads: int | None = None):
+    """Oracle fwd+bwd of one sequence (B=1, T=4096, 16 heads) in fp32 on the
+    host; returns (seconds, tokens, threads)."""
+    from oracle import screening_oracle as oracle
+    nt = threads or os.cpu_count() or 1
+    torch.set_num_threads(nt)
+    torch.manual_seed(0)
+    m = oracle.OracleScreeningAttention(D_MODEL, HEADS, windowed=True)
+    r, w = head_params()
+    with torch.no_grad():
+        m.s_r.copy_(torch.log(r - 1.0))
+        m.s_v.copy_(torch.log(w - 1.0))
+    x = torch.randn(1, SEQ, D_MODEL, generator=torch.Generator().manual_seed(1))
+    x.requires_grad_(True)
+    cot = torch.randn(1, SEQ, D_MODEL, generator=torch.Generator().manual_seed(2))
+    t0 = time.perf_counter()
+    y = m(x, x, x)
+    y.backward(cot)
+    return time.perf_counter() - t0, SEQ, nt
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    times = []
+    for i in range(args.warmup + args.steps):
+        dt, toks, nt = cpu_reference_sample()
+        if i >= args.warmup:
+            times.append(dt)
+    per = sum(times) / len(times)
+    val = SEQ / per
+    sample = f"1 sequence x T={SEQ} x {HEADS} heads (1/{BATCH} of one GPU's batch) per step, fp32"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "seq_len": SEQ, "global_batch": BATCH * args.gpus},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": nt, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=BATCH, help="per-GPU batch (profiling: smaller)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-reps", type=int, default=5)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import importlib
+    ms = importlib.import_module(PKG)
+    L = ms._lib
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dt, toks, nt = cpu_reference_sample()
+        cpu = {"value": toks / dt, "unit": "tokens/s", "cores": nt, "kind": "port",
+               "sample": f"oracle fwd+bwd, 1 sequence x T={SEQ} x {HEADS} heads, fp32, {dt:.1f} s"}
+
+    B = args.batch
+    torch.manual_seed(0)
+    attn = ms.ScreeningAttention(D_MODEL, HEADS).to(dev)
+    r_h, w_h = head_params()
+    with torch.no_grad():
+        attn.s_r.copy_(torch.log(r_h - 1.0))
+        attn.s_v.copy_(torch.log(w_h - 1.0))
+    attn = attn.to(torch.bfloat16)
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(B, SEQ, D_MODEL, device=dev, generator=gen).to(torch.bfloat16)
+    cot = torch.randn(B, SEQ, D_MODEL, device=dev, generator=gen).to(torch.bfloat16)
+    params = [p for p in attn.parameters()]
+
+    def step(inp):
+        for p in params:
+            p.grad = None
+        y = attn(inp, inp, inp)
+        y.backward(cot)
+        if dist is not None:
+            flat = torch.cat([p.grad.reshape(-1).float() for p in params])
+            dist.all_reduce(flat)
+        return y
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, L2 flushed between steps (outside the events)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for s0, s1 in evs:
+            flush.zero_()
+            s0.record()
+            step(x)
+            s1.record()
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    total_ms = sum(step_ms)
+    if dist is not None:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    tokens_per_step = B * SEQ * world
+    value = tokens_per_step / (ms_per_step / 1e3)
+
+    # ---- per-kernel timing of the screening core (CUDA events, same stream)
+    H, Dh = HEADS, HEAD_DIM
+    qkv = torch.nn.functional.linear(x, torch.cat([attn.q_proj.weight, attn.k_proj.weight,
+                                                   attn.v_proj.weight], 0)).view(B, SEQ, 3, H, Dh)
+    q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+    rr, ww = attn.sharpness().detach(), attn.window().detach()
+    stats = torch.zeros(2, dtype=torch.int64, device=dev)
+    y, no, nq, nk, nv, q2, k2, v2 = L.screen_fwd(q, k, v, rr, ww, True, tile_stats=stats)
+    dy = cot.view(B, SEQ, H, Dh)
+
+    def time_call(fn, reps):
+        out = []
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            out.append(a.elapsed_time(b))
+        return statistics.median(out)
+
+    kt = {
+        "norms": time_call(lambda: L.screen_fwd(q, k, v, rr, ww, True, stages=1), args.kernel_reps),
+        "fwd": time_call(lambda: L.screen_fwd(q, k, v, rr, ww, True, norms=(nq, nk, nv), stages=2),
+                         args.kernel_reps),
+        "bwd_prologue": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww,
+                                                       stages=1), args.kernel_reps),
+        "bwd_dq": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww, stages=3),
+                            args.kernel_reps),
+        "bwd_dkdv": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww,
+                                                   stages=5), args.kernel_reps),
+    }
+    # stages 3 / 5 include the prologue; isolate the attention kernels
+    kt["bwd_dq"] = max(kt["bwd_dq"] - kt["bwd_prologue"], 1e-6)
+    kt["bwd_dkdv"] = max(kt["bwd_dkdv"] - kt["bwd_prologue"], 1e-6)
+    stats.zero_()
+    L.screen_fwd(q, k, v, rr, ww, True, norms=(nq, nk, nv), stages=2, tile_stats=stats)
+    torch.cuda.synchronize()
+    visited, live = (int(t) for t in stats.tolist())
+
+    pairs_w = windowed_pairs(ww.cpu(), SEQ) * B
+    pairs_dense = H * SEQ * (SEQ + 1) / 2 * B
+    gemm = 2.0 * Dh  # flops per (i, j) pair per GEMM
+    kernel_flops = {"fwd": 2 * gemm * pairs_w, "bwd_dq": 3 * gemm * pairs_w,
+                    "bwd_dkdv": 4 * gemm * pairs_w}
+    dom = max(kernel_flops, key=lambda n: kt[n])
+    pk, pk_kind = peaks()
+    peak = float(pk["bf16_tflops"])
+    achieved = kernel_flops[dom] / (kt[dom] / 1e3) / 1e12
+    blk = 16 * 64 * gemm  # flops of one 16x64 score block per GEMM
+    fwd_exec = (visited + live) * blk
+    step_s = ms_per_step / 1e3
+    tflops = {
+        "dense_equiv": 7 * gemm * pairs_dense / step_s / 1e12 * world,
+        "windowed": 7 * gemm * pairs_w / step_s / 1e12 * world,
+        "fwd_executed_fraction_of_windowed": fwd_exec / (2 * gemm * pairs_w),
+    }
+    traffic = None
+    tfile = REPO / "profiles" / f"{dom}_traffic.txt"
+    if tfile.exists():
+        for ln in tfile.read_text().splitlines():
+            if ln.startswith("dram_bytes_per_launch_full_workload:"):
+                traffic = float(ln.split(":")[1])
+
+    # ---- end to end through the module with host buffers
+    x_host = x.cpu().pin_memory()
+    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e_ev = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        x_dev.copy_(x_host, non_blocking=True)
+        yy = step(x_dev)
+        loss_host.copy_(yy.float().square().mean().view(1), non_blocking=True)
+        b.record()
+        if i >= args.warmup:
+            e2e_ev.append((a, b))
+    torch.cuda.synchronize()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev) / len(e2e_ev)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "model": "ScreeningAttention(1024, 16)",
+                       "global_batch": B * world, "seq_len": SEQ,
+                       "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) between steps"},
+            "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": pk_kind,
+                         "traffic": traffic,
+                         "flops_basis": "windowed algorithmic pairs x 2*D per GEMM"},
+            "kernel_ms": kt, "tflops": tflops,
+            "tile_stats": {"fwd_blocks_in_window": visited, "fwd_blocks_live": live},
+            "cpu_baseline": cpu,
+            "e2e": {"value": tokens_per_step / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4},
+            "clocks": clk.summary(),
+            "gpu_launches": 6 * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

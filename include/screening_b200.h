@@ -1,0 +1,213 @@
+/*
+ * screening_b200.h -- C ABI of the B200 (sm_100a) Screening Attention kernels.
+ *
+ * Screening Attention ("Screening Is Enough", arXiv:2604.01178) as computed by
+ * multiscreen/attention.py:151-196 and multiscreen/norm.py:23-25 of the
+ * reference package `multiscreen`:
+ *
+ *   q^ = q / max(|q|, eps)    k^, v^ likewise              (attention.py:156-158)
+ *   S  = q^ k^T                                           (attention.py:161)
+ *   a  = relu(1 - r (1 - S)),  alpha = a^2                 (attention.py:75-90)
+ *   m  = (cos(pi rel / w) + 1) / 2 inside the window       (attention.py:92-119,174-183)
+ *        causal:     -w < rel <= 0      non-causal: |rel| < w,   rel = j - i
+ *   alpha *= m;  alpha[:, :, :, j] = 0 for padded keys j   (attention.py:186-188)
+ *   o  = alpha v^  (no normaliser)                         (attention.py:193)
+ *   y  = tanh(|o|) / max(|o|, eps) * o                     (norm.py:23-25)
+ *
+ * Layout: every (B, T, H, D) tensor is row-major with unit stride over D and
+ * stride D over H; the batch and time strides of the raw inputs are free
+ * (given in elements).  All buffers are device memory owned by the caller; the
+ * library never allocates or frees device memory and keeps no mutable global
+ * state besides a per-device attribute cache.  Every entry point returns 0 on
+ * success or a negative screen_status; nothing aborts and no C++ exception
+ * crosses this boundary.  Launches go to `stream` (a cudaStream_t).
+ *
+ * Supported: D in {16, 32, 64, 128}; dtype SCREEN_F32 (fp32 I/O, fp32 math) or
+ * SCREEN_BF16 (bf16 I/O, fp32 accumulation); any T_q, T_k >= 0.  Raw inputs
+ * need 16-byte aligned base pointers and strides that are multiples of 8
+ * elements (bf16) / 4 elements (fp32).
+ */
+#ifndef SCREENING_B200_H
+#define SCREENING_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SCREEN_ABI_VERSION 2
+
+#if defined(__GNUC__)
+#define SCREEN_API __attribute__((visibility("default")))
+#else
+#define SCREEN_API
+#endif
+
+typedef void* screen_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+enum screen_dtype { SCREEN_F32 = 0, SCREEN_BF16 = 1 };
+
+enum screen_status {
+  SCREEN_OK = 0,
+  SCREEN_ERR_INVALID_ARG = -1,     /* null pointer, negative size, bad enum   */
+  SCREEN_ERR_HEAD_DIM = -2,        /* D not in {16, 32, 64, 128}              */
+  SCREEN_ERR_DTYPE = -3,           /* dtype not SCREEN_F32 / SCREEN_BF16      */
+  SCREEN_ERR_ALIGNMENT = -4,       /* pointer or stride not 16-byte aligned   */
+  SCREEN_ERR_WORKSPACE = -5,       /* workspace missing or too small          */
+  SCREEN_ERR_LAUNCH = -6,          /* cudaGetLastError after a launch         */
+  SCREEN_ERR_TIMEOUT = -7,         /* a bounded device-side wait gave up      */
+  SCREEN_ERR_CUDA = -8,            /* other CUDA runtime error                */
+  SCREEN_ERR_UNSUPPORTED = -9      /* valid request this build does not do    */
+};
+
+/* ------------------------------------------------------------------------ */
+/* Forward.                                                                  */
+/* The kernels read the RAW projections and apply the unit-normalisation as  */
+/* fp32 per-row / per-column scales (S = (q.k) / (|q| |k|)), so bf16 inputs   */
+/* enter the tensor cores exactly and no normalised copy is written.         */
+/* ------------------------------------------------------------------------ */
+typedef struct screen_fwd_args {
+  int32_t dtype;                 /* enum screen_dtype of q, k, v, y           */
+  int32_t B, H, Tq, Tk, D;
+  int32_t causal;                /* nonzero: causal softmask                  */
+  int32_t norms_given;           /* nonzero: nq, nk, nv are inputs            */
+  int64_t q_offset;              /* key-axis position of query row 0; rel =   */
+                                 /*   j - (i + q_offset).  0 for self-attn    */
+  float eps;                     /* F.normalize / TanhNorm eps (1e-8)         */
+  int32_t stages;                /* 0 = all; else bitmask: 1 norms,           */
+                                 /*   2 attention (profiling)                 */
+  /* raw projections (B,T,H,D), strides in elements                          */
+  const void* q; int64_t q_sb, q_st;
+  const void* k; int64_t k_sb, k_st;
+  const void* v; int64_t v_sb, v_st;
+  const float* r;                /* (H,) acceptance sharpness r = exp(s_r)+1 */
+  const float* w;                /* (H,) window w = exp(s_v)+1               */
+  const uint8_t* key_padding_mask; /* (B,Tk), nonzero = ignore key; or NULL  */
+  int64_t kpm_sb;                /* batch stride of key_padding_mask          */
+  float* nq; float* nk; float* nv; /* (B,T,H) max(|x|, eps), contiguous      */
+  void* y;                       /* (B,Tq,H,D) TanhNorm(alpha v^), contiguous */
+  float* no;                     /* (B,Tq,H) |alpha v^| before TanhNorm       */
+  int64_t* tile_stats;           /* optional [2]: += 16x64 score blocks in    */
+                                 /*   the window, += blocks with live scores  */
+} screen_fwd_args;
+
+/* Fused screening forward (unit-normalisation, S, trim-and-square, softmask,
+ * key padding, alpha v^, TanhNorm).
+ * Replaces multiscreen/attention.py:156-196 and the op-level
+ * screening_attention_fwd (multiscreen/kernels/screening_fwd.py:216-270),
+ * whose inputs are pre-normalised (B,H,T,D) and whose output is pre-TanhNorm;
+ * here the unit-normalisation and TanhNorm are fused in. */
+SCREEN_API int screen_fwd(const screen_fwd_args* a, screen_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Backward.                                                                 */
+/* ------------------------------------------------------------------------ */
+typedef struct screen_bwd_args {
+  int32_t dtype;
+  int32_t B, H, Tq, Tk, D;
+  int32_t causal;
+  int32_t stages;                /* 0 = all; else bitmask: 1 TanhNorm grad,   */
+                                 /*   2 dq, 4 dk/dv, 8 dr/dw reduce           */
+  int64_t q_offset;
+  float eps;
+  int32_t _pad0;
+  /* forward inputs and what screen_fwd returned                             */
+  const void* q; int64_t q_sb, q_st;
+  const void* k; int64_t k_sb, k_st;
+  const void* v; int64_t v_sb, v_st;
+  const float* nq; const float* nk; const float* nv;
+  const void* y; const float* no;
+  /* incoming gradient dL/dy (B,Tq,H,D), strides in elements                 */
+  const void* dy; int64_t dy_sb, dy_st;
+  const float* r; const float* w;
+  const uint8_t* key_padding_mask; int64_t kpm_sb;
+  /* outputs: gradients of the RAW projections (B,T,H,D), strides in elements*/
+  void* dq; int64_t dq_sb, dq_st;
+  void* dk; int64_t dk_sb, dk_st;
+  void* dv; int64_t dv_sb, dv_st;
+  float* dr; float* dw;          /* (H,) dL/dr, dL/dw                         */
+  void* workspace; size_t workspace_bytes;
+} screen_bwd_args;
+
+/* Bytes of device workspace screen_bwd needs for these shapes. */
+SCREEN_API size_t screen_bwd_workspace_size(const screen_bwd_args* a);
+
+/* Gradients dq, dk, dv (through the unit-normalisation and TanhNorm
+ * Jacobians) and the per-head dr, dw.  Replaces autograd of
+ * multiscreen/attention.py:156-196 and screening_attention_bwd
+ * (multiscreen/kernels/screening_bwd.py:229-287), which returns no dr/dw. */
+SCREEN_API int screen_bwd(const screen_bwd_args* a, screen_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Paged K/V cache and single-token decode (serves MultiscreenLM.generate,    */
+/* replacing the full-prefix recompute at multiscreen/model.py:131-133).     */
+/* ------------------------------------------------------------------------ */
+typedef struct screen_kv_cache {
+  void* k_pages;                 /* [num_pages, H, page_size, D] unit rows    */
+  void* v_pages;                 /* same                                      */
+  const int32_t* block_table;    /* [B, max_blocks] page ids                  */
+  int32_t num_pages, page_size, max_blocks, _pad0;
+} screen_kv_cache;
+
+typedef struct screen_kv_append_args {
+  int32_t dtype;                 /* of k, v and the pages                     */
+  int32_t B, H, D, n_new;
+  float eps;
+  const void* k; int64_t k_sb, k_st;   /* raw (B,n_new,H,D)                   */
+  const void* v; int64_t v_sb, v_st;
+  const int32_t* positions;      /* (B,) position of token 0 of k, v         */
+  screen_kv_cache cache;
+} screen_kv_append_args;
+
+/* Unit-normalise n_new new key/value rows per sequence and write them into
+ * the paged cache at positions[b] .. positions[b]+n_new-1. */
+SCREEN_API int screen_kv_append(const screen_kv_append_args* a, screen_stream_t stream);
+
+typedef struct screen_decode_args {
+  int32_t dtype;
+  int32_t B, H, D;
+  int32_t num_splits;            /* key-axis splits per (b,h); >= 1           */
+  float eps;
+  const void* q; int64_t q_sb;   /* raw (B,H,D) query of the newest token     */
+  const int32_t* seq_lens;       /* (B,) tokens in cache incl. the newest one */
+  const float* r; const float* w;
+  screen_kv_cache cache;
+  void* y;                       /* (B,H,D) TanhNorm output                   */
+  float* no;                     /* (B,H) or NULL                             */
+  void* workspace; size_t workspace_bytes;
+} screen_decode_args;
+
+SCREEN_API size_t screen_decode_workspace_size(const screen_decode_args* a);
+
+/* One causal query per (b,h) at position seq_lens[b]-1 against the cached
+ * keys inside its window.  Equals the last row of screen_fwd over the whole
+ * prefix (the logits row generate() keeps at multiscreen/model.py:133). */
+SCREEN_API int screen_decode(const screen_decode_args* a, screen_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Stand-alone TanhNorm (multiscreen/norm.py:8-25) over contiguous rows of   */
+/* length D (any D >= 1).                                                    */
+/* ------------------------------------------------------------------------ */
+SCREEN_API int screen_tanhnorm_fwd(int32_t dtype, int64_t rows, int32_t D, float eps,
+                        const void* x, void* y, screen_stream_t stream);
+SCREEN_API int screen_tanhnorm_bwd(int32_t dtype, int64_t rows, int32_t D, float eps,
+                        const void* x, const void* dy, void* dx,
+                        screen_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Misc.                                                                     */
+/* ------------------------------------------------------------------------ */
+SCREEN_API const char* screen_strerror(int status);
+SCREEN_API int screen_version(void);                  /* SCREEN_ABI_VERSION             */
+/* sizeof of the argument structs, for binding checks: 0 fwd, 1 bwd,
+ * 2 kv_cache, 3 kv_append, 4 decode; -1 for an unknown id. */
+SCREEN_API int64_t screen_sizeof_args(int which);
+/* Last CUDA error string seen by this thread inside the library. */
+SCREEN_API const char* screen_last_cuda_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SCREENING_B200_H */

@@ -1,0 +1,122 @@
+"""ScreeningAttention on the B200 kernels -- drop-in for
+multiscreen/attention.py:23-200.
+
+Same constructor, forward signature, parameter names and initialisation
+(q/k/v/out_proj bias-free Linear; s_v = linspace(0, ln 255, H) so w = 2..256;
+s_r = 0 so r = 2; attention.py:52-66), so reference checkpoints load
+unchanged.  Everything between the projections and out_proj
+(attention.py:156-196) runs in one fused CUDA forward and one fused CUDA
+backward (functional.screening_attention).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib
+from .functional import screening_attention
+from .norm import TanhNorm
+
+
+class ScreeningAttention(nn.Module):
+    """Multi-head Screening Attention.
+
+    Args match the reference: d_model, num_heads, dropout (on alpha; the fused
+    kernels implement p = 0 only and raise in training mode for p > 0),
+    causal, eps.
+    """
+
+    def __init__(self, d_model: int, num_heads: int, dropout: float = 0.0, causal: bool = True,
+                 eps: float = 1e-8):
+        super().__init__()
+        assert d_model % num_heads == 0, "d_model must be divisible by num_heads"
+        self.d_model = d_model
+        self.num_heads = num_heads
+        self.head_dim = d_model // num_heads
+        self.causal = causal
+        self.eps = eps
+        self.q_proj = nn.Linear(d_model, d_model, bias=False)
+        self.k_proj = nn.Linear(d_model, d_model, bias=False)
+        self.v_proj = nn.Linear(d_model, d_model, bias=False)
+        self.out_proj = nn.Linear(d_model, d_model, bias=False)
+        self.s_v = nn.Parameter(torch.linspace(0, math.log(255), num_heads))   # log(w - 1)
+        self.s_r = nn.Parameter(torch.zeros(num_heads))                         # log(r - 1)
+        self.attn_dropout = nn.Dropout(dropout)
+        self.tahn_norm = TanhNorm(eps=eps)  # attribute name kept from the reference
+
+    # ------------------------------------------------------------------
+    def window(self) -> torch.Tensor:
+        """w = exp(s_v) + 1 (attention.py:164), float32."""
+        return torch.exp(self.s_v.float()) + 1.0
+
+    def sharpness(self) -> torch.Tensor:
+        """r = exp(s_r) + 1 (attention.py:165), float32."""
+        return torch.exp(self.s_r.float()) + 1.0
+
+    def _qkv(self, query, key, value):
+        B, Tq, _ = query.shape
+        Tk = key.shape[1]
+        H, D = self.num_heads, self.head_dim
+        if query is key and key is value:
+            # self-attention: one GEMM for the three projections; q, k, v are
+            # strided (B,T,H,D) views the kernel reads in place
+            wqkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
+            qkv = F.linear(query, wqkv).view(B, Tq, 3, H, D)
+            return qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+        q = self.q_proj(query).view(B, Tq, H, D)
+        k = self.k_proj(key).view(B, Tk, H, D)
+        v = self.v_proj(value).view(B, Tk, H, D)
+        return q, k, v
+
+    def _check_dropout(self):
+        if self.training and self.attn_dropout.p > 0 and torch.is_grad_enabled():
+            raise NotImplementedError(
+                "attention dropout > 0 in training is not implemented by the fused kernels")
+
+    def forward(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                key_padding_mask: torch.Tensor | None = None) -> torch.Tensor:
+        """query (B,T_q,d_model), key/value (B,T_k,d_model),
+        key_padding_mask (B,T_k) bool, True = ignore.  Returns (B,T_q,d_model)."""
+        self._check_dropout()
+        B, Tq, _ = query.shape
+        q, k, v = self._qkv(query, key, value)
+        y = screening_attention(q, k, v, self.sharpness(), self.window(), causal=self.causal,
+                                key_padding_mask=key_padding_mask, eps=self.eps)
+        return self.out_proj(y.reshape(B, Tq, self.d_model))
+
+    # ------------------------------------------------------------------
+    # KV-cached inference (used by MultiscreenLM.generate)
+    # ------------------------------------------------------------------
+    @torch.no_grad()
+    def prefill(self, x: torch.Tensor, cache, layer: int) -> torch.Tensor:
+        """Causal self-attention over a whole prompt x (B,T,d) that also
+        writes the prompt's last `cache.keep` unit keys/values into `cache`."""
+        B, T, _ = x.shape
+        q, k, v = self._qkv(x, x, x)
+        keep = min(T, cache.keep)
+        if keep > 0:
+            pos = torch.full((B,), T - keep, dtype=torch.int32, device=x.device)
+            cache.append(layer, k[:, T - keep:], v[:, T - keep:], pos, eps=self.eps)
+        y = screening_attention(q, k, v, self.sharpness(), self.window(), causal=True,
+                                eps=self.eps)
+        return self.out_proj(y.reshape(B, T, self.d_model))
+
+    @torch.no_grad()
+    def decode_step(self, x: torch.Tensor, cache, layer: int, positions: torch.Tensor,
+                    seq_lens: torch.Tensor, wqkv: torch.Tensor | None = None,
+                    r: torch.Tensor | None = None, w: torch.Tensor | None = None) -> torch.Tensor:
+        """One new token per sequence: x (B,1,d) at `positions` (B,) int32.
+        Appends its unit k/v to the cache and attends over the cached window."""
+        B = x.shape[0]
+        H, D = self.num_heads, self.head_dim
+        if wqkv is None:
+            wqkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
+        qkv = F.linear(x, wqkv).view(B, 1, 3, H, D)
+        cache.append(layer, qkv[:, :, 1], qkv[:, :, 2], positions, eps=self.eps)
+        y, _ = cache.decode(layer, qkv[:, 0, 0], seq_lens,
+                            self.sharpness() if r is None else r,
+                            self.window() if w is None else w, eps=self.eps)
+        return self.out_proj(y.reshape(B, 1, self.d_model))

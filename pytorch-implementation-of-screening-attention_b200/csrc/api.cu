@@ -1,0 +1,254 @@
+// extern "C" entry points of libscreening_b200.so (declared in
+// include/screening_b200.h).  Validation, workspace carving and kernel
+// dispatch; no allocation, no exceptions across the boundary.
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include "rowops.cuh"
+#include "decode.cuh"
+
+using namespace screen;
+
+namespace {
+
+thread_local char g_last_err[256] = "";
+
+int check_launch() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(g_last_err, sizeof(g_last_err), "%s", cudaGetErrorString(e));
+    return SCREEN_ERR_LAUNCH;
+  }
+  return SCREEN_OK;
+}
+
+bool dim_ok(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
+bool dtype_ok(int t) { return t == SCREEN_F32 || t == SCREEN_BF16; }
+size_t elem_size(int t) { return t == SCREEN_F32 ? 4 : 2; }
+bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+// raw (B,T,H,D) rows are read in 16-byte pieces
+bool strides_ok(long long sb, long long st) { return sb % 4 == 0 && st % 4 == 0; }
+bool raw_ok(int dtype, const void* p, long long sb, long long st) {
+  const long long vec = 16 / (long long)elem_size(dtype);
+  return al16(p) && sb % vec == 0 && st % vec == 0;
+}
+size_t round_up(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// SCREEN_FORCE_SIMT=1 routes bf16 D=64 to the SIMT kernels (a debugging aid
+// for comparing the two implementations on identical inputs).
+bool use_mma(int dtype, int D) {
+  static const bool force_simt = [] {
+    const char* e = getenv("SCREEN_FORCE_SIMT");
+    return e && e[0] == '1';
+  }();
+  return !force_simt && mma_supported(dtype, D);
+}
+
+int common_checks(int dtype, int B, int H, int Tq, int Tk, int D) {
+  if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;
+  if (!dim_ok(D)) return SCREEN_ERR_HEAD_DIM;
+  if (B < 0 || H < 0 || Tq < 0 || Tk < 0) return SCREEN_ERR_INVALID_ARG;
+  return SCREEN_OK;
+}
+
+AttnShape make_shape(int B, int H, int Tq, int Tk, int causal, long long q_offset, float eps,
+                     const float* r, const float* w, const uint8_t* kpm, long long kpm_sb) {
+  AttnShape s;
+  s.B = B; s.H = H; s.Tq = Tq; s.Tk = Tk; s.causal = causal; s.q_offset = q_offset;
+  s.eps = eps; s.r = r; s.w = w; s.kpm = kpm; s.kpm_sb = kpm_sb;
+  return s;
+}
+
+struct BwdLayout {
+  size_t g_off, pr_off, pw_off, total;
+  long long P;
+};
+BwdLayout bwd_layout(const screen_bwd_args* a) {
+  BwdLayout L;
+  AttnShape s = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
+                           a->key_padding_mask, a->kpm_sb);
+  L.P = use_mma(a->dtype, a->D) ? mma_bwd_partials(a->D, s) : simt_bwd_partials(s);
+  L.g_off = 0;
+  L.pr_off = round_up((size_t)a->B * a->Tq * a->H * a->D * elem_size(a->dtype));
+  L.pw_off = L.pr_off + round_up((size_t)a->H * L.P * sizeof(float));
+  L.total = L.pw_off + round_up((size_t)a->H * L.P * sizeof(float));
+  return L;
+}
+
+}  // namespace
+
+extern "C" {
+
+int screen_version(void) { return SCREEN_ABI_VERSION; }
+
+const char* screen_last_cuda_error(void) { return g_last_err; }
+
+const char* screen_strerror(int status) {
+  switch (status) {
+    case SCREEN_OK: return "success";
+    case SCREEN_ERR_INVALID_ARG: return "invalid argument (null pointer, negative size or bad flag)";
+    case SCREEN_ERR_HEAD_DIM: return "unsupported head dim (supported: 16, 32, 64, 128)";
+    case SCREEN_ERR_DTYPE: return "unsupported dtype (supported: float32, bfloat16)";
+    case SCREEN_ERR_ALIGNMENT: return "pointer not 16-byte aligned or stride not a multiple of 4 elements";
+    case SCREEN_ERR_WORKSPACE: return "workspace missing or smaller than the size query returned";
+    case SCREEN_ERR_LAUNCH: return "kernel launch failed (see screen_last_cuda_error)";
+    case SCREEN_ERR_TIMEOUT: return "a bounded device-side wait timed out";
+    case SCREEN_ERR_CUDA: return "CUDA runtime error (see screen_last_cuda_error)";
+    case SCREEN_ERR_UNSUPPORTED: return "request not supported by this build";
+    default: return "unknown status";
+  }
+}
+
+int64_t screen_sizeof_args(int which) {
+  switch (which) {
+    case 0: return (int64_t)sizeof(screen_fwd_args);
+    case 1: return (int64_t)sizeof(screen_bwd_args);
+    case 2: return (int64_t)sizeof(screen_kv_cache);
+    case 3: return (int64_t)sizeof(screen_kv_append_args);
+    case 4: return (int64_t)sizeof(screen_decode_args);
+    default: return -1;
+  }
+}
+
+int screen_fwd(const screen_fwd_args* a, screen_stream_t stream) {
+  if (!a) return SCREEN_ERR_INVALID_ARG;
+  int st = common_checks(a->dtype, a->B, a->H, a->Tq, a->Tk, a->D);
+  if (st) return st;
+  const int stages = a->stages ? a->stages : 3;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool nq = (long long)a->B * a->H * a->Tq > 0, nk = (long long)a->B * a->H * a->Tk > 0;
+  if (nq && (!a->q || !a->nq || !a->y || !a->no || !a->r || !a->w)) return SCREEN_ERR_INVALID_ARG;
+  if (nk && (!a->k || !a->v || !a->nk || !a->nv)) return SCREEN_ERR_INVALID_ARG;
+  if (!raw_ok(a->dtype, a->q, a->q_sb, a->q_st) || !raw_ok(a->dtype, a->k, a->k_sb, a->k_st) ||
+      !raw_ok(a->dtype, a->v, a->v_sb, a->v_st) || !al16(a->y))
+    return SCREEN_ERR_ALIGNMENT;
+  if (!a->norms_given && (stages & 1)) {
+    NormJob jobs[3];
+    int n = 0;
+    if (nq) jobs[n++] = NormJob{Rows{a->q, a->q_sb, a->q_st}, a->B, a->Tq, a->H, a->nq};
+    if (nk) {
+      jobs[n++] = NormJob{Rows{a->k, a->k_sb, a->k_st}, a->B, a->Tk, a->H, a->nk};
+      jobs[n++] = NormJob{Rows{a->v, a->v_sb, a->v_st}, a->B, a->Tk, a->H, a->nv};
+    }
+    if (n) row_norms(a->dtype, a->D, jobs, n, a->eps, s);
+    if ((st = check_launch())) return st;
+  }
+  if (!nq || !(stages & 2)) return SCREEN_OK;
+  AttnShape sh = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
+                            a->key_padding_mask, a->kpm_sb);
+  FwdPtrs p{Rows{a->q, a->q_sb, a->q_st}, Rows{a->k, a->k_sb, a->k_st},
+            Rows{a->v, a->v_sb, a->v_st}, a->nq, a->nk, a->nv, a->y, a->no, a->tile_stats};
+  if (use_mma(a->dtype, a->D))
+    mma_fwd(a->D, sh, p, s);
+  else
+    simt_fwd(a->dtype, a->D, sh, p, s);
+  return check_launch();
+}
+
+size_t screen_bwd_workspace_size(const screen_bwd_args* a) {
+  if (!a || common_checks(a->dtype, a->B, a->H, a->Tq, a->Tk, a->D)) return 0;
+  return bwd_layout(a).total;
+}
+
+int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
+  if (!a) return SCREEN_ERR_INVALID_ARG;
+  int st = common_checks(a->dtype, a->B, a->H, a->Tq, a->Tk, a->D);
+  if (st) return st;
+  const int stages = a->stages ? a->stages : 15;
+  if (a->H > 0 && (!a->r || !a->w || !a->dr || !a->dw)) return SCREEN_ERR_INVALID_ARG;
+  const bool nq = (long long)a->B * a->H * a->Tq > 0, nk = (long long)a->B * a->H * a->Tk > 0;
+  if (nq && (!a->q || !a->nq || !a->y || !a->no || !a->dy || !a->dq)) return SCREEN_ERR_INVALID_ARG;
+  if (nk && (!a->k || !a->v || !a->nk || !a->nv || !a->dk || !a->dv)) return SCREEN_ERR_INVALID_ARG;
+  if (!raw_ok(a->dtype, a->q, a->q_sb, a->q_st) || !raw_ok(a->dtype, a->k, a->k_sb, a->k_st) ||
+      !raw_ok(a->dtype, a->v, a->v_sb, a->v_st) || !raw_ok(a->dtype, a->dy, a->dy_sb, a->dy_st) ||
+      !raw_ok(a->dtype, a->dq, a->dq_sb, a->dq_st) || !raw_ok(a->dtype, a->dk, a->dk_sb, a->dk_st) ||
+      !raw_ok(a->dtype, a->dv, a->dv_sb, a->dv_st) || !al16(a->y) || !al16(a->workspace))
+    return SCREEN_ERR_ALIGNMENT;
+  BwdLayout L = bwd_layout(a);
+  if (L.total > 0 && (!a->workspace || a->workspace_bytes < L.total)) return SCREEN_ERR_WORKSPACE;
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+  void* G = ws + L.g_off;
+  float* pr = reinterpret_cast<float*>(ws + L.pr_off);
+  float* pw = reinterpret_cast<float*>(ws + L.pw_off);
+  if (nq && (stages & 1))
+    tanhnorm_grad_from_y(a->dtype, a->D, a->y, a->no, a->dy, a->dy_sb, a->dy_st, G, a->B, a->Tq,
+                         a->H, a->eps, s);
+  if ((st = check_launch())) return st;
+  AttnShape sh = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
+                            a->key_padding_mask, a->kpm_sb);
+  BwdPtrs p{Rows{a->q, a->q_sb, a->q_st}, Rows{a->k, a->k_sb, a->k_st},
+            Rows{a->v, a->v_sb, a->v_st}, a->nq, a->nk, a->nv, G,
+            OutRows{a->dq, a->dq_sb, a->dq_st}, OutRows{a->dk, a->dk_sb, a->dk_st},
+            OutRows{a->dv, a->dv_sb, a->dv_st}, pr, pw};
+  if (use_mma(a->dtype, a->D))
+    mma_bwd(a->D, sh, p, stages, s);
+  else
+    simt_bwd(a->dtype, a->D, sh, p, stages, s);
+  if ((st = check_launch())) return st;
+  if (a->H > 0 && (stages & 8)) reduce_param_grads(pr, pw, L.P, a->H, a->w, a->dr, a->dw, s);
+  return check_launch();
+}
+
+int screen_kv_append(const screen_kv_append_args* a, screen_stream_t stream) {
+  if (!a) return SCREEN_ERR_INVALID_ARG;
+  int st = common_checks(a->dtype, a->B, a->H, a->n_new, 0, a->D);
+  if (st) return st;
+  if ((long long)a->B * a->H * a->n_new == 0) return SCREEN_OK;
+  if (!a->k || !a->v || !a->positions || !a->cache.k_pages || !a->cache.v_pages ||
+      !a->cache.block_table || a->cache.page_size <= 0 || a->cache.max_blocks <= 0)
+    return SCREEN_ERR_INVALID_ARG;
+  if (!al16(a->k) || !al16(a->v) || !al16(a->cache.k_pages) || !al16(a->cache.v_pages))
+    return SCREEN_ERR_ALIGNMENT;
+  if (!strides_ok(a->k_sb, a->k_st) || !strides_ok(a->v_sb, a->v_st)) return SCREEN_ERR_ALIGNMENT;
+  kv_append(*a, (cudaStream_t)stream);
+  return check_launch();
+}
+
+size_t screen_decode_workspace_size(const screen_decode_args* a) {
+  if (!a || a->num_splits < 1 || a->B < 0 || a->H < 0 || !dim_ok(a->D)) return 0;
+  return round_up((size_t)a->B * a->H * a->num_splits * a->D * sizeof(float));
+}
+
+int screen_decode(const screen_decode_args* a, screen_stream_t stream) {
+  if (!a) return SCREEN_ERR_INVALID_ARG;
+  int st = common_checks(a->dtype, a->B, a->H, 0, 0, a->D);
+  if (st) return st;
+  if (a->num_splits < 1) return SCREEN_ERR_INVALID_ARG;
+  if ((long long)a->B * a->H == 0) return SCREEN_OK;
+  if (!a->q || !a->seq_lens || !a->r || !a->w || !a->y || !a->cache.k_pages ||
+      !a->cache.v_pages || !a->cache.block_table || a->cache.page_size <= 0 ||
+      a->cache.max_blocks <= 0)
+    return SCREEN_ERR_INVALID_ARG;
+  if (!al16(a->q) || !al16(a->cache.k_pages) || !al16(a->cache.v_pages) || !al16(a->workspace))
+    return SCREEN_ERR_ALIGNMENT;
+  if (a->q_sb % 4 != 0) return SCREEN_ERR_ALIGNMENT;
+  const size_t need = screen_decode_workspace_size(a);
+  if (!a->workspace || a->workspace_bytes < need) return SCREEN_ERR_WORKSPACE;
+  decode(*a, reinterpret_cast<float*>(a->workspace), (cudaStream_t)stream);
+  return check_launch();
+}
+
+int screen_tanhnorm_fwd(int32_t dtype, int64_t rows, int32_t D, float eps, const void* x,
+                        void* y, screen_stream_t stream) {
+  if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;
+  if (D < 1) return SCREEN_ERR_INVALID_ARG;
+  if (rows < 0) return SCREEN_ERR_INVALID_ARG;
+  if (rows == 0) return SCREEN_OK;
+  if (!x || !y) return SCREEN_ERR_INVALID_ARG;
+  tanhnorm(dtype, D, false, x, nullptr, y, rows, eps, (cudaStream_t)stream);
+  return check_launch();
+}
+
+int screen_tanhnorm_bwd(int32_t dtype, int64_t rows, int32_t D, float eps, const void* x,
+                        const void* dy, void* dx, screen_stream_t stream) {
+  if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;
+  if (D < 1) return SCREEN_ERR_INVALID_ARG;
+  if (rows < 0) return SCREEN_ERR_INVALID_ARG;
+  if (rows == 0) return SCREEN_OK;
+  if (!x || !dy || !dx) return SCREEN_ERR_INVALID_ARG;
+  tanhnorm(dtype, D, true, x, dy, dx, rows, eps, (cudaStream_t)stream);
+  return check_launch();
+}
+
+}  // extern "C"

@@ -1,0 +1,266 @@
+// Row-wise kernels: the clamped row norms of q/k/v that the unit-normalisation
+// of attention.py:156-158 divides by,
+// stand-alone TanhNorm forward/backward (norm.py:23-25), the TanhNorm
+// backward prologue of the attention backward, and the deterministic
+// per-head reduction of the dr / dw partials.
+#include "rowops.cuh"
+
+namespace screen {
+
+// 4 consecutive elements <-> float4
+template <typename T> struct Vec4;
+template <> struct Vec4<float> {
+  static __device__ __forceinline__ float4 load(const float* p) {
+    return *reinterpret_cast<const float4*>(p);
+  }
+  static __device__ __forceinline__ void store(float* p, float4 v) {
+    *reinterpret_cast<float4*>(p) = v;
+  }
+};
+template <> struct Vec4<__nv_bfloat16> {
+  static __device__ __forceinline__ float4 load(const __nv_bfloat16* p) {
+    uint2 u = *reinterpret_cast<const uint2*>(p);
+    float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y);
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, float4 v) {
+    uint2 u;
+    u.x = pack_bf16(v.x, v.y);
+    u.y = pack_bf16(v.z, v.w);
+    *reinterpret_cast<uint2*>(p) = u;
+  }
+};
+
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Clamped row norms max(|x|, eps) of up to three (B,T,H,D) tensors; one group
+// of G = D/4 lanes per row, blockIdx.y selects the tensor.
+template <typename T, int D>
+__global__ void row_norms_kernel(NormJob job0, NormJob job1, NormJob job2, int njobs, float eps) {
+  constexpr int G = D / 4;
+  constexpr int RPB = 256 / G;  // rows per block
+  if ((int)blockIdx.y >= njobs) return;
+  const NormJob& job = blockIdx.y == 0 ? job0 : (blockIdx.y == 1 ? job1 : job2);
+  long long row = (long long)blockIdx.x * RPB + threadIdx.x / G;
+  int lane = threadIdx.x % G;
+  long long nrows = (long long)job.B * job.T * job.H;
+  bool valid = row < nrows;
+  long long rr = valid ? row : 0;
+  long long h = rr % job.H;
+  long long t = (rr / job.H) % job.T;
+  long long b = rr / ((long long)job.H * job.T);
+  const T* src = reinterpret_cast<const T*>(job.x.p) + b * job.x.sb + t * job.x.st + h * D +
+                 lane * 4;
+  float4 v = valid ? Vec4<T>::load(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  ss = group_sum<G>(ss);
+  if (valid && lane == 0) job.norms[rr] = fmaxf(sqrtf(ss), eps);
+}
+
+template <typename T, int D>
+static void launch_row_norms(const NormJob* jobs, int njobs, float eps, cudaStream_t s) {
+  constexpr int G = D / 4;
+  constexpr int RPB = 256 / G;
+  long long maxrows = 0;
+  for (int i = 0; i < njobs; ++i) {
+    long long n = (long long)jobs[i].B * jobs[i].T * jobs[i].H;
+    if (n > maxrows) maxrows = n;
+  }
+  if (maxrows == 0) return;
+  dim3 grid((unsigned)((maxrows + RPB - 1) / RPB), njobs);
+  NormJob j1 = njobs > 1 ? jobs[1] : jobs[0];
+  NormJob j2 = njobs > 2 ? jobs[2] : jobs[0];
+  row_norms_kernel<T, D><<<grid, 256, 0, s>>>(jobs[0], j1, j2, njobs, eps);
+}
+
+void row_norms(int dtype, int D, const NormJob* jobs, int njobs, float eps, cudaStream_t s) {
+#define NORM_CASE(TT, DD) launch_row_norms<TT, DD>(jobs, njobs, eps, s)
+  if (dtype == SCREEN_F32) {
+    switch (D) {
+      case 16: NORM_CASE(float, 16); break;
+      case 32: NORM_CASE(float, 32); break;
+      case 64: NORM_CASE(float, 64); break;
+      case 128: NORM_CASE(float, 128); break;
+    }
+  } else {
+    switch (D) {
+      case 16: NORM_CASE(__nv_bfloat16, 16); break;
+      case 32: NORM_CASE(__nv_bfloat16, 32); break;
+      case 64: NORM_CASE(__nv_bfloat16, 64); break;
+      case 128: NORM_CASE(__nv_bfloat16, 128); break;
+    }
+  }
+#undef NORM_CASE
+}
+
+// ---------------------------------------------------------------------------
+// Stand-alone TanhNorm over contiguous rows of any length D (norm.py:23-25):
+// one warp per row, two passes over the row.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void tanhnorm_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, long long rows,
+                                    int D, float eps) {
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;  // whole warps exit together
+  const T* xr = x + row * D;
+  float ss = 0.f;
+  for (int d = lane; d < D; d += 32) {
+    const float v = to_f(xr[d]);
+    ss += v * v;
+  }
+  const float g = tanhnorm_scale(sqrtf(warp_sum(ss)), eps);
+  for (int d = lane; d < D; d += 32) y[row * D + d] = from_f<T>(to_f(xr[d]) * g);
+}
+
+// dx = g dy + [|x| > eps] g'(n)/n (x.dy) x
+template <typename T>
+__global__ void tanhnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ dy,
+                                    T* __restrict__ dx, long long rows, int D, float eps) {
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + row * D;
+  const T* dr = dy + row * D;
+  float ss = 0.f, xd = 0.f;
+  for (int d = lane; d < D; d += 32) {
+    const float v = to_f(xr[d]), g = to_f(dr[d]);
+    ss += v * v;
+    xd += v * g;
+  }
+  ss = warp_sum(ss);
+  xd = warp_sum(xd);
+  const float nraw = sqrtf(ss);
+  const float g = tanhnorm_scale(nraw, eps);
+  const float k = (nraw > eps) ? tanhnorm_bwd_coef(nraw) * g * g * xd : 0.f;
+  for (int d = lane; d < D; d += 32)
+    dx[row * D + d] = from_f<T>(g * to_f(dr[d]) + k * to_f(xr[d]));
+}
+
+void tanhnorm(int dtype, int D, bool bwd, const void* x, const void* dy, void* out,
+              long long rows, float eps, cudaStream_t s) {
+  if (rows == 0) return;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  if (dtype == SCREEN_F32) {
+    if (!bwd)
+      tanhnorm_fwd_kernel<float><<<grid, 256, 0, s>>>((const float*)x, (float*)out, rows, D, eps);
+    else
+      tanhnorm_bwd_kernel<float><<<grid, 256, 0, s>>>((const float*)x, (const float*)dy,
+                                                      (float*)out, rows, D, eps);
+  } else {
+    typedef __nv_bfloat16 bf;
+    if (!bwd)
+      tanhnorm_fwd_kernel<bf><<<grid, 256, 0, s>>>((const bf*)x, (bf*)out, rows, D, eps);
+    else
+      tanhnorm_bwd_kernel<bf><<<grid, 256, 0, s>>>((const bf*)x, (const bf*)dy, (bf*)out, rows,
+                                                   D, eps);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Attention-backward prologue: G = dL/do from dL/dy through TanhNorm, using
+// the saved output y = g o and the saved |o|.  G is written contiguous in the
+// compute dtype.
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void tanhnorm_grad_from_y_kernel(const T* __restrict__ y, const float* __restrict__ no,
+                                            const T* __restrict__ dy, long long dy_sb,
+                                            long long dy_st, T* __restrict__ G, int B, int T_,
+                                            int H, float eps) {
+  constexpr int Gl = D / 4;
+  constexpr int RPB = 256 / Gl;
+  long long row = (long long)blockIdx.x * RPB + threadIdx.x / Gl;
+  int lane = threadIdx.x % Gl;
+  long long rows = (long long)B * T_ * H;
+  bool valid = row < rows;
+  long long rr = valid ? row : 0;
+  long long h = rr % H, t = (rr / H) % T_, b = rr / ((long long)H * T_);
+  float4 yv = valid ? Vec4<T>::load(y + rr * D + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 d = valid ? Vec4<T>::load(dy + b * dy_sb + t * dy_st + h * D + lane * 4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+  float yd = group_sum<Gl>(yv.x * d.x + yv.y * d.y + yv.z * d.z + yv.w * d.w);
+  float nraw = valid ? no[rr] : 0.f;
+  float g = tanhnorm_scale(nraw, eps);
+  float k = (nraw > eps) ? tanhnorm_bwd_coef(nraw) * yd : 0.f;
+  if (valid)
+    Vec4<T>::store(G + rr * D + lane * 4,
+                   make_float4(g * d.x + k * yv.x, g * d.y + k * yv.y, g * d.z + k * yv.z,
+                               g * d.w + k * yv.w));
+}
+
+template <typename T, int D>
+static void launch_grad_from_y(const void* y, const float* no, const void* dy, long long sb,
+                               long long st, void* G, int B, int T_, int H, float eps,
+                               cudaStream_t s) {
+  constexpr int RPB = 256 / (D / 4);
+  long long rows = (long long)B * T_ * H;
+  if (rows == 0) return;
+  tanhnorm_grad_from_y_kernel<T, D><<<(unsigned)((rows + RPB - 1) / RPB), 256, 0, s>>>(
+      (const T*)y, no, (const T*)dy, sb, st, (T*)G, B, T_, H, eps);
+}
+
+void tanhnorm_grad_from_y(int dtype, int D, const void* y, const float* no, const void* dy,
+                          long long dy_sb, long long dy_st, void* G, int B, int T_, int H,
+                          float eps, cudaStream_t s) {
+#define GY_CASE(TT, DD) launch_grad_from_y<TT, DD>(y, no, dy, dy_sb, dy_st, G, B, T_, H, eps, s)
+  if (dtype == SCREEN_F32) {
+    switch (D) {
+      case 16: GY_CASE(float, 16); break;
+      case 32: GY_CASE(float, 32); break;
+      case 64: GY_CASE(float, 64); break;
+      case 128: GY_CASE(float, 128); break;
+    }
+  } else {
+    switch (D) {
+      case 16: GY_CASE(__nv_bfloat16, 16); break;
+      case 32: GY_CASE(__nv_bfloat16, 32); break;
+      case 64: GY_CASE(__nv_bfloat16, 64); break;
+      case 128: GY_CASE(__nv_bfloat16, 128); break;
+    }
+  }
+#undef GY_CASE
+}
+
+// ---------------------------------------------------------------------------
+// dr[h] = sum_p part_r[h][p];  dw[h] = pi / (2 w^2) * sum_p part_w[h][p].
+// Fixed summation order => deterministic.
+// ---------------------------------------------------------------------------
+__global__ void reduce_param_grads_kernel(const float* __restrict__ part_r,
+                                          const float* __restrict__ part_w, long long P,
+                                          const float* __restrict__ w, float* __restrict__ dr,
+                                          float* __restrict__ dw) {
+  int h = blockIdx.x;
+  __shared__ float sr[256], sw[256];
+  float ar = 0.f, aw = 0.f;
+  for (long long p = threadIdx.x; p < P; p += 256) {
+    ar += part_r[(long long)h * P + p];
+    aw += part_w[(long long)h * P + p];
+  }
+  sr[threadIdx.x] = ar;
+  sw[threadIdx.x] = aw;
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if ((int)threadIdx.x < s) {
+      sr[threadIdx.x] += sr[threadIdx.x + s];
+      sw[threadIdx.x] += sw[threadIdx.x + s];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    float wh = w[h];
+    dr[h] = sr[0];
+    dw[h] = sw[0] * (3.14159265358979323846f / (2.0f * wh * wh));
+  }
+}
+
+void reduce_param_grads(const float* part_r, const float* part_w, long long P, int H,
+                        const float* w, float* dr, float* dw, cudaStream_t s) {
+  reduce_param_grads_kernel<<<H, 256, 0, s>>>(part_r, part_w, P, w, dr, dw);
+}
+
+}  // namespace screen

@@ -1,0 +1,72 @@
+// Host-side declarations of the row-wise kernels (rowops.cu) and of the
+// attention kernel launchers (attn_simt.cu, attn_mma.cu).
+#pragma once
+#include "common.cuh"
+
+namespace screen {
+
+// A (B,T,H,D) tensor with unit stride over D, stride D over H and free
+// batch / time strides (elements).
+struct Rows {
+  const void* p;
+  long long sb, st;
+};
+struct OutRows {
+  void* p;
+  long long sb, st;
+};
+
+struct NormJob {
+  Rows x;
+  int B, T, H;
+  float* norms;        // contiguous (B,T,H): max(|x|, eps)
+};
+
+void row_norms(int dtype, int D, const NormJob* jobs, int njobs, float eps, cudaStream_t s);
+void tanhnorm(int dtype, int D, bool bwd, const void* x, const void* dy, void* out,
+              long long rows, float eps, cudaStream_t s);
+void tanhnorm_grad_from_y(int dtype, int D, const void* y, const float* no, const void* dy,
+                          long long dy_sb, long long dy_st, void* G, int B, int T_, int H,
+                          float eps, cudaStream_t s);
+void reduce_param_grads(const float* part_r, const float* part_w, long long P, int H,
+                        const float* w, float* dr, float* dw, cudaStream_t s);
+
+struct AttnShape {
+  int B, H, Tq, Tk;
+  int causal;
+  long long q_offset;
+  float eps;
+  const float* r;
+  const float* w;
+  const uint8_t* kpm;   // (B,Tk) or null
+  long long kpm_sb;
+};
+
+struct FwdPtrs {
+  Rows q, k, v;
+  const float* nq; const float* nk; const float* nv;
+  void* y; float* no;   // contiguous
+  int64_t* tile_stats;
+};
+
+struct BwdPtrs {
+  Rows q, k, v;
+  const float* nq; const float* nk; const float* nv;
+  const void* G;          // dL/do, contiguous (B,Tq,H,D)
+  OutRows dq, dk, dv;
+  float* part_r; float* part_w;   // [H][P] partials
+};
+
+// Generic SIMT kernels (fp32 math; any dtype, any supported D).
+void simt_fwd(int dtype, int D, const AttnShape& s, const FwdPtrs& p, cudaStream_t st);
+long long simt_bwd_partials(const AttnShape& s);
+void simt_bwd(int dtype, int D, const AttnShape& s, const BwdPtrs& p, int stages,
+              cudaStream_t st);
+
+// bf16 tensor-core kernels (D = 64).
+bool mma_supported(int dtype, int D);
+void mma_fwd(int D, const AttnShape& s, const FwdPtrs& p, cudaStream_t st);
+long long mma_bwd_partials(int D, const AttnShape& s);
+void mma_bwd(int D, const AttnShape& s, const BwdPtrs& p, int stages, cudaStream_t st);
+
+}  // namespace screen

@@ -1,0 +1,135 @@
+"""MultiscreenLM on the B200 kernels -- drop-in for multiscreen/model.py:12-141.
+
+forward() keeps the reference signature and result dict.  generate() keeps
+the reference signature and sampling (temperature, top-k, softmax,
+multinomial; model.py:131-140) but replaces the full-prefix recompute per
+token (model.py:133) by one prefill pass plus a KV-cached single-token decode
+per step, computing logits for the last position only.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .kv_cache import PagedKVCache
+from .layers import MultiscreenBlock
+
+
+class MultiscreenLM(nn.Module):
+    def __init__(self, vocab_size: int, d_model: int = 512, num_heads: int = 8,
+                 num_layers: int = 6, ffn_dim: int | None = None, max_seq_len: int = 2048,
+                 dropout: float = 0.0, tie_weights: bool = True):
+        super().__init__()
+        self.d_model = d_model
+        self.token_emb = nn.Embedding(vocab_size, d_model)
+        self.pos_emb = nn.Embedding(max_seq_len, d_model)
+        self.emb_dropout = nn.Dropout(dropout)
+        self.blocks = nn.ModuleList([
+            MultiscreenBlock(d_model=d_model, num_heads=num_heads, ffn_dim=ffn_dim,
+                             dropout=dropout, causal=True)
+            for _ in range(num_layers)
+        ])
+        self.norm = nn.RMSNorm(d_model)
+        self.lm_head = nn.Linear(d_model, vocab_size, bias=False)
+        if tie_weights:
+            self.lm_head.weight = self.token_emb.weight
+        self._init_weights()
+
+    def _init_weights(self):
+        """model.py:62-69: N(0, 0.02) for embeddings and every Linear."""
+        nn.init.normal_(self.token_emb.weight, std=0.02)
+        nn.init.normal_(self.pos_emb.weight, std=0.02)
+        for module in self.modules():
+            if isinstance(module, nn.Linear):
+                nn.init.normal_(module.weight, std=0.02)
+
+    def forward(self, input_ids: torch.Tensor, key_padding_mask: torch.Tensor | None = None,
+                labels: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
+        B, T = input_ids.shape
+        positions = torch.arange(T, device=input_ids.device).unsqueeze(0)
+        x = self.emb_dropout(self.token_emb(input_ids) + self.pos_emb(positions))
+        for block in self.blocks:
+            x = block(x, key_padding_mask=key_padding_mask)
+        x = self.norm(x)
+        logits = self.lm_head(x)
+        result = {"logits": logits}
+        if labels is not None:
+            result["loss"] = F.cross_entropy(logits.view(-1, logits.size(-1)), labels.view(-1),
+                                             ignore_index=-100)
+        return result
+
+    # ------------------------------------------------------------------
+    def _max_window(self) -> float:
+        ws = torch.cat([blk.attn.window().detach() for blk in self.blocks])
+        return float(ws.max()) if ws.numel() else 0.0
+
+    def make_cache(self, batch: int, max_len: int, dtype: torch.dtype | None = None,
+                   page_size: int = 64) -> PagedKVCache:
+        a0 = self.blocks[0].attn
+        dt = dtype or self.token_emb.weight.dtype
+        if dt not in (torch.float32, torch.bfloat16):
+            dt = torch.float32
+        return PagedKVCache(len(self.blocks), batch, a0.num_heads, a0.head_dim, max_len,
+                            self._max_window(), dt, self.token_emb.weight.device, page_size)
+
+    @torch.no_grad()
+    def prefill(self, input_ids: torch.Tensor, cache: PagedKVCache) -> torch.Tensor:
+        """Run the prompt once, fill `cache`, return last-position logits (B,V)."""
+        B, T = input_ids.shape
+        positions = torch.arange(T, device=input_ids.device).unsqueeze(0)
+        x = self.emb_dropout(self.token_emb(input_ids) + self.pos_emb(positions))
+        for li, blk in enumerate(self.blocks):
+            x = x + blk.attn.prefill(blk.norm1(x), cache, li)
+            x = x + blk.ffn(blk.norm2(x))
+        return self.lm_head(self.norm(x[:, -1:]))[:, -1]
+
+    @torch.no_grad()
+    def decode_step(self, tokens: torch.Tensor, position: int, cache: PagedKVCache,
+                    state: dict | None = None) -> torch.Tensor:
+        """tokens (B,1) at absolute `position`; returns logits (B,V)."""
+        B = tokens.shape[0]
+        dev = tokens.device
+        if state is None:
+            state = self._decode_state()
+        pos_t = torch.full((B,), position, dtype=torch.int32, device=dev)
+        x = self.token_emb(tokens) + self.pos_emb.weight[position].view(1, 1, -1)
+        for li, blk in enumerate(self.blocks):
+            wqkv, r, w = state["layers"][li]
+            x = x + blk.attn.decode_step(blk.norm1(x), cache, li, pos_t, pos_t + 1, wqkv, r, w)
+            x = x + blk.ffn(blk.norm2(x))
+        return self.lm_head(self.norm(x))[:, -1]
+
+    def _decode_state(self) -> dict:
+        layers = []
+        for blk in self.blocks:
+            a = blk.attn
+            wqkv = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0)
+            layers.append((wqkv, a.sharpness().contiguous(), a.window().contiguous()))
+        return {"layers": layers}
+
+    @torch.no_grad()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 100,
+                 temperature: float = 1.0, top_k: int | None = None) -> torch.Tensor:
+        """(B,T) prompt -> (B, T + max_new_tokens), sampling as model.py:134-140."""
+        self.eval()
+        if max_new_tokens <= 0:
+            return input_ids
+        B, T0 = input_ids.shape
+        if T0 + max_new_tokens - 1 > self.pos_emb.num_embeddings:
+            # the reference fails the same way inside pos_emb (model.py:90-92)
+            raise IndexError("index out of range in self: prompt + new tokens exceed max_seq_len")
+        cache = self.make_cache(B, T0 + max_new_tokens)
+        state = self._decode_state()
+        logits = self.prefill(input_ids, cache)
+        for step in range(max_new_tokens):
+            logits = logits / temperature
+            if top_k is not None:
+                values, _ = torch.topk(logits, top_k)
+                logits[logits < values[:, -1:]] = float("-inf")
+            probs = F.softmax(logits, dim=-1)
+            next_token = torch.multinomial(probs, num_samples=1)
+            input_ids = torch.cat([input_ids, next_token], dim=1)
+            if step + 1 < max_new_tokens:
+                logits = self.decode_step(next_token, T0 + step, cache, state)
+        return input_ids

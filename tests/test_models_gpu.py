@@ -1,0 +1,132 @@
+"""Module-, model- and decode-level parity on the GPU."""
+import math
+
+import pytest
+import torch
+
+from tests.conftest import rel_err
+from tests.helpers import golden_module
+
+MG = golden_module()
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def test_cfg1_module_fp32_vs_reference(ms, golden):
+    """cfg1: ScreeningAttention(512, 8), default init from seed 0, B=2, T=128,
+    fp32 fwd+bwd, against the reference's recorded numbers."""
+    rec = golden["cfg1"]
+    attn, x, cot = MG.cfg1_inputs(ms.ScreeningAttention)
+    attn = attn.to(DEV)
+    xr = x.to(DEV).requires_grad_(True)
+    out = attn(xr, xr, xr)
+    (out * cot.to(DEV)).sum().backward()
+    assert rel_err(out[:, ::8], rec["y_rows"]) <= 1e-4
+    assert rel_err(xr.grad[:, ::8], rec["dx_rows"]) <= 1e-4
+    probe = torch.randn(512, generator=torch.Generator().manual_seed(99)).to(DEV)
+    for name in ("q_proj", "k_proj", "v_proj", "out_proj"):
+        gw = getattr(attn, name).weight.grad
+        assert rel_err(gw @ probe, rec[f"{name}_grad_probe"]) <= 1e-4
+    assert rel_err(attn.s_r.grad, rec["ds_r"]) <= 1e-4
+    assert rel_err(attn.s_v.grad, rec["ds_v"]) <= 1e-4
+
+
+@pytest.mark.parametrize("name", list(MG.LM_CASES))
+def test_lm_fp32_vs_reference(ms, golden, name):
+    rec = golden["lm"][name]
+    spec = rec["spec"]
+    m = ms.MultiscreenLM(spec["vocab"], spec["d_model"], spec["H"], spec["L"], spec["ffn"],
+                         spec["max_seq_len"]).to(DEV)
+    m.load_state_dict(rec["state"])
+    g = torch.Generator().manual_seed(spec["seed"] + 1000)
+    ids = torch.randint(0, spec["vocab"], (spec["B"], spec["T"]), generator=g)
+    labels = ids.clone()
+    labels[:, :3] = -100
+    prompt = torch.randint(0, spec["vocab"], spec["prompt"], generator=g)
+    out = m(ids.to(DEV), labels=labels.to(DEV))
+    assert rel_err(out["logits"], rec["logits"]) <= 1e-4
+    assert out["loss"].item() == pytest.approx(rec["loss"].item(), rel=1e-4)
+    out["loss"].backward()
+    for li, blk in enumerate(m.blocks):
+        assert rel_err(blk.attn.s_r.grad, rec["s_r_grad"][li]) <= 1e-3
+        assert rel_err(blk.attn.s_v.grad, rec["s_v_grad"][li]) <= 1e-3
+    toks = m.generate(prompt.to(DEV), max_new_tokens=spec["new"], top_k=1)
+    assert torch.equal(toks.cpu(), rec["tokens"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D", [16, 64, 128])
+def test_decode_equals_forward_last_rows(ms, dtype, D):
+    """screen_decode over the paged ring cache == rows of screen_fwd over the
+    whole prefix, for every prefix length in a sweep."""
+    B, T, H = 3, 300, 2
+    g = torch.Generator(device=DEV).manual_seed(D)
+    q = torch.randn(B, T, H, D, device=DEV, generator=g).to(dtype)
+    k = (q.float() + 0.6 * torch.randn(B, T, H, D, device=DEV, generator=g)).to(dtype)
+    v = torch.randn(B, T, H, D, device=DEV, generator=g).to(dtype)
+    r = torch.tensor([1.1, 1.4], device=DEV)
+    w = torch.tensor([37.5, 150.0], device=DEV)
+    y_full = ms.screening_attention(q, k, v, r, w, True)
+    cache = ms.PagedKVCache(1, B, H, D, max_len=T, max_window=150.0, dtype=dtype, device=DEV,
+                            page_size=16)
+    assert cache.pages_per_seq < cache.max_blocks  # the ring actually wraps
+    for t in range(T):
+        pos = torch.full((B,), t, dtype=torch.int32, device=DEV)
+        cache.append(0, k[:, t:t + 1], v[:, t:t + 1], pos)
+        y, _ = cache.decode(0, q[:, t], pos + 1, r, w)
+        tol = 1e-4 if dtype == torch.float32 else 2e-2
+        assert rel_err(y, y_full[:, t]) <= tol, t
+
+
+def test_bf16_lm_generate_matches_full_recompute(ms):
+    """KV-cached generate == the reference's recompute-everything loop run on
+    the same (bf16) model with the same kernels, token for token."""
+    torch.manual_seed(0)
+    m = ms.MultiscreenLM(97, d_model=128, num_heads=2, num_layers=2, max_seq_len=128).to(DEV)
+    with torch.no_grad():
+        for blk in m.blocks:
+            blk.attn.s_r.fill_(math.log(0.05))
+            blk.attn.s_v.copy_(torch.tensor([2.0, 3.5]))
+    m = m.to(torch.bfloat16)
+    prompt = torch.randint(0, 97, (3, 30), device=DEV)
+    fast = m.generate(prompt, max_new_tokens=12, top_k=1)
+    ids = prompt
+    for _ in range(12):
+        logits = m(ids)["logits"][:, -1, :].float()
+        ids = torch.cat([ids, logits.argmax(-1, keepdim=True)], 1)
+    agree = (fast == ids).float().mean().item()
+    assert agree >= 0.95, agree
+
+
+def test_decoder_layer_cross_attention(ms, oracle):
+    torch.manual_seed(1)
+    layer = ms.MultiscreenDecoderLayer(64, 4).to(DEV)
+    x = torch.randn(2, 12, 64, device=DEV, requires_grad=True)
+    mem = torch.randn(2, 30, 64, device=DEV, requires_grad=True)
+    mask = torch.zeros(2, 30, dtype=torch.bool, device=DEV)
+    mask[1, 20:] = True
+    out = layer(x, mem, memory_key_padding_mask=mask)
+    out.sum().backward()
+    assert out.shape == x.shape and mem.grad is not None
+    # the cross-attention alone against the oracle module with the same weights
+    o = oracle.OracleScreeningAttention(64, 4, causal=False)
+    o.load_state_dict({k: v.cpu() for k, v in layer.cross_attn.state_dict().items()})
+    h = torch.randn(2, 12, 64)
+    ref = o(h, mem.detach().cpu(), mem.detach().cpu(), key_padding_mask=mask.cpu())
+    got = layer.cross_attn(h.to(DEV), mem.detach(), mem.detach(), key_padding_mask=mask)
+    assert rel_err(got, ref) <= 1e-4
+
+
+def test_tanhnorm_module_grad(ms, oracle):
+    x = torch.randn(37, 64, dtype=torch.float64) * 3
+    x[3] = 0
+    x[5] *= 1e-9
+    xr = x.float().clone().requires_grad_(True)
+    ref = oracle.tanh_norm(xr, 1e-8)
+    dy = torch.randn_like(ref)
+    ref.backward(dy)
+    xc = x.float().to(DEV).requires_grad_(True)
+    y = ms.TanhNorm()(xc)
+    y.backward(dy.to(DEV))
+    assert rel_err(y, ref) <= 1e-5
+    assert rel_err(xc.grad, xr.grad) <= 1e-4
