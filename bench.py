@@ -83,7 +83,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
@@ -173,6 +173,8 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH, help="per-GPU batch (profiling: smaller)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-reps", type=int, default=5)
+    ap.add_argument("--profile-only", action="store_true",
+                    help="warm-up steps + one step, nothing else (for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -194,7 +196,7 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.profile_only):
         dt, toks, nt = cpu_reference_sample()
         cpu = {"value": toks / dt, "unit": "tokens/s", "cores": nt, "kind": "port",
                "sample": f"oracle fwd+bwd, 1 sequence x T={SEQ} x {HEADS} heads, fp32, {dt:.1f} s"}
@@ -223,9 +225,18 @@ def main():
         return y
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    # clocks are sampled from the warm-up through the e2e loop (all GPU-bound);
+    # the median is taken over samples drawing > 200 W
+    clk = ClockSampler(local)
+    if not args.profile_only:
+        clk.__enter__()
     for _ in range(args.warmup):
         step(x)
     torch.cuda.synchronize()
+    if args.profile_only:
+        step(x)
+        torch.cuda.synchronize()
+        return
 
     # ---- timed region: K steps, L2 flushed between steps (outside the events)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -233,13 +244,12 @@ def main():
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        for s0, s1 in evs:
-            flush.zero_()
-            s0.record()
-            step(x)
-            s1.record()
-        torch.cuda.synchronize()
+    for s0, s1 in evs:
+        flush.zero_()
+        s0.record()
+        step(x)
+        s1.record()
+    torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     step_ms = [a.elapsed_time(b) for a, b in evs]
@@ -334,6 +344,7 @@ def main():
             e2e_ev.append((a, b))
     torch.cuda.synchronize()
     e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev) / len(e2e_ev)
+    clk.__exit__(None, None, None)
     if dist is not None:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -69,7 +69,8 @@ BwdLayout bwd_layout(const screen_bwd_args* a) {
                            a->key_padding_mask, a->kpm_sb);
   L.P = use_mma(a->dtype, a->D) ? mma_bwd_partials(a->D, s) : simt_bwd_partials(s);
   L.g_off = 0;
-  L.pr_off = round_up((size_t)a->B * a->Tq * a->H * a->D * elem_size(a->dtype));
+  // G: fp32, or two bf16 planes (hi, lo) on the tensor-core path -- 4 bytes/elem either way
+  L.pr_off = round_up((size_t)a->B * a->Tq * a->H * a->D * 4);
   L.pw_off = L.pr_off + round_up((size_t)a->H * L.P * sizeof(float));
   L.total = L.pw_off + round_up((size_t)a->H * L.P * sizeof(float));
   return L;
@@ -172,8 +173,8 @@ int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
   float* pr = reinterpret_cast<float*>(ws + L.pr_off);
   float* pw = reinterpret_cast<float*>(ws + L.pw_off);
   if (nq && (stages & 1))
-    tanhnorm_grad_from_y(a->dtype, a->D, a->y, a->no, a->dy, a->dy_sb, a->dy_st, G, a->B, a->Tq,
-                         a->H, a->eps, s);
+    tanhnorm_grad_from_y(a->dtype, a->D, a->y, a->no, a->dy, a->dy_sb, a->dy_st, G,
+                         use_mma(a->dtype, a->D), a->B, a->Tq, a->H, a->eps, s);
   if ((st = check_launch())) return st;
   AttnShape sh = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
                             a->key_padding_mask, a->kpm_sb);

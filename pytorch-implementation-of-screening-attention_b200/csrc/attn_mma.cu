@@ -350,16 +350,17 @@ __global__ void __launch_bounds__(kFwdThreads, 2) mma_fwd_kernel(AttnShape s, Fw
 //   with the raw k rows.
 // ===========================================================================
 constexpr int kDqBM = 128, kDqBN = 64, kDqThreads = 256;
-constexpr size_t kDqSmem = 2 * (size_t)kDqBM * kD * 2 + 4 * (size_t)kDqBN * kD * 2 +
+constexpr size_t kDqSmem = 3 * (size_t)kDqBM * kD * 2 + 4 * (size_t)kDqBN * kD * 2 +
                            2 * kDqBN * sizeof(float4) + 2 * kDqBN * sizeof(float);
 
 __global__ void __launch_bounds__(kDqThreads, 1) mma_bwd_dq_kernel(AttnShape s, BwdPtrs p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sQ = smem_u32(smem);
   const uint32_t sG = sQ + kDqBM * kD * 2;
-  const uint32_t sK = sG + kDqBM * kD * 2;
+  const uint32_t sGl = sG + kDqBM * kD * 2;
+  const uint32_t sK = sGl + kDqBM * kD * 2;
   const uint32_t sV = sK + 2 * kDqBN * kD * 2;
-  float4* sCol = reinterpret_cast<float4*>(smem + 2 * kDqBM * kD * 2 + 4 * kDqBN * kD * 2);
+  float4* sCol = reinterpret_cast<float4*>(smem + 3 * kDqBM * kD * 2 + 4 * kDqBN * kD * 2);
   float* sIk = reinterpret_cast<float*>(sCol + 2 * kDqBN);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -381,10 +382,12 @@ __global__ void __launch_bounds__(kDqThreads, 1) mma_bwd_dq_kernel(AttnShape s, 
   const bf16* kh = head_ptr(p.k, b, h);
   const bf16* vh = head_ptr(p.v, b, h);
   const bf16* gh = reinterpret_cast<const bf16*>(p.G) + ((long long)b * s.Tq * s.H + h) * kD;
+  const bf16* glh = gh + (long long)s.B * s.Tq * s.H * kD;  // G_lo plane
   const long long nkb = (long long)b * s.Tk * s.H + h;
 
   load_tile<kDqBM, kDqThreads>(sQ, qh, p.q.st, i0, s.Tq, tid);
   load_tile<kDqBM, kDqThreads>(sG, gh, (long long)s.H * kD, i0, s.Tq, tid);
+  load_tile<kDqBM, kDqThreads>(sGl, glh, (long long)s.H * kD, i0, s.Tq, tid);
   const int kt0 = any ? (int)(lo / kDqBN) : 0;
   const int kt1 = any ? (int)(hi / kDqBN) : -1;
   auto col_info = [&](int kt, int buf) {
@@ -471,6 +474,11 @@ __global__ void __launch_bounds__(kDqThreads, 1) mma_bwd_dq_kernel(AttnShape s, 
 #pragma unroll
         for (int n = 0; n < 8; ++n) dp[n][0] = dp[n][1] = dp[n][2] = dp[n][3] = 0.f;
         gemm_abt(dp, gf, vb, lane);
+        {
+          uint32_t gl[kKS][4];
+          load_a_frags(sGl, warp * 16, lane, gl);
+          gemm_abt(dp, gl, vb, lane);
+        }
         const bool inside = block_inside(dlo, dhi, dmax, causal);
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
@@ -499,7 +507,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) mma_bwd_dq_kernel(AttnShape s, 
 //   Column (query) scale 1/|q| on S and dS; row (key) scales 1/|k|, 1/|v|.
 // ===========================================================================
 constexpr int kKvBN = 128, kKvBQ = 64, kKvThreads = 256;
-constexpr size_t kKvSmem = 2 * (size_t)kKvBN * kD * 2 + 4 * (size_t)kKvBQ * kD * 2 +
+constexpr size_t kKvSmem = 2 * (size_t)kKvBN * kD * 2 + 6 * (size_t)kKvBQ * kD * 2 +
                            2 * kKvBQ * sizeof(float4);
 
 __global__ void __launch_bounds__(kKvThreads, 1) mma_bwd_dkdv_kernel(AttnShape s, BwdPtrs p) {
@@ -509,7 +517,8 @@ __global__ void __launch_bounds__(kKvThreads, 1) mma_bwd_dkdv_kernel(AttnShape s
   const uint32_t sV = sK + kKvBN * kD * 2;
   const uint32_t sQ = sV + kKvBN * kD * 2;
   const uint32_t sG = sQ + 2 * kKvBQ * kD * 2;
-  float4* sCol = reinterpret_cast<float4*>(smem + 2 * kKvBN * kD * 2 + 4 * kKvBQ * kD * 2);
+  const uint32_t sGl = sG + 2 * kKvBQ * kD * 2;
+  float4* sCol = reinterpret_cast<float4*>(smem + 2 * kKvBN * kD * 2 + 6 * kKvBQ * kD * 2);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
@@ -532,6 +541,7 @@ __global__ void __launch_bounds__(kKvThreads, 1) mma_bwd_dkdv_kernel(AttnShape s
   const bf16* kh = head_ptr(p.k, b, h);
   const bf16* vh = head_ptr(p.v, b, h);
   const bf16* gh = reinterpret_cast<const bf16*>(p.G) + ((long long)b * s.Tq * s.H + h) * kD;
+  const bf16* glh = gh + (long long)s.B * s.Tq * s.H * kD;  // G_lo plane
   const long long gst = (long long)s.H * kD;
 
   load_tile<kKvBN, kKvThreads>(sK, kh, p.k.st, j0, s.Tk, tid);
@@ -551,6 +561,7 @@ __global__ void __launch_bounds__(kKvThreads, 1) mma_bwd_dkdv_kernel(AttnShape s
   if (any) {
     load_tile<kKvBQ, kKvThreads>(sQ, qh, p.q.st, (long long)qt0 * kKvBQ, s.Tq, tid);
     load_tile<kKvBQ, kKvThreads>(sG, gh, gst, (long long)qt0 * kKvBQ, s.Tq, tid);
+    load_tile<kKvBQ, kKvThreads>(sGl, glh, gst, (long long)qt0 * kKvBQ, s.Tq, tid);
     col_info(qt0, 0);
   }
   cp_async_commit();
@@ -600,6 +611,7 @@ __global__ void __launch_bounds__(kKvThreads, 1) mma_bwd_dkdv_kernel(AttnShape s
       const uint32_t off = (buf ^ 1) * kKvBQ * kD * 2;
       load_tile<kKvBQ, kKvThreads>(sQ + off, qh, p.q.st, (long long)(qt + 1) * kKvBQ, s.Tq, tid);
       load_tile<kKvBQ, kKvThreads>(sG + off, gh, gst, (long long)(qt + 1) * kKvBQ, s.Tq, tid);
+      load_tile<kKvBQ, kKvThreads>(sGl + off, glh, gst, (long long)(qt + 1) * kKvBQ, s.Tq, tid);
       cp_async_commit();
       col_info(qt + 1, buf ^ 1);
       cp_async_wait<1>();
@@ -631,6 +643,7 @@ __global__ void __launch_bounds__(kKvThreads, 1) mma_bwd_dkdv_kernel(AttnShape s
 #pragma unroll
         for (int n = 0; n < 8; ++n) dp[n][0] = dp[n][1] = dp[n][2] = dp[n][3] = 0.f;
         gemm_abt(dp, vf, gb, lane);
+        gemm_abt(dp, vf, sGl + buf * kKvBQ * kD * 2, lane);
         const bool inside = block_inside(dlo, dhi, dmax, causal);
 #pragma unroll
         for (int n = 0; n < 8; ++n) {

@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(256) simt_bwd_dq_kernel(AttnShape s, BwdPtrs p
   const long long qrow = ((long long)b * s.Tq + i) * s.H + h;
   float q[NE], g[NE], dq[NE], kk[NE], vv[NE];
   load_unit<T, D>(p.q, p.nq, b, i, s.Tq, s.H, h, q, lane);
-  load_row<T, D>(reinterpret_cast<const T*>(p.G) + qrow * D, g, lane);
+  load_row<float, D>(reinterpret_cast<const float*>(p.G) + qrow * D, g, lane);
 #pragma unroll
   for (int e = 0; e < NE; ++e) dq[e] = 0.f;
   for (long long j = lo; j <= hi && dmax >= 0; ++j) {
@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(256) simt_bwd_dkdv_kernel(AttnShape s, BwdPtrs
   const int dmax = window_dmax(w);
   float acc_r = 0.f, acc_w = 0.f;
   if (j < s.Tk) {
-    const T* Gp = reinterpret_cast<const T*>(p.G);
+    const float* Gp = reinterpret_cast<const float*>(p.G);
     const long long krow = ((long long)b * s.Tk + j) * s.H + h;
     float k[NE], v[NE], dk[NE], dv[NE], qq[NE], gg[NE];
     load_unit<T, D>(p.k, p.nk, b, j, s.Tk, s.H, h, k, lane);
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(256) simt_bwd_dkdv_kernel(AttnShape s, BwdPtrs
       for (long long i = ilo; i <= ihi; ++i) {
         const long long qrow = ((long long)b * s.Tq + i) * s.H + h;
         load_unit<T, D>(p.q, p.nq, b, i, s.Tq, s.H, h, qq, lane);
-        load_row<T, D>(Gp + qrow * D, gg, lane);
+        load_row<float, D>(Gp + qrow * D, gg, lane);
         float d1 = 0.f, d2 = 0.f;
 #pragma unroll
         for (int e = 0; e < NE; ++e) {

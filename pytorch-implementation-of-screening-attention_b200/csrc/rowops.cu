@@ -164,14 +164,16 @@ void tanhnorm(int dtype, int D, bool bwd, const void* x, const void* dy, void* o
 
 // ---------------------------------------------------------------------------
 // Attention-backward prologue: G = dL/do from dL/dy through TanhNorm, using
-// the saved output y = g o and the saved |o|.  G is written contiguous in the
-// compute dtype.
+// the saved output y = g o and the saved |o|, contiguous (B,Tq,H,D).
+// split = false: G in fp32.  split = true (tensor-core path): two bf16
+// planes G_hi = bf16(G) and G_lo = bf16(G - G_hi), rows*D elements apart, so
+// G_hi + G_lo carries ~16 mantissa bits into the dP = G v^T GEMM.
 // ---------------------------------------------------------------------------
 template <typename T, int D>
 __global__ void tanhnorm_grad_from_y_kernel(const T* __restrict__ y, const float* __restrict__ no,
                                             const T* __restrict__ dy, long long dy_sb,
-                                            long long dy_st, T* __restrict__ G, int B, int T_,
-                                            int H, float eps) {
+                                            long long dy_st, void* __restrict__ G, bool split,
+                                            int B, int T_, int H, float eps) {
   constexpr int Gl = D / 4;
   constexpr int RPB = 256 / Gl;
   long long row = (long long)blockIdx.x * RPB + threadIdx.x / Gl;
@@ -187,27 +189,39 @@ __global__ void tanhnorm_grad_from_y_kernel(const T* __restrict__ y, const float
   float nraw = valid ? no[rr] : 0.f;
   float g = tanhnorm_scale(nraw, eps);
   float k = (nraw > eps) ? tanhnorm_bwd_coef(nraw) * yd : 0.f;
-  if (valid)
-    Vec4<T>::store(G + rr * D + lane * 4,
-                   make_float4(g * d.x + k * yv.x, g * d.y + k * yv.y, g * d.z + k * yv.z,
-                               g * d.w + k * yv.w));
+  if (!valid) return;
+  const float4 gv = make_float4(g * d.x + k * yv.x, g * d.y + k * yv.y, g * d.z + k * yv.z,
+                                g * d.w + k * yv.w);
+  if (!split) {
+    Vec4<float>::store(reinterpret_cast<float*>(G) + rr * D + lane * 4, gv);
+  } else {
+    __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(G);
+    const float4 h4 = make_float4(__bfloat162float(__float2bfloat16_rn(gv.x)),
+                                  __bfloat162float(__float2bfloat16_rn(gv.y)),
+                                  __bfloat162float(__float2bfloat16_rn(gv.z)),
+                                  __bfloat162float(__float2bfloat16_rn(gv.w)));
+    Vec4<__nv_bfloat16>::store(hi + rr * D + lane * 4, h4);
+    Vec4<__nv_bfloat16>::store(hi + rows * D + rr * D + lane * 4,
+                               make_float4(gv.x - h4.x, gv.y - h4.y, gv.z - h4.z, gv.w - h4.w));
+  }
 }
 
 template <typename T, int D>
 static void launch_grad_from_y(const void* y, const float* no, const void* dy, long long sb,
-                               long long st, void* G, int B, int T_, int H, float eps,
+                               long long st, void* G, bool split, int B, int T_, int H, float eps,
                                cudaStream_t s) {
   constexpr int RPB = 256 / (D / 4);
   long long rows = (long long)B * T_ * H;
   if (rows == 0) return;
   tanhnorm_grad_from_y_kernel<T, D><<<(unsigned)((rows + RPB - 1) / RPB), 256, 0, s>>>(
-      (const T*)y, no, (const T*)dy, sb, st, (T*)G, B, T_, H, eps);
+      (const T*)y, no, (const T*)dy, sb, st, G, split, B, T_, H, eps);
 }
 
 void tanhnorm_grad_from_y(int dtype, int D, const void* y, const float* no, const void* dy,
-                          long long dy_sb, long long dy_st, void* G, int B, int T_, int H,
-                          float eps, cudaStream_t s) {
-#define GY_CASE(TT, DD) launch_grad_from_y<TT, DD>(y, no, dy, dy_sb, dy_st, G, B, T_, H, eps, s)
+                          long long dy_sb, long long dy_st, void* G, bool split, int B, int T_,
+                          int H, float eps, cudaStream_t s) {
+#define GY_CASE(TT, DD) \
+  launch_grad_from_y<TT, DD>(y, no, dy, dy_sb, dy_st, G, split, B, T_, H, eps, s)
   if (dtype == SCREEN_F32) {
     switch (D) {
       case 16: GY_CASE(float, 16); break;

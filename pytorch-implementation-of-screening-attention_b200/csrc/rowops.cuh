@@ -26,8 +26,8 @@ void row_norms(int dtype, int D, const NormJob* jobs, int njobs, float eps, cuda
 void tanhnorm(int dtype, int D, bool bwd, const void* x, const void* dy, void* out,
               long long rows, float eps, cudaStream_t s);
 void tanhnorm_grad_from_y(int dtype, int D, const void* y, const float* no, const void* dy,
-                          long long dy_sb, long long dy_st, void* G, int B, int T_, int H,
-                          float eps, cudaStream_t s);
+                          long long dy_sb, long long dy_st, void* G, bool split, int B, int T_,
+                          int H, float eps, cudaStream_t s);
 void reduce_param_grads(const float* part_r, const float* part_w, long long P, int H,
                         const float* w, float* dr, float* dw, cudaStream_t s);
 
@@ -52,7 +52,8 @@ struct FwdPtrs {
 struct BwdPtrs {
   Rows q, k, v;
   const float* nq; const float* nk; const float* nv;
-  const void* G;          // dL/do, contiguous (B,Tq,H,D)
+  const void* G;          // dL/do, contiguous (B,Tq,H,D): fp32 (SIMT path) or
+                          // bf16 hi plane followed by bf16 lo plane (tensor cores)
   OutRows dq, dk, dv;
   float* part_r; float* part_w;   // [H][P] partials
 };
