@@ -59,7 +59,8 @@ enum screen_status {
   SCREEN_ERR_LAUNCH = -6,          /* cudaGetLastError after a launch         */
   SCREEN_ERR_TIMEOUT = -7,         /* a bounded device-side wait gave up      */
   SCREEN_ERR_CUDA = -8,            /* other CUDA runtime error                */
-  SCREEN_ERR_UNSUPPORTED = -9      /* valid request this build does not do    */
+  SCREEN_ERR_UNSUPPORTED = -9,     /* valid request this build does not do    */
+  SCREEN_ERR_SCRATCH_LIMIT = -10   /* needs more than the static scratch      */
 };
 
 /* ------------------------------------------------------------------------ */
@@ -185,6 +186,22 @@ SCREEN_API size_t screen_decode_workspace_size(const screen_decode_args* a);
  * keys inside its window.  Equals the last row of screen_fwd over the whole
  * prefix (the logits row generate() keeps at multiscreen/model.py:133). */
 SCREEN_API int screen_decode(const screen_decode_args* a, screen_stream_t stream);
+
+/* Bytes of the static device scratch array used by screen_decode_noalloc. */
+#define SCREEN_DECODE_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* screen_decode without a workspace.  No counterpart in the reference.
+ * For callers that cannot allocate device memory on their serving path (a
+ * process whose device footprint is fixed after start-up, or a C / FFI caller
+ * with no device allocator to provide a workspace).  The split-K partials go
+ * to a static 4 MiB device array (SCREEN_DECODE_NOALLOC_SCRATCH_BYTES) that
+ * every GPU loading this library keeps until exit; requests needing more
+ * (B * H * num_splits * D * 4 bytes) return SCREEN_ERR_SCRATCH_LIMIT.  The
+ * array's device address is looked up on the first call on each device, so
+ * make that first call before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race and must be serialised by the
+ * caller.  `workspace` / `workspace_bytes` are ignored.  Allocates nothing. */
+SCREEN_API int screen_decode_noalloc(const screen_decode_args* a, screen_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Stand-alone TanhNorm (multiscreen/norm.py:8-25) over contiguous rows of   */

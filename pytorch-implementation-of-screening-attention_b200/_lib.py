@@ -85,7 +85,7 @@ EXPORTED = (
     "screen_fwd", "screen_bwd", "screen_bwd_workspace_size", "screen_kv_append",
     "screen_decode", "screen_decode_workspace_size", "screen_tanhnorm_fwd",
     "screen_tanhnorm_bwd", "screen_strerror", "screen_version", "screen_sizeof_args",
-    "screen_last_cuda_error",
+    "screen_last_cuda_error", "screen_decode_noalloc",
 )
 ABI_VERSION = 2
 
@@ -110,6 +110,7 @@ def load() -> ctypes.CDLL:
     lib.screen_decode.argtypes = [P(DecodeArgs), c_void_p]
     lib.screen_decode_workspace_size.argtypes = [P(DecodeArgs)]
     lib.screen_decode_workspace_size.restype = c_size_t
+    lib.screen_decode_noalloc.argtypes = [P(DecodeArgs), c_void_p]
     lib.screen_tanhnorm_fwd.argtypes = [c_int32, c_int64, c_int32, c_float, c_void_p, c_void_p,
                                         c_void_p]
     lib.screen_tanhnorm_bwd.argtypes = [c_int32, c_int64, c_int32, c_float, c_void_p, c_void_p,

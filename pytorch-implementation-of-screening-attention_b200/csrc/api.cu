@@ -96,6 +96,9 @@ const char* screen_strerror(int status) {
     case SCREEN_ERR_TIMEOUT: return "a bounded device-side wait timed out";
     case SCREEN_ERR_CUDA: return "CUDA runtime error (see screen_last_cuda_error)";
     case SCREEN_ERR_UNSUPPORTED: return "request not supported by this build";
+    case SCREEN_ERR_SCRATCH_LIMIT:
+      return "request needs more than the static scratch of screen_decode_noalloc "
+             "(B * H * num_splits * D * 4 bytes must be <= SCREEN_DECODE_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown status";
   }
 }

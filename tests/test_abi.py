@@ -34,7 +34,7 @@ def test_struct_sizes_and_version(ms):
 
 def test_strerror_covers_codes(ms):
     lib = ms._lib.load()
-    for code in range(0, -10, -1):
+    for code in range(0, -11, -1):
         assert lib.screen_strerror(code).decode() != "unknown status"
     assert lib.screen_strerror(-77).decode() == "unknown status"
 
