@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define SCREEN_ABI_VERSION 2
+#define SCREEN_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define SCREEN_API __attribute__((visibility("default")))
@@ -92,7 +92,13 @@ typedef struct screen_fwd_args {
   float* no;                     /* (B,Tq,H) |alpha v^| before TanhNorm       */
   int64_t* tile_stats;           /* optional [2]: += 16x64 score blocks in    */
                                  /*   the window, += blocks with live scores  */
+  void* workspace;               /* screen_fwd_workspace_size() bytes         */
+  size_t workspace_bytes;
 } screen_fwd_args;
+
+/* Bytes of device workspace screen_fwd needs (bf16 D=64 tensor-core path: the
+ * unit-V operand, 1/|k| per key and per-tile bounds; 0 otherwise). */
+SCREEN_API size_t screen_fwd_workspace_size(const screen_fwd_args* a);
 
 /* Fused screening forward (unit-normalisation, S, trim-and-square, softmask,
  * key padding, alpha v^, TanhNorm).
@@ -223,6 +229,10 @@ SCREEN_API int screen_version(void);                  /* SCREEN_ABI_VERSION     
 SCREEN_API int64_t screen_sizeof_args(int which);
 /* Last CUDA error string seen by this thread inside the library. */
 SCREEN_API const char* screen_last_cuda_error(void);
+/* SCREEN_OK, or SCREEN_ERR_TIMEOUT if a kernel since the last clear gave up
+ * a bounded device-side wait (the kernel then drained and returned).  Reads a
+ * device status word (synchronising copy); `clear` resets it. */
+SCREEN_API int screen_device_status(int clear);
 
 #ifdef __cplusplus
 }

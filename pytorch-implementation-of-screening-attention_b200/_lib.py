@@ -29,6 +29,7 @@ class FwdArgs(ctypes.Structure):
         ("r", c_void_p), ("w", c_void_p), ("key_padding_mask", c_void_p), ("kpm_sb", c_int64),
         ("nq", c_void_p), ("nk", c_void_p), ("nv", c_void_p),
         ("y", c_void_p), ("no", c_void_p), ("tile_stats", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -85,9 +86,10 @@ EXPORTED = (
     "screen_fwd", "screen_bwd", "screen_bwd_workspace_size", "screen_kv_append",
     "screen_decode", "screen_decode_workspace_size", "screen_tanhnorm_fwd",
     "screen_tanhnorm_bwd", "screen_strerror", "screen_version", "screen_sizeof_args",
-    "screen_last_cuda_error", "screen_decode_noalloc",
+    "screen_last_cuda_error", "screen_decode_noalloc", "screen_fwd_workspace_size",
+    "screen_device_status",
 )
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _lib = None
 
@@ -104,6 +106,9 @@ def load() -> ctypes.CDLL:
     P = ctypes.POINTER
     lib.screen_fwd.argtypes = [P(FwdArgs), c_void_p]
     lib.screen_bwd.argtypes = [P(BwdArgs), c_void_p]
+    lib.screen_fwd_workspace_size.argtypes = [P(FwdArgs)]
+    lib.screen_fwd_workspace_size.restype = c_size_t
+    lib.screen_device_status.argtypes = [ctypes.c_int]
     lib.screen_bwd_workspace_size.argtypes = [P(BwdArgs)]
     lib.screen_bwd_workspace_size.restype = c_size_t
     lib.screen_kv_append.argtypes = [P(KVAppendArgs), c_void_p]
@@ -213,8 +218,19 @@ def screen_fwd(q, k, v, r, w, causal=True, key_padding_mask=None, eps=1e-8, q_of
                 kpm_sb=0 if kpm is None else kpm.stride(0),
                 nq=_ptr(nq), nk=_ptr(nk), nv=_ptr(nv), y=_ptr(y), no=_ptr(no),
                 tile_stats=_ptr(tile_stats))
+    nbytes = int(lib.screen_fwd_workspace_size(ctypes.byref(a)))
+    ws = None
+    if nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        a.workspace = ws.data_ptr()
+        a.workspace_bytes = nbytes
     _check(lib.screen_fwd(ctypes.byref(a), _stream(dev)))
     return y, no, nq, nk, nv, q, k, v
+
+
+def device_status(clear: bool = True) -> int:
+    """0, or the status code a kernel left after giving up a bounded wait."""
+    return int(load().screen_device_status(int(clear)))
 
 
 def row_norms(x, eps=1e-8):

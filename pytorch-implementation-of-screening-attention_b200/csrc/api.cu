@@ -34,15 +34,22 @@ bool raw_ok(int dtype, const void* p, long long sb, long long st) {
 }
 size_t round_up(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// SCREEN_FORCE_SIMT=1 routes bf16 D=64 to the SIMT kernels (a debugging aid
-// for comparing the two implementations on identical inputs).
-bool use_mma(int dtype, int D) {
-  static const bool force_simt = [] {
-    const char* e = getenv("SCREEN_FORCE_SIMT");
-    return e && e[0] == '1';
+// Kernel family for bf16 D=64: the tcgen05 forward by default.  The
+// environment variable SCREEN_KERNELS=mma|simt selects the warp-level mma.sync
+// or the SIMT kernels instead -- a debugging aid for comparing implementations
+// on identical inputs.
+enum Family { FAM_TC, FAM_MMA, FAM_SIMT };
+Family family_choice() {
+  static const Family f = [] {
+    const char* e = getenv("SCREEN_KERNELS");
+    if (e && e[0] == 's') return FAM_SIMT;
+    if (e && e[0] == 'm') return FAM_MMA;
+    return FAM_TC;
   }();
-  return !force_simt && mma_supported(dtype, D);
+  return f;
 }
+bool use_tc_fwd(int dtype, int D) { return family_choice() == FAM_TC && tc_supported(dtype, D); }
+bool use_mma(int dtype, int D) { return family_choice() != FAM_SIMT && mma_supported(dtype, D); }
 
 int common_checks(int dtype, int B, int H, int Tq, int Tk, int D) {
   if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;
@@ -126,7 +133,9 @@ int screen_fwd(const screen_fwd_args* a, screen_stream_t stream) {
   if (!raw_ok(a->dtype, a->q, a->q_sb, a->q_st) || !raw_ok(a->dtype, a->k, a->k_sb, a->k_st) ||
       !raw_ok(a->dtype, a->v, a->v_sb, a->v_st) || !al16(a->y))
     return SCREEN_ERR_ALIGNMENT;
-  if (!a->norms_given && (stages & 1)) {
+  // the tensor-core forward computes the norms in its own prep pass
+  const bool tc = use_tc_fwd(a->dtype, a->D) && nq && (stages & 2);
+  if (!tc && !a->norms_given && (stages & 1)) {
     NormJob jobs[3];
     int n = 0;
     if (nq) jobs[n++] = NormJob{Rows{a->q, a->q_sb, a->q_st}, a->B, a->Tq, a->H, a->nq};
@@ -142,12 +151,27 @@ int screen_fwd(const screen_fwd_args* a, screen_stream_t stream) {
                             a->key_padding_mask, a->kpm_sb);
   FwdPtrs p{Rows{a->q, a->q_sb, a->q_st}, Rows{a->k, a->k_sb, a->k_st},
             Rows{a->v, a->v_sb, a->v_st}, a->nq, a->nk, a->nv, a->y, a->no, a->tile_stats};
-  if (use_mma(a->dtype, a->D))
+  if (tc) {
+    const size_t need = tc_fwd_workspace(sh);
+    if (need > 0 && (!a->workspace || a->workspace_bytes < need || !al16(a->workspace)))
+      return SCREEN_ERR_WORKSPACE;
+    tc_fwd(sh, p, a->workspace, a->norms_given || !(stages & 1), s);
+  } else if (use_mma(a->dtype, a->D))
     mma_fwd(a->D, sh, p, s);
   else
     simt_fwd(a->dtype, a->D, sh, p, s);
   return check_launch();
 }
+
+size_t screen_fwd_workspace_size(const screen_fwd_args* a) {
+  if (!a || common_checks(a->dtype, a->B, a->H, a->Tq, a->Tk, a->D)) return 0;
+  if (!use_tc_fwd(a->dtype, a->D)) return 0;
+  AttnShape sh = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
+                            a->key_padding_mask, a->kpm_sb);
+  return round_up(tc_fwd_workspace(sh));
+}
+
+int screen_device_status(int clear) { return tc_device_status(clear != 0); }
 
 size_t screen_bwd_workspace_size(const screen_bwd_args* a) {
   if (!a || common_checks(a->dtype, a->B, a->H, a->Tq, a->Tk, a->D)) return 0;

@@ -1,0 +1,543 @@
+// Screening attention forward on the 5th-generation tensor cores (tcgen05,
+// TMEM accumulators), bf16, head dim 64.
+//
+// Math: multiscreen/attention.py:156-196 -- S = q^ k^T, a = relu(1-r(1-S)),
+// alpha = a^2 m(rel), o = alpha v^, y = TanhNorm(o) (norm.py:23-25).
+//
+// A prep pass reads q, k, v once: clamped norms (kept for the backward), the
+// unit rows V^ (bf16, padded keys zeroed) and 1/|k| transposed per (b, h)
+// plus its per-64-key-tile (min, max).  K itself enters the tensor cores raw
+// (exact bf16) with 1/|k| applied in fp32 per column, because r amplifies any
+// error of S near the trim threshold; rounding V^ is harmless (alpha is
+// rounded to bf16 anyway).
+//
+// CTA = 128 queries of one (b, h), six warps:
+//   warps 0-3  "compute": thread t owns query row t = TMEM lane t.  Reads the
+//              S tile from TMEM, applies 1/|k|, the trim, the softmask (rank-2
+//              cos identity against per-row and per-column (cos, sin) pairs)
+//              with packed f32x2 math, and writes P = alpha (bf16) back to
+//              TMEM as the A operand of the PV MMA; TanhNorm epilogue.
+//   warp 4     producer: cp.async Q once, then per 64-key tile K, V^, 1/|k|
+//              and the tile's (min, max) through a 3-stage ring; the column
+//              (cos, sin) come from one sincospif per tile and a rotation.
+//   warp 5     MMA issuer (one thread): S_j = Q K_j^T (M=128, N=64, K=64) into
+//              a double-buffered TMEM S, then O += P_{j-1} V^_{j-1} (A from
+//              TMEM, V^ MN-major from shared memory) into the TMEM O.
+// TMEM: S0 [0,64) S1 [64,128) P0 [128,160) P1 [160,192) O [192,256) -> 256
+// columns, so two CTAs share an SM.  Key tiles outside the window are never
+// loaded; a tile whose scores provably all fall under the trim threshold
+// skips the alpha/PV work.  Every wait is bounded by a global-timer limit; on
+// expiry the CTA drains, frees its TMEM and records SCREEN_ERR_TIMEOUT in a
+// device status word (screen_device_status).
+#include "rowops.cuh"
+
+namespace screen {
+namespace {
+
+using namespace sm100;
+typedef __nv_bfloat16 bf16;
+
+constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 3, kThreads = 192;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+// shared-memory layout (offsets from a 1024-byte aligned base)
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_K = OFF_Q + kBM * kD * 2;
+constexpr uint32_t OFF_V = OFF_K + kNS * kBN * kD * 2;
+constexpr uint32_t OFF_COL = OFF_V + kNS * kBN * kD * 2;  // per stage ik|cos|sin [64] + meta
+constexpr uint32_t COL_BYTES = 3 * kBN * 4 + 16;           // meta = (ik min, ik max, -, -)
+constexpr uint32_t OFF_TAB = OFF_COL + kNS * COL_BYTES;    // (cos, sin)(pi c / w), c < 64
+constexpr uint32_t OFF_BAR = OFF_TAB + 2 * kBN * 4;
+constexpr int BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = BAR_KV_FULL + kNS,
+              BAR_S_FULL = BAR_KV_EMPTY + kNS, BAR_S_FREE = BAR_S_FULL + 2,
+              BAR_P_FULL = BAR_S_FREE + 2, BAR_O_FULL = BAR_P_FULL + 2;
+constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 16;
+constexpr uint32_t SMEM_USED = OFF_MISC + 64;
+// at least 80 KB per CTA: at most two CTAs (2 x 256 TMEM columns) per SM
+constexpr uint32_t kSmemBytes = (SMEM_USED + 1024 > 80 * 1024) ? SMEM_USED + 1024 : 80 * 1024;
+
+constexpr uint32_t TM_S = 0, TM_P = 128, TM_O = 192, TM_COLS = 256;
+
+__device__ int g_device_status = 0;
+
+__global__ void __launch_bounds__(kThreads, 2)
+    tc_fwd_kernel(AttnShape s, FwdPtrs p, const bf16* __restrict__ vhat,
+                  const float* __restrict__ ikT, const float4* __restrict__ ikmeta, int Tkp) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw_addr);
+  const uint32_t sQ = base + OFF_Q, sK = base + OFF_K, sV = base + OFF_V;
+  float* colp = reinterpret_cast<float*>(gbase + OFF_COL);
+  float* tab = reinterpret_cast<float*>(gbase + OFF_TAB);
+  const uint32_t bars = base + OFF_BAR;
+  uint32_t* misc = reinterpret_cast<uint32_t*>(gbase + OFF_MISC);
+  // misc[0] tmem base, misc[1..2] skip flags, misc[3] O valid, misc[4] abort
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
+  auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y, b = bh / s.H, h = bh % s.H;
+  const long long i0 = (long long)blockIdx.x * kBM;
+  const bool causal = s.causal != 0;
+  const float r = s.r[h], w = s.w[h];
+  const int dmax = window_dmax(w);
+  const long long p0 = i0 + s.q_offset;
+  long long ilast = i0 + kBM - 1;
+  if (ilast > s.Tq - 1) ilast = s.Tq - 1;
+  long long lo, hi;
+  key_range(p0, ilast + s.q_offset, dmax, causal, s.Tk, lo, hi);
+  const bool any = dmax >= 0 && lo <= hi;
+  const int kt0 = any ? (int)(lo / kBN) : 0;
+  const int n = any ? (int)(hi / kBN) - kt0 + 1 : 0;
+
+  if (tid == 0) {
+    mbar_init(bar(BAR_Q), 32);
+    for (int i = 0; i < kNS; ++i) {
+      mbar_init(bar(BAR_KV_FULL + i), 33);
+      mbar_init(bar(BAR_KV_EMPTY + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(BAR_S_FULL + i), 1);
+      mbar_init(bar(BAR_S_FREE + i), 128);
+      mbar_init(bar(BAR_P_FULL + i), 128);
+    }
+    mbar_init(bar(BAR_O_FULL), 2);
+    misc[1] = misc[2] = misc[3] = 0;
+    misc[4] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc(base + OFF_MISC, TM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    const bf16* qh = reinterpret_cast<const bf16*>(p.q.p) + (long long)b * p.q.sb + (long long)h * kD;
+    const bf16* kh = reinterpret_cast<const bf16*>(p.k.p) + (long long)b * p.k.sb + (long long)h * kD;
+    const bf16* vh = vhat + ((long long)b * s.Tk * s.H + h) * kD;
+    const long long vst = (long long)s.H * kD;
+    for (int c = lane; c < kBM * 8; c += 32) {
+      const int row = c >> 3, ch = c & 7;
+      const long long t = i0 + row;
+      const bool ok = t < s.Tq;
+      cp_async16(sQ + tile_off<kD>(row, ch), qh + (ok ? t * p.q.st : 0) + ch * 8, ok);
+    }
+    mbar_arrive_cp_async(bar(BAR_Q));
+    // (cos, sin)(pi c / w) for the 64 column offsets of a tile
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int c = lane + 32 * hh;
+      float sn, cs;
+      sincospif((float)c / w, &sn, &cs);
+      tab[c] = cs;
+      tab[kBN + c] = sn;
+    }
+    __syncwarp();
+    const float cphi0 = tab[lane], sphi0 = tab[kBN + lane];
+    const float cphi1 = tab[lane + 32], sphi1 = tab[kBN + lane + 32];
+    const float* ikh = ikT + (long long)bh * Tkp;          // 1/|k| of (b, h), padded to 64
+    const float4* mh = ikmeta + (long long)bh * (Tkp / kBN);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % kNS;
+      if (j >= kNS) {
+        // lane 0 waits, the whole warp follows its verdict (no divergent exit)
+        int okw = 1;
+        if (lane == 0)
+          okw = mbar_wait(bar(BAR_KV_EMPTY + st), ((j / kNS) - 1) & 1, abort_flag, kWaitLimitNs);
+        if (!__shfl_sync(0xffffffffu, okw, 0)) break;
+      }
+      const int kt = kt0 + j;
+      const long long j0 = (long long)kt * kBN;
+      const uint32_t kb = sK + st * kBN * kD * 2, vb = sV + st * kBN * kD * 2;
+      for (int c = lane; c < kBN * 8; c += 32) {
+        const int row = c >> 3, ch = c & 7;
+        const long long t = j0 + row;
+        const bool ok = t < s.Tk;
+        cp_async16(kb + tile_off<kD>(row, ch), kh + (ok ? t * p.k.st : 0) + ch * 8, ok);
+        cp_async16(vb + tile_off<kD>(row, ch), vh + (ok ? t * vst : 0) + ch * 8, ok);
+      }
+      const uint32_t colb = base + OFF_COL + st * COL_BYTES;
+      float* col = colp + st * (COL_BYTES / 4);
+      if (lane < 16) cp_async16(colb + lane * 16, ikh + j0 + lane * 4, true);
+      else if (lane == 16) cp_async16(colb + 3 * kBN * 4, mh + kt, true);
+      // column angle pi (j0 + c - p0) / w = base + pi c / w, by rotation
+      float sb = 0.f, cb = 0.f;
+      if (lane == 0) sincospif((float)(j0 - p0) / w, &sb, &cb);
+      sb = __shfl_sync(0xffffffffu, sb, 0);
+      cb = __shfl_sync(0xffffffffu, cb, 0);
+      col[kBN + lane] = cb * cphi0 - sb * sphi0;
+      col[2 * kBN + lane] = sb * cphi0 + cb * sphi0;
+      col[kBN + lane + 32] = cb * cphi1 - sb * sphi1;
+      col[2 * kBN + lane + 32] = sb * cphi1 + cb * sphi1;
+      mbar_arrive_cp_async(bar(BAR_KV_FULL + st));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_KV_FULL + st));
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(kBM, kBN, 0, 0);
+      constexpr uint32_t idPV = idesc_bf16(kBM, kD, 0, 1);
+      bool o_started = false, ok = mbar_wait(bar(BAR_Q), 0, abort_flag, kWaitLimitNs);
+      auto issue_pv = [&](int jj) -> bool {
+        const int bb = jj & 1, st = jj % kNS;
+        if (!mbar_wait(bar(BAR_P_FULL + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
+        tc_fence_after();
+        if (!misc[1 + bb]) {
+          const uint32_t vb = sV + st * kBN * kD * 2;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            mma_ts(tmem + TM_O, tmem + TM_P + 32 * bb + 8 * kk,
+                   desc_sw128(vb + kk * 16 * 128, kBN * kD * 2, 1024), idPV,
+                   (o_started || kk > 0) ? 1u : 0u);
+          o_started = true;
+        }
+        mma_commit(bar(BAR_KV_EMPTY + st));
+        return true;
+      };
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j % kNS, bb = j & 1;
+        ok = mbar_wait(bar(BAR_KV_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
+        if (ok && j >= 2)
+          ok = mbar_wait(bar(BAR_S_FREE + bb), ((j >> 1) - 1) & 1, abort_flag, kWaitLimitNs);
+        if (!ok) break;
+        tc_fence_after();
+        fence_proxy_async_smem();
+        const uint32_t kb = sK + st * kBN * kD * 2;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem + TM_S + kBN * bb, desc_sw128(sQ + kk * 32, 16, 1024),
+                 desc_sw128(kb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        mma_commit(bar(BAR_S_FULL + bb));
+        if (j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok && n >= 1) ok = issue_pv(n - 1);
+      misc[3] = o_started ? 1u : 0u;
+      mma_commit(bar(BAR_O_FULL));
+      mbar_arrive(bar(BAR_O_FULL));
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ compute
+    const int t = tid;  // 0..127 = query row in tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const long long i = i0 + t;
+    const float rq = (i < s.Tq) ? r / p.nq[((long long)b * s.Tq + i) * s.H + h] : 0.f;
+    float crow, srow;
+    {
+      float sn, cs;
+      sincospif((float)t / w, &sn, &cs);
+      crow = 0.5f * cs;
+      srow = 0.5f * sn;
+    }
+    const float omr = 1.0f - r;
+    const long long pos = i + s.q_offset;
+    const float2 rq2 = make_float2(rq, rq), omr2 = make_float2(omr, omr);
+    const float2 cr2 = make_float2(crow, crow), sr2 = make_float2(srow, srow);
+    const float2 half2 = make_float2(0.5f, 0.5f);
+    // alpha of columns (c, c+1) from the pair's S, 1/|k|, cos, sin
+    auto pair_alpha = [&](float s0, float s1, float ik0, float ik1, float c0, float c1, float n0,
+                          float n1, bool k0, bool k1) -> uint32_t {
+      const float2 x = __fmul2_rn(make_float2(s0, s1), make_float2(ik0, ik1));
+      const float2 t2 = __ffma2_rn(rq2, x, omr2);
+      const float2 a2 = make_float2(k0 ? fmaxf(t2.x, 0.f) : 0.f, k1 ? fmaxf(t2.y, 0.f) : 0.f);
+      const float2 m2 =
+          __ffma2_rn(cr2, make_float2(c0, c1), __ffma2_rn(sr2, make_float2(n0, n1), half2));
+      const float2 al = __fmul2_rn(__fmul2_rn(a2, m2), a2);
+      return pack_bf16(al.x, al.y);
+    };
+    bool ok = true;
+    unsigned long long live_tiles = 0;
+    for (int j = 0; j < n; ++j) {
+      const int st = j % kNS, bb = j & 1;
+      ok = mbar_wait(bar(BAR_KV_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
+           mbar_wait(bar(BAR_S_FULL + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
+      // all 128 threads take the same branch before the next named barrier
+      if (bar_red_or(1, 128, !ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[64];
+      {
+        uint32_t (&a0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
+        uint32_t (&a1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
+        tmem_ld32(tmem + TM_S + kBN * bb + lane_off, a0);
+        tmem_ld32(tmem + TM_S + kBN * bb + 32 + lane_off, a1);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(bar(BAR_S_FREE + bb));
+
+      const float* col = colp + st * (COL_BYTES / 4);
+      // trim pre-test.  For r >= 1 the threshold (r-1)/r on S is >= 0, so
+      // only positive scores can be live; positive floats order like their
+      // int bit patterns and negative ones are negative ints, so an integer
+      // max over the raw bits finds the largest score when it is positive.
+      int imax = (int)sv[0];
+#pragma unroll
+      for (int c = 1; c + 1 < 64; c += 2) imax = __vimax3_s32(imax, (int)sv[c], (int)sv[c + 1]);
+      imax = max(imax, (int)sv[63]);
+      const float smax = __int_as_float(imax);
+      const float ikmax = col[3 * kBN + 1];
+      const bool mine = r < 1.0f || (imax > 0 && fmaf(rq, smax * ikmax, omr) > 0.f);
+      const bool live = bar_red_or(1, 128, mine);
+      if (live) {
+        const long long j0 = (long long)(kt0 + j) * kBN;
+        const bool inside = (causal ? (p0 - (j0 + kBN - 1) >= 0 && p0 + kBM - 1 - j0 <= dmax)
+                                    : (p0 - (j0 + kBN - 1) >= -(long long)dmax &&
+                                       p0 + kBM - 1 - j0 <= dmax));
+        uint32_t pk[32];
+        const float4* ik4 = reinterpret_cast<const float4*>(col);
+        const float4* cc4 = reinterpret_cast<const float4*>(col + kBN);
+        const float4* sc4 = reinterpret_cast<const float4*>(col + 2 * kBN);
+        if (inside) {
+#pragma unroll
+          for (int q4 = 0; q4 < 16; ++q4) {
+            const float4 ikv = ik4[q4], ccv = cc4[q4], scv = sc4[q4];
+            const int c = 4 * q4;
+            pk[2 * q4] = pair_alpha(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), ikv.x,
+                                    ikv.y, ccv.x, ccv.y, scv.x, scv.y, true, true);
+            pk[2 * q4 + 1] = pair_alpha(__uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]),
+                                        ikv.z, ikv.w, ccv.z, ccv.w, scv.z, scv.w, true, true);
+          }
+        } else {
+          // window edge: this row's valid columns are the interval [clo, chi]
+          const long long clo = pos - dmax - j0, chi = causal ? pos - j0 : pos + dmax - j0;
+          const int iclo = (int)(clo < 0 ? 0 : (clo > 64 ? 64 : clo));
+          const int ichi = (int)(chi < -1 ? -1 : (chi > 63 ? 63 : chi));
+#pragma unroll
+          for (int q4 = 0; q4 < 16; ++q4) {
+            const float4 ikv = ik4[q4], ccv = cc4[q4], scv = sc4[q4];
+            const int c = 4 * q4;
+            pk[2 * q4] = pair_alpha(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), ikv.x,
+                                    ikv.y, ccv.x, ccv.y, scv.x, scv.y,
+                                    c >= iclo && c <= ichi, c + 1 >= iclo && c + 1 <= ichi);
+            pk[2 * q4 + 1] = pair_alpha(__uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]),
+                                        ikv.z, ikv.w, ccv.z, ccv.w, scv.z, scv.w,
+                                        c + 2 >= iclo && c + 2 <= ichi,
+                                        c + 3 >= iclo && c + 3 <= ichi);
+          }
+        }
+        tmem_st32(tmem + TM_P + 32 * bb + lane_off, pk);
+        tmem_wait_st();
+      }
+      if (t == 0) {
+        misc[1 + bb] = live ? 0u : 1u;
+        live_tiles += live ? 1 : 0;
+      }
+      tc_fence_before();
+      mbar_arrive(bar(BAR_P_FULL + bb));
+    }
+    if (p.tile_stats && t == 0) {
+      // reported in 16x64 score blocks, the unit of the warp-level kernels
+      atomicAdd((unsigned long long*)&p.tile_stats[0], 8ull * (unsigned long long)n);
+      atomicAdd((unsigned long long*)&p.tile_stats[1], 8ull * live_tiles);
+    }
+    // epilogue: O -> TanhNorm -> y
+    ok = ok && mbar_wait(bar(BAR_O_FULL), 0, abort_flag, kWaitLimitNs);
+    tc_fence_after();
+    if (ok) {
+      float o[64];
+      if (misc[3]) {
+        uint32_t ov[64];
+        uint32_t (&a0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&ov[0]);
+        uint32_t (&a1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&ov[32]);
+        tmem_ld32(tmem + TM_O + lane_off, a0);
+        tmem_ld32(tmem + TM_O + 32 + lane_off, a1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 64; ++c) o[c] = __uint_as_float(ov[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) o[c] = 0.f;
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) ss = fmaf(o[c], o[c], ss);
+      const float nraw = sqrtf(ss);
+      const float g = tanhnorm_scale(nraw, s.eps);
+      if (i < s.Tq) {
+        const long long row = ((long long)b * s.Tq + i) * s.H + h;
+        uint4* yr = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(p.y) + row * kD);
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint4 v;
+          v.x = pack_bf16(o[8 * c8 + 0] * g, o[8 * c8 + 1] * g);
+          v.y = pack_bf16(o[8 * c8 + 2] * g, o[8 * c8 + 3] * g);
+          v.z = pack_bf16(o[8 * c8 + 4] * g, o[8 * c8 + 5] * g);
+          v.w = pack_bf16(o[8 * c8 + 6] * g, o[8 * c8 + 7] * g);
+          yr[c8] = v;
+        }
+        p.no[row] = nraw;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, TM_COLS);
+  if (tid == 0 && *abort_flag) atomicExch(&g_device_status, (int)SCREEN_ERR_TIMEOUT);
+}
+
+// One pass over q, k, v (bf16, D = 64; 8 lanes x 16 B per row): the clamped
+// row norms (written unless the caller gave them), the unit rows
+// V^ = v / |v| (zero for padded keys) that the forward multiplies by alpha,
+// and 1/|k| transposed to [B][H][Tk padded to 64] so a key tile's factors are
+// one contiguous 256-byte run.
+__global__ void tc_prep_kernel(Rows q, Rows k, Rows v, int B, int Tq, int Tk, int H, float eps,
+                               int norms_given, const uint8_t* kpm, long long kpm_sb,
+                               float* __restrict__ nq, float* __restrict__ nk,
+                               float* __restrict__ nv, bf16* __restrict__ vhat,
+                               float* __restrict__ ikT, int Tkp) {
+  const int sub = threadIdx.x & 7;
+  const long long rows_q = norms_given ? 0 : (long long)B * Tq * H;
+  const long long rows_k = (long long)B * Tk * H;
+  const long long total = rows_q + rows_k;
+  // every lane of a warp runs the same number of iterations (32 rows per
+  // block step), so the 8-lane shuffles below always see full groups
+  for (long long base_row = (long long)blockIdx.x * 32; base_row < total;
+       base_row += (long long)gridDim.x * 32) {
+    const long long row = base_row + (threadIdx.x >> 3);
+    const bool valid = row < total;
+    const bool isq = row < rows_q;
+    const long long rr = !valid ? 0 : (isq ? row : row - rows_q);
+    const int T = isq ? Tq : Tk;
+    const long long hh = rr % H, t = (rr / H) % T, bb = rr / ((long long)H * T);
+    // a = the q row (q part) or the k row; c = the v row (k part) or zeros
+    uint4 ua = make_uint4(0, 0, 0, 0), uc = make_uint4(0, 0, 0, 0);
+    if (valid && isq) {
+      ua = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(q.p) + bb * q.sb +
+                                           t * q.st + hh * kD + sub * 8);
+    } else if (valid) {
+      ua = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(k.p) + bb * k.sb +
+                                           t * k.st + hh * kD + sub * 8);
+      uc = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(v.p) + bb * v.sb +
+                                           t * v.st + hh * kD + sub * 8);
+    }
+    float sa = 0.f, sc = 0.f;
+    const uint32_t a4[4] = {ua.x, ua.y, ua.z, ua.w};
+    const uint32_t c4[4] = {uc.x, uc.y, uc.z, uc.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 fa = unpack_bf16(a4[e]), fc = unpack_bf16(c4[e]);
+      sa = fmaf(fa.x, fa.x, fmaf(fa.y, fa.y, sa));
+      sc = fmaf(fc.x, fc.x, fmaf(fc.y, fc.y, sc));
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      sa += __shfl_xor_sync(0xffffffffu, sa, o);
+      sc += __shfl_xor_sync(0xffffffffu, sc, o);
+    }
+    if (!valid) continue;
+    if (isq) {
+      if (sub == 0) nq[rr] = fmaxf(sqrtf(sa), eps);
+      continue;
+    }
+    const float nkr = norms_given ? nk[rr] : fmaxf(sqrtf(sa), eps);
+    const float nvr = norms_given ? nv[rr] : fmaxf(sqrtf(sc), eps);
+    const bool masked = kpm && kpm[bb * kpm_sb + t];
+    const float inv = masked ? 0.f : 1.0f / nvr;
+    uint4 o;
+    float2 f;
+    f = unpack_bf16(uc.x); o.x = pack_bf16(f.x * inv, f.y * inv);
+    f = unpack_bf16(uc.y); o.y = pack_bf16(f.x * inv, f.y * inv);
+    f = unpack_bf16(uc.z); o.z = pack_bf16(f.x * inv, f.y * inv);
+    f = unpack_bf16(uc.w); o.w = pack_bf16(f.x * inv, f.y * inv);
+    *reinterpret_cast<uint4*>(vhat + rr * kD + sub * 8) = o;
+    if (sub == 0) {
+      if (!norms_given) {
+        nk[rr] = nkr;
+        nv[rr] = nvr;
+      }
+      ikT[(bb * H + hh) * Tkp + t] = 1.0f / nkr;
+    }
+  }
+}
+
+// zero 1/|k| for the padding keys Tk..Tkp-1, then per 64-key tile the
+// (min, max) of 1/|k| for the forward's trim pre-test
+__global__ void tc_ik_meta_kernel(float* __restrict__ ikT, float4* __restrict__ meta, int BH,
+                                  int Tk, int Tkp) {
+  const int ntiles = Tkp / kBN;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)BH * ntiles) return;
+  const long long bhh = idx / ntiles;
+  const int tile = (int)(idx % ntiles);
+  float* x = ikT + bhh * Tkp + (long long)tile * kBN;
+  float mn = 3.0e38f, mx = 0.f;
+  for (int c = 0; c < kBN; ++c) {
+    const long long t = (long long)tile * kBN + c;
+    float vv = 0.f;
+    if (t < Tk) vv = x[c]; else x[c] = 0.f;
+    mn = fminf(mn, vv);
+    mx = fmaxf(mx, vv);
+  }
+  meta[idx] = make_float4(mn, mx, 0.f, 0.f);
+}
+
+bool g_tc_attr[64];
+
+long long tk_pad(int Tk) { return ((long long)Tk + kBN - 1) / kBN * kBN; }
+size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+bool tc_supported(int dtype, int D) { return dtype == SCREEN_BF16 && D == kD; }
+
+size_t tc_fwd_workspace(const AttnShape& s) {
+  const long long BH = (long long)s.B * s.H, Tkp = tk_pad(s.Tk);
+  return al256((size_t)s.B * s.Tk * s.H * kD * 2) + al256((size_t)BH * Tkp * 4) +
+         al256((size_t)BH * (Tkp / kBN) * 16);
+}
+
+void tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
+            cudaStream_t st) {
+  if (s.B == 0 || s.H == 0) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !g_tc_attr[dev]) {
+    cudaFuncSetAttribute(tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kSmemBytes);
+    g_tc_attr[dev] = true;
+  }
+  const long long BH = (long long)s.B * s.H, Tkp = tk_pad(s.Tk);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  bf16* vhat = reinterpret_cast<bf16*>(ws);
+  float* ikT = reinterpret_cast<float*>(ws + al256((size_t)s.B * s.Tk * s.H * kD * 2));
+  float4* meta = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(ikT) +
+                                           al256((size_t)BH * Tkp * 4));
+  const long long rows = (long long)s.B * ((norms_given ? 0 : s.Tq) + s.Tk) * s.H;
+  if (rows > 0) {
+    long long blocks = (rows + 31) / 32;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    tc_prep_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+        p.q, p.k, p.v, s.B, s.Tq, s.Tk, s.H, s.eps, norms_given ? 1 : 0, s.kpm, s.kpm_sb,
+        const_cast<float*>(p.nq), const_cast<float*>(p.nk), const_cast<float*>(p.nv), vhat, ikT,
+        (int)Tkp);
+  }
+  const long long mt = BH * (Tkp / kBN);
+  if (mt > 0)
+    tc_ik_meta_kernel<<<(unsigned)((mt + 255) / 256), 256, 0, st>>>(ikT, meta, (int)BH, s.Tk,
+                                                                   (int)Tkp);
+  if (s.Tq == 0) return;
+  dim3 grid((s.Tq + kBM - 1) / kBM, s.B * s.H);
+  tc_fwd_kernel<<<grid, kThreads, kSmemBytes, st>>>(s, p, vhat, ikT, meta, (int)Tkp);
+}
+
+int tc_device_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return SCREEN_ERR_CUDA;
+  if (clear && v != 0) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_device_status, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace screen

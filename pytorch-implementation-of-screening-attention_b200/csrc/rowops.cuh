@@ -64,7 +64,14 @@ long long simt_bwd_partials(const AttnShape& s);
 void simt_bwd(int dtype, int D, const AttnShape& s, const BwdPtrs& p, int stages,
               cudaStream_t st);
 
-// bf16 tensor-core kernels (D = 64).
+// tcgen05 / TMEM forward (bf16, D = 64).
+bool tc_supported(int dtype, int D);
+size_t tc_fwd_workspace(const AttnShape& s);
+void tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
+            cudaStream_t st);
+int tc_device_status(bool clear);
+
+// bf16 warp-level mma.sync kernels (D = 64).
 bool mma_supported(int dtype, int D);
 void mma_fwd(int D, const AttnShape& s, const FwdPtrs& p, cudaStream_t st);
 long long mma_bwd_partials(int D, const AttnShape& s);
