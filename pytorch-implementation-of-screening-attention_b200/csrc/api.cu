@@ -67,19 +67,22 @@ AttnShape make_shape(int B, int H, int Tq, int Tk, int causal, long long q_offse
 }
 
 struct BwdLayout {
-  size_t g_off, pr_off, pw_off, total;
+  size_t g_off, pr_off, pw_off, aux_off, total;
   long long P;
 };
 BwdLayout bwd_layout(const screen_bwd_args* a) {
   BwdLayout L;
   AttnShape s = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
                            a->key_padding_mask, a->kpm_sb);
-  L.P = use_mma(a->dtype, a->D) ? mma_bwd_partials(a->D, s) : simt_bwd_partials(s);
+  const bool tc = use_tc_fwd(a->dtype, a->D);
+  L.P = tc ? tc_bwd_partials(s)
+           : (use_mma(a->dtype, a->D) ? mma_bwd_partials(a->D, s) : simt_bwd_partials(s));
   L.g_off = 0;
   // G: fp32, or two bf16 planes (hi, lo) on the tensor-core path -- 4 bytes/elem either way
   L.pr_off = round_up((size_t)a->B * a->Tq * a->H * a->D * 4);
   L.pw_off = L.pr_off + round_up((size_t)a->H * L.P * sizeof(float));
-  L.total = L.pw_off + round_up((size_t)a->H * L.P * sizeof(float));
+  L.aux_off = L.pw_off + round_up((size_t)a->H * L.P * sizeof(float));
+  L.total = L.aux_off + (tc ? round_up(tc_bwd_aux_bytes(s)) : 0);
   return L;
 }
 
@@ -171,7 +174,10 @@ size_t screen_fwd_workspace_size(const screen_fwd_args* a) {
   return round_up(tc_fwd_workspace(sh));
 }
 
-int screen_device_status(int clear) { return tc_device_status(clear != 0); }
+int screen_device_status(int clear) {
+  const int a = tc_device_status(clear != 0), b = tc_bwd_device_status(clear != 0);
+  return a != 0 ? a : b;
+}
 
 size_t screen_bwd_workspace_size(const screen_bwd_args* a) {
   if (!a || common_checks(a->dtype, a->B, a->H, a->Tq, a->Tk, a->D)) return 0;
@@ -209,7 +215,9 @@ int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
             Rows{a->v, a->v_sb, a->v_st}, a->nq, a->nk, a->nv, G,
             OutRows{a->dq, a->dq_sb, a->dq_st}, OutRows{a->dk, a->dk_sb, a->dk_st},
             OutRows{a->dv, a->dv_sb, a->dv_st}, pr, pw};
-  if (use_mma(a->dtype, a->D))
+  if (use_tc_fwd(a->dtype, a->D))
+    tc_bwd(sh, p, ws + L.aux_off, stages, s);
+  else if (use_mma(a->dtype, a->D))
     mma_bwd(a->D, sh, p, stages, s);
   else
     simt_bwd(a->dtype, a->D, sh, p, stages, s);

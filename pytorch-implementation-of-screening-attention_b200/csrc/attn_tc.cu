@@ -340,6 +340,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // epilogue: O -> TanhNorm -> y
     ok = ok && mbar_wait(bar(BAR_O_FULL), 0, abort_flag, kWaitLimitNs);
+    // tcgen05.ld below is warp-collective: every lane takes the same branch
+    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     if (ok) {
       float o[64];

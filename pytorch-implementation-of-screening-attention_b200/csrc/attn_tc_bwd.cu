@@ -1,0 +1,864 @@
+// Screening attention backward on tcgen05 / TMEM (bf16, head dim 64).
+//
+// Autograd of multiscreen/attention.py:156-196 (the reference leaves it to
+// PyTorch; its Triton backward, kernels/screening_bwd.py, has no dr / dw):
+//   dP = G v^T (G = dL/do through TanhNorm, as bf16 hi + lo planes),
+//   dS = dP m 2a r [a > 0],  dv^ = alpha^T G,  dq^ = dS k^,  dk^ = dS^T q^,
+//   dr = sum dP m 2a (S - 1),  dw = pi/(2 w^2) sum dP a^2 rel sin(pi rel / w),
+// then the unit-normalisation Jacobians.  As in the forward the tensor cores
+// see raw bf16 q / k / v; 1/|q|, 1/|k|, 1/|v| are fp32 row / column scales.
+//
+// Two kernels, both warp specialised (10 warps: 8 compute = two warpgroups
+// splitting every 64-column tile in halves, 1 cp.async producer, 1 MMA
+// issuer), 512 TMEM columns, one CTA per SM:
+//   tc_bwd_dq_kernel  (query-major, 128 queries, key tiles of 64):
+//       S = Q K^T, dP = G_hi V^T + G_lo V^T, dQ += dS K
+//   tc_bwd_kv_kernel  (key-major, 128 keys, query tiles of 64):
+//       S^T = K Q^T, dP^T = V G_hi^T + V G_lo^T, dV += alpha G_hi, dK += dS Q,
+//       plus the per-CTA dr / dw partials (summed in a fixed order later).
+// Every wait is bounded (global timer); on expiry the CTA drains and records
+// SCREEN_ERR_TIMEOUT in the device status word.
+#include "rowops.cuh"
+
+namespace screen {
+namespace {
+
+using namespace sm100;
+typedef __nv_bfloat16 bf16;
+
+constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 3, kThreads = 320;
+constexpr int kCompute = 256;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint32_t TILE_A = kBM * kD * 2;  // 128-row operand tile, 16 KB
+constexpr uint32_t TILE_B = kBN * kD * 2;  // 64-row tile, 8 KB
+constexpr uint32_t TM_S = 0, TM_DP = 128, TM_P1 = 256, TM_P2 = 320, TM_ACC1 = 384,
+                   TM_ACC2 = 448, TM_COLS = 512;
+
+struct Aux {
+  const float* iqT;   // [B*H][Tqp] 1/|q| (0 past Tq)
+  const float* ikT;   // [B*H][Tkp] 1/|k| (0 past Tk)
+  const float* ivT;   // [B*H][Tkp] 1/|v| (0 past Tk and for padded keys)
+  const float4* mq;   // [B*H][Tqp/64] (max 1/|q| of the tile, -, -, -)
+  const float4* mk;   // [B*H][Tkp/64] (max 1/|k| of the tile, -, -, -)
+  int Tqp, Tkp;
+};
+
+__device__ int g_bwd_status = 0;
+__device__ __forceinline__ int* status_word() { return &g_bwd_status; }
+
+__device__ __forceinline__ void store_unit_jacobian(const float (&acc)[64], const bf16* xrow,
+                                                    float inv, bf16* out) {
+  // out = inv * (acc - inv^2 (x . acc) x), x the raw row (the Jacobian of
+  // x / |x| applied to acc = dL/dx^)
+  float xv[64];
+#pragma unroll
+  for (int c8 = 0; c8 < 8; ++c8) {
+    const uint4 u = reinterpret_cast<const uint4*>(xrow)[c8];
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16(w4[e]);
+      xv[8 * c8 + 2 * e] = f.x;
+      xv[8 * c8 + 2 * e + 1] = f.y;
+    }
+  }
+  float dot = 0.f;
+#pragma unroll
+  for (int c = 0; c < 64; ++c) dot = fmaf(xv[c], acc[c], dot);
+  const float cf = inv * inv * dot;
+#pragma unroll
+  for (int c8 = 0; c8 < 8; ++c8) {
+    uint4 v;
+    v.x = pack_bf16(inv * (acc[8 * c8 + 0] - cf * xv[8 * c8 + 0]),
+                    inv * (acc[8 * c8 + 1] - cf * xv[8 * c8 + 1]));
+    v.y = pack_bf16(inv * (acc[8 * c8 + 2] - cf * xv[8 * c8 + 2]),
+                    inv * (acc[8 * c8 + 3] - cf * xv[8 * c8 + 3]));
+    v.z = pack_bf16(inv * (acc[8 * c8 + 4] - cf * xv[8 * c8 + 4]),
+                    inv * (acc[8 * c8 + 5] - cf * xv[8 * c8 + 5]));
+    v.w = pack_bf16(inv * (acc[8 * c8 + 6] - cf * xv[8 * c8 + 6]),
+                    inv * (acc[8 * c8 + 7] - cf * xv[8 * c8 + 7]));
+    reinterpret_cast<uint4*>(out)[c8] = v;
+  }
+}
+
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&o)[64]) {
+  uint32_t u[64];
+  uint32_t (&a0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&u[0]);
+  uint32_t (&a1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&u[32]);
+  tmem_ld32(taddr, a0);
+  tmem_ld32(taddr + 32, a1);
+  tmem_wait_ld();
+#pragma unroll
+  for (int c = 0; c < 64; ++c) o[c] = __uint_as_float(u[c]);
+}
+
+// ===========================================================================
+// dq kernel
+// ===========================================================================
+namespace dq {
+constexpr uint32_t OFF_Q = 0, OFF_GH = TILE_A, OFF_GL = 2 * TILE_A;
+constexpr uint32_t OFF_K = 3 * TILE_A;
+constexpr uint32_t OFF_V = OFF_K + kNS * TILE_B;
+constexpr uint32_t OFF_COL = OFF_V + kNS * TILE_B;  // ik | iv | cos | sin [64] + meta
+constexpr uint32_t COLB = 4 * kBN * 4 + 16;
+constexpr uint32_t OFF_TAB = OFF_COL + kNS * COLB;
+constexpr uint32_t OFF_BAR = OFF_TAB + 2 * kBN * 4;
+constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNS, BAR_SD = BAR_EMPTY + kNS,
+              BAR_SDFREE = BAR_SD + 2, BAR_P = BAR_SDFREE + 2, BAR_DONE = BAR_P + 2;
+constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 16;
+// >= 120 KB: one CTA per SM (each allocates all 512 TMEM columns)
+constexpr uint32_t SMEM = (OFF_MISC + 64 + 1024 > 120 * 1024) ? OFF_MISC + 64 + 1024 : 120 * 1024;
+}  // namespace dq
+
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_bwd_dq_kernel(AttnShape s, BwdPtrs p, Aux ax) {
+  using namespace dq;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw_addr);
+  float* colp = reinterpret_cast<float*>(gbase + OFF_COL);
+  float* tab = reinterpret_cast<float*>(gbase + OFF_TAB);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(gbase + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
+  const uint32_t bars = base + OFF_BAR;
+  auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y, b = bh / s.H, h = bh % s.H;
+  const long long i0 = (long long)blockIdx.x * kBM;
+  const bool causal = s.causal != 0;
+  const float r = s.r[h], w = s.w[h];
+  const int dmax = window_dmax(w);
+  const long long p0 = i0 + s.q_offset;
+  long long ilast = i0 + kBM - 1;
+  if (ilast > s.Tq - 1) ilast = s.Tq - 1;
+  long long lo, hi;
+  key_range(p0, ilast + s.q_offset, dmax, causal, s.Tk, lo, hi);
+  const bool any = dmax >= 0 && lo <= hi;
+  const int kt0 = any ? (int)(lo / kBN) : 0;
+  const int n = any ? (int)(hi / kBN) - kt0 + 1 : 0;
+
+  if (tid == 0) {
+    mbar_init(bar(BAR_A), 32);
+    for (int i = 0; i < kNS; ++i) {
+      mbar_init(bar(BAR_FULL + i), 33);
+      mbar_init(bar(BAR_EMPTY + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(BAR_SD + i), 1);
+      mbar_init(bar(BAR_SDFREE + i), kCompute);
+      mbar_init(bar(BAR_P + i), kCompute);
+    }
+    mbar_init(bar(BAR_DONE), 2);
+    misc[1] = misc[2] = misc[3] = misc[4] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc(base + OFF_MISC, TM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+
+  if (warp == 8) {
+    // ---------------------------------------------------------- producer
+    const bf16* qh = reinterpret_cast<const bf16*>(p.q.p) + (long long)b * p.q.sb + (long long)h * kD;
+    const bf16* kh = reinterpret_cast<const bf16*>(p.k.p) + (long long)b * p.k.sb + (long long)h * kD;
+    const bf16* vh = reinterpret_cast<const bf16*>(p.v.p) + (long long)b * p.v.sb + (long long)h * kD;
+    const bf16* gh = reinterpret_cast<const bf16*>(p.G) + ((long long)b * s.Tq * s.H + h) * kD;
+    const bf16* gl = gh + (long long)s.B * s.Tq * s.H * kD;
+    const long long gst = (long long)s.H * kD;
+    for (int c = lane; c < kBM * 8; c += 32) {
+      const int row = c >> 3, ch = c & 7;
+      const long long t = i0 + row;
+      const bool ok = t < s.Tq;
+      const uint32_t off = tile_off<kD>(row, ch);
+      cp_async16(base + OFF_Q + off, qh + (ok ? t * p.q.st : 0) + ch * 8, ok);
+      cp_async16(base + OFF_GH + off, gh + (ok ? t * gst : 0) + ch * 8, ok);
+      cp_async16(base + OFF_GL + off, gl + (ok ? t * gst : 0) + ch * 8, ok);
+    }
+    mbar_arrive_cp_async(bar(BAR_A));
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int c = lane + 32 * hh;
+      float sn, cs;
+      sincospif((float)c / w, &sn, &cs);
+      tab[c] = cs;
+      tab[kBN + c] = sn;
+    }
+    __syncwarp();
+    const float cphi0 = tab[lane], sphi0 = tab[kBN + lane];
+    const float cphi1 = tab[lane + 32], sphi1 = tab[kBN + lane + 32];
+    const float* ikh = ax.ikT + (long long)bh * ax.Tkp;
+    const float* ivh = ax.ivT + (long long)bh * ax.Tkp;
+    const float4* mh = ax.mk + (long long)bh * (ax.Tkp / kBN);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % kNS;
+      if (j >= kNS) {
+        int okw = 1;
+        if (lane == 0) okw = mbar_wait(bar(BAR_EMPTY + st), ((j / kNS) - 1) & 1, abort_flag, kWaitLimitNs);
+        if (!__shfl_sync(0xffffffffu, okw, 0)) break;
+      }
+      const int kt = kt0 + j;
+      const long long j0 = (long long)kt * kBN;
+      const uint32_t kb = base + OFF_K + st * TILE_B, vb = base + OFF_V + st * TILE_B;
+      for (int c = lane; c < kBN * 8; c += 32) {
+        const int row = c >> 3, ch = c & 7;
+        const long long t = j0 + row;
+        const bool ok = t < s.Tk;
+        cp_async16(kb + tile_off<kD>(row, ch), kh + (ok ? t * p.k.st : 0) + ch * 8, ok);
+        cp_async16(vb + tile_off<kD>(row, ch), vh + (ok ? t * p.v.st : 0) + ch * 8, ok);
+      }
+      const uint32_t colb = base + OFF_COL + st * COLB;
+      float* col = colp + st * (COLB / 4);
+      if (lane < 16) cp_async16(colb + lane * 16, ikh + j0 + lane * 4, true);
+      else cp_async16(colb + kBN * 4 + (lane - 16) * 16, ivh + j0 + (lane - 16) * 4, true);
+      if (lane == 0) cp_async16(colb + 4 * kBN * 4, mh + kt, true);
+      float sb = 0.f, cb = 0.f;
+      if (lane == 0) sincospif((float)(j0 - p0) / w, &sb, &cb);
+      sb = __shfl_sync(0xffffffffu, sb, 0);
+      cb = __shfl_sync(0xffffffffu, cb, 0);
+      col[2 * kBN + lane] = cb * cphi0 - sb * sphi0;
+      col[3 * kBN + lane] = sb * cphi0 + cb * sphi0;
+      col[2 * kBN + lane + 32] = cb * cphi1 - sb * sphi1;
+      col[3 * kBN + lane + 32] = sb * cphi1 + cb * sphi1;
+      mbar_arrive_cp_async(bar(BAR_FULL + st));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_FULL + st));
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == 9) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(kBM, kBN, 0, 0);
+      constexpr uint32_t idQ = idesc_bf16(kBM, kD, 0, 1);
+      bool started = false, ok = mbar_wait(bar(BAR_A), 0, abort_flag, kWaitLimitNs);
+      auto issue_dq = [&](int jj) -> bool {
+        const int bb = jj & 1, st = jj % kNS;
+        if (!mbar_wait(bar(BAR_P + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
+        tc_fence_after();
+        if (!misc[1 + bb]) {
+          const uint32_t kb = base + OFF_K + st * TILE_B;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            mma_ts(tmem + TM_ACC1, tmem + TM_P1 + 32 * bb + 8 * kk,
+                   desc_sw128(kb + kk * 16 * 128, TILE_B, 1024), idQ,
+                   (started || kk > 0) ? 1u : 0u);
+          started = true;
+        }
+        mma_commit(bar(BAR_EMPTY + st));
+        return true;
+      };
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j % kNS, bb = j & 1;
+        ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
+        if (ok && j >= 2)
+          ok = mbar_wait(bar(BAR_SDFREE + bb), ((j >> 1) - 1) & 1, abort_flag, kWaitLimitNs);
+        if (!ok) break;
+        tc_fence_after();
+        fence_proxy_async_smem();
+        const uint32_t kb = base + OFF_K + st * TILE_B, vb = base + OFF_V + st * TILE_B;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem + TM_S + kBN * bb, desc_sw128(base + OFF_Q + kk * 32, 16, 1024),
+                 desc_sw128(kb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem + TM_DP + kBN * bb, desc_sw128(base + OFF_GH + kk * 32, 16, 1024),
+                 desc_sw128(vb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem + TM_DP + kBN * bb, desc_sw128(base + OFF_GL + kk * 32, 16, 1024),
+                 desc_sw128(vb + kk * 32, 16, 1024), idS, 1u);
+        mma_commit(bar(BAR_SD + bb));
+        if (j >= 1) ok = issue_dq(j - 1);
+      }
+      if (ok && n >= 1) ok = issue_dq(n - 1);
+      misc[3] = started ? 1u : 0u;
+      mma_commit(bar(BAR_DONE));
+      mbar_arrive(bar(BAR_DONE));
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------- compute
+    const int g = warp >> 2;                 // warpgroup: columns [32g, 32g+32)
+    const int t = tid & 127;                 // query row = TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int cb = 32 * g;
+    const long long i = i0 + t;
+    const float iq = (i < s.Tq) ? ax.iqT[(long long)bh * ax.Tqp + i] : 0.f;
+    const float rq = r * iq;
+    float crow, srow;
+    {
+      float sn, cs;
+      sincospif((float)t / w, &sn, &cs);
+      crow = 0.5f * cs;
+      srow = 0.5f * sn;
+    }
+    const float omr = 1.0f - r;
+    const long long pos = i + s.q_offset;
+    const float2 rq2 = make_float2(rq, rq), omr2 = make_float2(omr, omr);
+    const float2 cr2 = make_float2(crow, crow), sr2 = make_float2(srow, srow);
+    const float2 half2 = make_float2(0.5f, 0.5f), twor2 = make_float2(2.f * r, 2.f * r);
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const int st = j % kNS, bb = j & 1;
+      ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
+           mbar_wait(bar(BAR_SD + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
+      if (bar_red_or(1, kCompute, !ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[32], dv[32];
+      tmem_ld32(tmem + TM_S + kBN * bb + cb + lane_off, sv);
+      tmem_ld32(tmem + TM_DP + kBN * bb + cb + lane_off, dv);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(bar(BAR_SDFREE + bb));
+      const float* col = colp + st * (COLB / 4);
+      int imax = (int)sv[0];
+#pragma unroll
+      for (int c = 1; c + 1 < 32; c += 2) imax = __vimax3_s32(imax, (int)sv[c], (int)sv[c + 1]);
+      imax = max(imax, (int)sv[31]);
+      const bool mine = r < 1.0f ||
+                        (imax > 0 && fmaf(rq, __int_as_float(imax) * col[4 * kBN], omr) > 0.f);
+      const bool live = bar_red_or(1, kCompute, mine);
+      if (live) {
+        const long long j0 = (long long)(kt0 + j) * kBN;
+        const bool inside = (causal ? (p0 - (j0 + kBN - 1) >= 0 && p0 + kBM - 1 - j0 <= dmax)
+                                    : (p0 - (j0 + kBN - 1) >= -(long long)dmax &&
+                                       p0 + kBM - 1 - j0 <= dmax));
+        const long long clo_ = pos - dmax - j0 - cb, chi_ = (causal ? pos : pos + dmax) - j0 - cb;
+        const int iclo = inside ? 0 : (int)(clo_ < 0 ? 0 : (clo_ > 32 ? 32 : clo_));
+        const int ichi = inside ? 31 : (int)(chi_ < -1 ? -1 : (chi_ > 31 ? 31 : chi_));
+        const float4* ik4 = reinterpret_cast<const float4*>(col + cb);
+        const float4* iv4 = reinterpret_cast<const float4*>(col + kBN + cb);
+        const float4* cc4 = reinterpret_cast<const float4*>(col + 2 * kBN + cb);
+        const float4* sc4 = reinterpret_cast<const float4*>(col + 3 * kBN + cb);
+        uint32_t pk[16];
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const float4 ikv = ik4[q4], ivv = iv4[q4], ccv = cc4[q4], scv = sc4[q4];
+#pragma unroll
+          for (int hp = 0; hp < 2; ++hp) {
+            const int c = 4 * q4 + 2 * hp;
+            const float2 ik2 = hp ? make_float2(ikv.z, ikv.w) : make_float2(ikv.x, ikv.y);
+            const float2 iv2 = hp ? make_float2(ivv.z, ivv.w) : make_float2(ivv.x, ivv.y);
+            const float2 cc2 = hp ? make_float2(ccv.z, ccv.w) : make_float2(ccv.x, ccv.y);
+            const float2 sc2 = hp ? make_float2(scv.z, scv.w) : make_float2(scv.x, scv.y);
+            const float2 x = __fmul2_rn(make_float2(__uint_as_float(sv[c]),
+                                                    __uint_as_float(sv[c + 1])), ik2);
+            const float2 t2 = __ffma2_rn(rq2, x, omr2);
+            const float2 a2 = make_float2((c >= iclo && c <= ichi) ? fmaxf(t2.x, 0.f) : 0.f,
+                                          (c + 1 >= iclo && c + 1 <= ichi) ? fmaxf(t2.y, 0.f) : 0.f);
+            const float2 m2 = __ffma2_rn(cr2, cc2, __ffma2_rn(sr2, sc2, half2));
+            const float2 dp2 = __fmul2_rn(make_float2(__uint_as_float(dv[c]),
+                                                      __uint_as_float(dv[c + 1])), iv2);
+            const float2 q2 = __fmul2_rn(__fmul2_rn(dp2, m2), a2);
+            const float2 ds = __fmul2_rn(q2, __fmul2_rn(ik2, twor2));
+            pk[2 * q4 + hp] = pack_bf16(ds.x, ds.y);
+          }
+        }
+        tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, pk);
+        tmem_wait_st();
+      }
+      if (tid == 0) misc[1 + bb] = live ? 0u : 1u;
+      tc_fence_before();
+      mbar_arrive(bar(BAR_P + bb));
+    }
+    // epilogue (warpgroup 0): dQ -> normalisation Jacobian -> dq
+    if (g == 0) {
+      ok = ok && mbar_wait(bar(BAR_DONE), 0, abort_flag, kWaitLimitNs);
+      // tcgen05.ld is warp-collective: every lane takes the same branch
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      float acc[64];
+      if (ok && misc[3]) {
+        tmem_ld64(tmem + TM_ACC1 + lane_off, acc);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+      }
+      if (ok && i < s.Tq) {
+        const bf16* qrow = reinterpret_cast<const bf16*>(p.q.p) + (long long)b * p.q.sb +
+                           i * p.q.st + (long long)h * kD;
+        bf16* orow = reinterpret_cast<bf16*>(p.dq.p) + (long long)b * p.dq.sb + i * p.dq.st +
+                     (long long)h * kD;
+        store_unit_jacobian(acc, qrow, iq, orow);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, TM_COLS);
+  if (tid == 0 && *abort_flag) atomicExch(status_word(), (int)SCREEN_ERR_TIMEOUT);
+}
+
+// ===========================================================================
+// dk / dv kernel
+// ===========================================================================
+namespace kv {
+constexpr uint32_t OFF_K = 0, OFF_V = TILE_A;
+constexpr uint32_t OFF_Q = 2 * TILE_A;                 // per stage: Q | G_hi | G_lo (8 KB each)
+constexpr uint32_t STAGE = 3 * TILE_B;
+constexpr uint32_t OFF_COL = OFF_Q + kNS * STAGE;       // per stage iq | cos | sin [64] + meta
+constexpr uint32_t COLB = 3 * kBN * 4 + 16;
+constexpr uint32_t OFF_TAB = OFF_COL + kNS * COLB;
+constexpr uint32_t OFF_RED = OFF_TAB + 2 * kBN * 4;     // [2][8] dr / dw warp sums
+constexpr uint32_t OFF_BAR = OFF_RED + 64 * 4;
+constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNS, BAR_SD = BAR_EMPTY + kNS,
+              BAR_SDFREE = BAR_SD + 2, BAR_P = BAR_SDFREE + 2, BAR_DONE = BAR_P + 2;
+constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 16;
+constexpr uint32_t SMEM = (OFF_MISC + 64 + 1024 > 120 * 1024) ? OFF_MISC + 64 + 1024 : 120 * 1024;
+}  // namespace kv
+
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_bwd_kv_kernel(AttnShape s, BwdPtrs p, Aux ax) {
+  using namespace kv;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw_addr);
+  float* colp = reinterpret_cast<float*>(gbase + OFF_COL);
+  float* tab = reinterpret_cast<float*>(gbase + OFF_TAB);
+  float* red = reinterpret_cast<float*>(gbase + OFF_RED);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(gbase + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
+  const uint32_t bars = base + OFF_BAR;
+  auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y, b = bh / s.H, h = bh % s.H;
+  const long long j0 = (long long)blockIdx.x * kBM;
+  const bool causal = s.causal != 0;
+  const float r = s.r[h], w = s.w[h];
+  const int dmax = window_dmax(w);
+  long long jlast = j0 + kBM - 1;
+  if (jlast > s.Tk - 1) jlast = s.Tk - 1;
+  long long plo, phi;
+  query_pos_range(j0, jlast, dmax, causal, plo, phi);
+  long long ilo = plo - s.q_offset, ihi = phi - s.q_offset;
+  if (ilo < 0) ilo = 0;
+  if (ihi > s.Tq - 1) ihi = s.Tq - 1;
+  const bool any = dmax >= 0 && ilo <= ihi;
+  const int qt0 = any ? (int)(ilo / kBN) : 0;
+  const int n = any ? (int)(ihi / kBN) - qt0 + 1 : 0;
+
+  if (tid == 0) {
+    mbar_init(bar(BAR_A), 32);
+    for (int i = 0; i < kNS; ++i) {
+      mbar_init(bar(BAR_FULL + i), 33);
+      mbar_init(bar(BAR_EMPTY + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(BAR_SD + i), 1);
+      mbar_init(bar(BAR_SDFREE + i), kCompute);
+      mbar_init(bar(BAR_P + i), kCompute);
+    }
+    mbar_init(bar(BAR_DONE), 2);
+    misc[1] = misc[2] = misc[3] = misc[4] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc(base + OFF_MISC, TM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+
+  const bf16* kh = reinterpret_cast<const bf16*>(p.k.p) + (long long)b * p.k.sb + (long long)h * kD;
+  const bf16* vh = reinterpret_cast<const bf16*>(p.v.p) + (long long)b * p.v.sb + (long long)h * kD;
+  float acc_r = 0.f, acc_w = 0.f;
+
+  if (warp == 8) {
+    // ---------------------------------------------------------- producer
+    const bf16* qh = reinterpret_cast<const bf16*>(p.q.p) + (long long)b * p.q.sb + (long long)h * kD;
+    const bf16* gh = reinterpret_cast<const bf16*>(p.G) + ((long long)b * s.Tq * s.H + h) * kD;
+    const bf16* gl = gh + (long long)s.B * s.Tq * s.H * kD;
+    const long long gst = (long long)s.H * kD;
+    for (int c = lane; c < kBM * 8; c += 32) {
+      const int row = c >> 3, ch = c & 7;
+      const long long t = j0 + row;
+      const bool ok = t < s.Tk;
+      const uint32_t off = tile_off<kD>(row, ch);
+      cp_async16(base + OFF_K + off, kh + (ok ? t * p.k.st : 0) + ch * 8, ok);
+      cp_async16(base + OFF_V + off, vh + (ok ? t * p.v.st : 0) + ch * 8, ok);
+    }
+    mbar_arrive_cp_async(bar(BAR_A));
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int c = lane + 32 * hh;
+      float sn, cs;
+      sincospif((float)c / w, &sn, &cs);
+      tab[c] = cs;
+      tab[kBN + c] = sn;
+    }
+    __syncwarp();
+    const float cphi0 = tab[lane], sphi0 = tab[kBN + lane];
+    const float cphi1 = tab[lane + 32], sphi1 = tab[kBN + lane + 32];
+    const float* iqh = ax.iqT + (long long)bh * ax.Tqp;
+    const float4* mh = ax.mq + (long long)bh * (ax.Tqp / kBN);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % kNS;
+      if (j >= kNS) {
+        int okw = 1;
+        if (lane == 0) okw = mbar_wait(bar(BAR_EMPTY + st), ((j / kNS) - 1) & 1, abort_flag, kWaitLimitNs);
+        if (!__shfl_sync(0xffffffffu, okw, 0)) break;
+      }
+      const int qt = qt0 + j;
+      const long long iq0 = (long long)qt * kBN;
+      const uint32_t sb_ = base + OFF_Q + st * STAGE;
+      for (int c = lane; c < kBN * 8; c += 32) {
+        const int row = c >> 3, ch = c & 7;
+        const long long t = iq0 + row;
+        const bool ok = t < s.Tq;
+        const uint32_t off = tile_off<kD>(row, ch);
+        cp_async16(sb_ + off, qh + (ok ? t * p.q.st : 0) + ch * 8, ok);
+        cp_async16(sb_ + TILE_B + off, gh + (ok ? t * gst : 0) + ch * 8, ok);
+        cp_async16(sb_ + 2 * TILE_B + off, gl + (ok ? t * gst : 0) + ch * 8, ok);
+      }
+      const uint32_t colb = base + OFF_COL + st * COLB;
+      float* col = colp + st * (COLB / 4);
+      if (lane < 16) cp_async16(colb + lane * 16, iqh + iq0 + lane * 4, true);
+      else if (lane == 16) cp_async16(colb + 3 * kBN * 4, mh + qt, true);
+      // column angle pi (iq0 + c + q_offset - j0) / w by rotation
+      float sb = 0.f, cbv = 0.f;
+      if (lane == 0) sincospif((float)(iq0 + s.q_offset - j0) / w, &sb, &cbv);
+      sb = __shfl_sync(0xffffffffu, sb, 0);
+      cbv = __shfl_sync(0xffffffffu, cbv, 0);
+      col[kBN + lane] = cbv * cphi0 - sb * sphi0;
+      col[2 * kBN + lane] = sb * cphi0 + cbv * sphi0;
+      col[kBN + lane + 32] = cbv * cphi1 - sb * sphi1;
+      col[2 * kBN + lane + 32] = sb * cphi1 + cbv * sphi1;
+      mbar_arrive_cp_async(bar(BAR_FULL + st));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_FULL + st));
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == 9) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(kBM, kBN, 0, 0);
+      constexpr uint32_t idMN = idesc_bf16(kBM, kD, 0, 1);
+      bool started = false, ok = mbar_wait(bar(BAR_A), 0, abort_flag, kWaitLimitNs);
+      auto issue_kv = [&](int jj) -> bool {
+        const int bb = jj & 1, st = jj % kNS;
+        if (!mbar_wait(bar(BAR_P + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
+        tc_fence_after();
+        if (!misc[1 + bb]) {
+          const uint32_t qb = base + OFF_Q + st * STAGE, ghb = qb + TILE_B;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            mma_ts(tmem + TM_ACC1, tmem + TM_P1 + 32 * bb + 8 * kk,
+                   desc_sw128(ghb + kk * 16 * 128, TILE_B, 1024), idMN,
+                   (started || kk > 0) ? 1u : 0u);
+            mma_ts(tmem + TM_ACC2, tmem + TM_P2 + 32 * bb + 8 * kk,
+                   desc_sw128(qb + kk * 16 * 128, TILE_B, 1024), idMN,
+                   (started || kk > 0) ? 1u : 0u);
+          }
+          started = true;
+        }
+        mma_commit(bar(BAR_EMPTY + st));
+        return true;
+      };
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j % kNS, bb = j & 1;
+        ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
+        if (ok && j >= 2)
+          ok = mbar_wait(bar(BAR_SDFREE + bb), ((j >> 1) - 1) & 1, abort_flag, kWaitLimitNs);
+        if (!ok) break;
+        tc_fence_after();
+        fence_proxy_async_smem();
+        const uint32_t qb = base + OFF_Q + st * STAGE, ghb = qb + TILE_B, glb = qb + 2 * TILE_B;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem + TM_S + kBN * bb, desc_sw128(base + OFF_K + kk * 32, 16, 1024),
+                 desc_sw128(qb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem + TM_DP + kBN * bb, desc_sw128(base + OFF_V + kk * 32, 16, 1024),
+                 desc_sw128(ghb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem + TM_DP + kBN * bb, desc_sw128(base + OFF_V + kk * 32, 16, 1024),
+                 desc_sw128(glb + kk * 32, 16, 1024), idS, 1u);
+        mma_commit(bar(BAR_SD + bb));
+        if (j >= 1) ok = issue_kv(j - 1);
+      }
+      if (ok && n >= 1) ok = issue_kv(n - 1);
+      misc[3] = started ? 1u : 0u;
+      mma_commit(bar(BAR_DONE));
+      mbar_arrive(bar(BAR_DONE));
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------- compute
+    const int g = warp >> 2;
+    const int t = tid & 127;                   // key row = TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int cb = 32 * g;
+    const long long jrow = j0 + t;
+    const bool valid = jrow < s.Tk;
+    const bool keep = valid && !(s.kpm && s.kpm[(long long)b * s.kpm_sb + jrow]);
+    const long long nidx = ((long long)b * s.Tk + (valid ? jrow : 0)) * s.H + h;
+    const float ik = valid ? 1.0f / p.nk[nidx] : 0.f;
+    const float iv = valid ? 1.0f / p.nv[nidx] : 0.f;
+    const float rk = keep ? r * ik : 0.f;
+    const float omr = keep ? 1.0f - r : -1.0f;  // masked key rows: t <= 0, a = 0
+    float crow, srow;
+    {
+      float sn, cs;
+      sincospif((float)t / w, &sn, &cs);
+      crow = 0.5f * cs;
+      srow = 0.5f * sn;
+    }
+    const float2 rk2 = make_float2(rk, rk), omr2 = make_float2(omr, omr);
+    const float2 cr2 = make_float2(crow, crow), sr2 = make_float2(srow, srow);
+    const float2 sr2x2 = make_float2(2.f * srow, 2.f * srow);
+    const float2 ncr2x2 = make_float2(-2.f * crow, -2.f * crow);
+    const float2 half2 = make_float2(0.5f, 0.5f), twor2 = make_float2(2.f * r, 2.f * r);
+    const float2 iv2 = make_float2(iv, iv), ik2 = make_float2(ik, ik);
+    const float2 m1 = make_float2(-1.f, -1.f);
+    float2 accr2 = make_float2(0.f, 0.f), accw2 = make_float2(0.f, 0.f);
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const int st = j % kNS, bb = j & 1;
+      ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
+           mbar_wait(bar(BAR_SD + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
+      if (bar_red_or(1, kCompute, !ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[32], dv[32];
+      tmem_ld32(tmem + TM_S + kBN * bb + cb + lane_off, sv);
+      tmem_ld32(tmem + TM_DP + kBN * bb + cb + lane_off, dv);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(bar(BAR_SDFREE + bb));
+      const float* col = colp + st * (COLB / 4);
+      int imax = (int)sv[0];
+#pragma unroll
+      for (int c = 1; c + 1 < 32; c += 2) imax = __vimax3_s32(imax, (int)sv[c], (int)sv[c + 1]);
+      imax = max(imax, (int)sv[31]);
+      const bool mine = (r < 1.0f && keep) ||
+                        (imax > 0 && fmaf(rk, __int_as_float(imax) * col[3 * kBN], omr) > 0.f);
+      const bool live = bar_red_or(1, kCompute, mine);
+      if (live) {
+        const long long pq0 = (long long)(qt0 + j) * kBN + s.q_offset;
+        // d = p - j over the tile: [pq0 - (j0 + 127), pq0 + 63 - j0]
+        const long long dlo = pq0 - (j0 + kBM - 1), dhi = pq0 + kBN - 1 - j0;
+        const bool inside = causal ? (dlo >= 0 && dhi <= dmax)
+                                   : (dlo >= -(long long)dmax && dhi <= dmax);
+        // this row's valid query columns: p - j in [0, dmax] (causal) or [-dmax, dmax]
+        const long long clo_ = (causal ? jrow : jrow - dmax) - pq0 - cb;
+        const long long chi_ = jrow + dmax - pq0 - cb;
+        const int iclo = inside ? 0 : (int)(clo_ < 0 ? 0 : (clo_ > 32 ? 32 : clo_));
+        const int ichi = inside ? 31 : (int)(chi_ < -1 ? -1 : (chi_ > 31 ? 31 : chi_));
+        const float relb = (float)(jrow - pq0 - cb);   // rel = j - p = relb - c
+        const float4* iq4 = reinterpret_cast<const float4*>(col + cb);
+        const float4* cv4 = reinterpret_cast<const float4*>(col + kBN + cb);
+        const float4* sv4 = reinterpret_cast<const float4*>(col + 2 * kBN + cb);
+        uint32_t pa[16], pd[16];
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const float4 iqv = iq4[q4], cvv = cv4[q4], svv = sv4[q4];
+#pragma unroll
+          for (int hp = 0; hp < 2; ++hp) {
+            const int c = 4 * q4 + 2 * hp;
+            const float2 iq2 = hp ? make_float2(iqv.z, iqv.w) : make_float2(iqv.x, iqv.y);
+            const float2 cv2 = hp ? make_float2(cvv.z, cvv.w) : make_float2(cvv.x, cvv.y);
+            const float2 sn2 = hp ? make_float2(svv.z, svv.w) : make_float2(svv.x, svv.y);
+            const float2 x = __fmul2_rn(make_float2(__uint_as_float(sv[c]),
+                                                    __uint_as_float(sv[c + 1])), iq2);
+            const float2 t2 = __ffma2_rn(rk2, x, omr2);
+            const float2 a2 = make_float2((c >= iclo && c <= ichi) ? fmaxf(t2.x, 0.f) : 0.f,
+                                          (c + 1 >= iclo && c + 1 <= ichi) ? fmaxf(t2.y, 0.f) : 0.f);
+            const float2 m2 = __ffma2_rn(cr2, cv2, __ffma2_rn(sr2, sn2, half2));
+            const float2 sinrel = __ffma2_rn(ncr2x2, sn2, __fmul2_rn(sr2x2, cv2));
+            const float2 dp2 = __fmul2_rn(make_float2(__uint_as_float(dv[c]),
+                                                      __uint_as_float(dv[c + 1])), iv2);
+            const float2 asq = __fmul2_rn(a2, a2);
+            const float2 al = __fmul2_rn(asq, m2);
+            const float2 q2 = __fmul2_rn(dp2, __fmul2_rn(a2, m2));  // dP m a
+            const float2 ds = __fmul2_rn(q2, __fmul2_rn(iq2, twor2));
+            pa[2 * q4 + hp] = pack_bf16(al.x, al.y);
+            pd[2 * q4 + hp] = pack_bf16(ds.x, ds.y);
+            accr2 = __ffma2_rn(q2, __ffma2_rn(x, ik2, m1), accr2);
+            const float2 rel = make_float2(relb - (float)c, relb - (float)(c + 1));
+            accw2 = __ffma2_rn(__fmul2_rn(dp2, asq), __fmul2_rn(rel, sinrel), accw2);
+          }
+        }
+        tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, pa);
+        tmem_st16(tmem + TM_P2 + 32 * bb + 16 * g + lane_off, pd);
+        tmem_wait_st();
+      }
+      if (tid == 0) misc[1 + bb] = live ? 0u : 1u;
+      tc_fence_before();
+      mbar_arrive(bar(BAR_P + bb));
+    }
+    acc_r = 2.f * (accr2.x + accr2.y);   // dr = sum dP m 2a (S - 1)
+    acc_w = accw2.x + accw2.y;
+    // epilogue: warpgroup 0 -> dk, warpgroup 1 -> dv (normalisation Jacobians)
+    ok = ok && mbar_wait(bar(BAR_DONE), 0, abort_flag, kWaitLimitNs);
+    // tcgen05.ld is warp-collective: every lane takes the same branch
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    float acc[64];
+    if (ok && misc[3]) {
+      tmem_ld64(tmem + (g == 0 ? TM_ACC2 : TM_ACC1) + lane_off, acc);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+    }
+    if (ok && valid) {
+      if (g == 0) {
+        store_unit_jacobian(acc, kh + jrow * p.k.st, ik,
+                            reinterpret_cast<bf16*>(p.dk.p) + (long long)b * p.dk.sb +
+                                jrow * p.dk.st + (long long)h * kD);
+      } else {
+        store_unit_jacobian(acc, vh + jrow * p.v.st, iv,
+                            reinterpret_cast<bf16*>(p.dv.p) + (long long)b * p.dv.sb +
+                                jrow * p.dv.st + (long long)h * kD);
+      }
+    }
+  }
+  // dr / dw partial of this CTA, fixed summation order
+  acc_r = warp_sum(acc_r);
+  acc_w = warp_sum(acc_w);
+  if (lane == 0 && warp < 8) {
+    red[warp] = acc_r;
+    red[8 + warp] = acc_w;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0) {
+    float sr = 0.f, sw = 0.f;
+    for (int k2 = 0; k2 < 8; ++k2) {
+      sr += red[k2];
+      sw += red[8 + k2];
+    }
+    const long long P = (long long)s.B * gridDim.x;
+    const long long idx = (long long)h * P + (long long)b * gridDim.x + blockIdx.x;
+    p.part_r[idx] = sr;
+    p.part_w[idx] = sw;
+    if (*abort_flag) atomicExch(status_word(), (int)SCREEN_ERR_TIMEOUT);
+  }
+  if (warp == 0) tmem_dealloc(tmem, TM_COLS);
+}
+
+// transposed inverse norms per (b, h) and per-64-tile maxima; grid
+// (B*H*tiles, 2): y = 0 for q, y = 1 for k (and v)
+__global__ void tc_bwd_aux_kernel(const float* __restrict__ nq, const float* __restrict__ nk,
+                                  const float* __restrict__ nv, const uint8_t* kpm,
+                                  long long kpm_sb, int B, int H, int Tq, int Tk, int Tqp,
+                                  int Tkp, float* iqT, float* ikT, float* ivT, float4* mq,
+                                  float4* mk) {
+  const bool isk = blockIdx.y == 1;
+  const int Tp = isk ? Tkp : Tqp, T = isk ? Tk : Tq;
+  const int ntiles = Tp / kBN;
+  const long long blk = blockIdx.x;
+  if (blk >= (long long)B * H * ntiles) return;
+  const long long bhh = blk / ntiles;
+  const int tile = (int)(blk % ntiles);
+  const int bb = (int)(bhh / H), hh = (int)(bhh % H);
+  const int c = threadIdx.x;  // 64 threads
+  const long long t = (long long)tile * kBN + c;
+  float x = 0.f;
+  if (t < T) {
+    const long long idx = ((long long)bb * T + t) * H + hh;
+    if (!isk) {
+      x = 1.0f / nq[idx];
+      iqT[bhh * Tp + t] = x;
+    } else {
+      x = 1.0f / nk[idx];
+      ikT[bhh * Tp + t] = x;
+      const bool masked = kpm && kpm[(long long)bb * kpm_sb + t];
+      ivT[bhh * Tp + t] = masked ? 0.f : 1.0f / nv[idx];
+    }
+  } else {
+    if (!isk) iqT[bhh * Tp + t] = 0.f;
+    else {
+      ikT[bhh * Tp + t] = 0.f;
+      ivT[bhh * Tp + t] = 0.f;
+    }
+  }
+  __shared__ float sm[2];
+  float m = x;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((c & 31) == 0) sm[c >> 5] = m;
+  __syncthreads();
+  if (c == 0) (isk ? mk : mq)[blk] = make_float4(fmaxf(sm[0], sm[1]), 0.f, 0.f, 0.f);
+}
+
+bool g_bwd_attr[64];
+long long padT(int T) { return ((long long)T + kBN - 1) / kBN * kBN; }
+size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+size_t tc_bwd_aux_bytes(const AttnShape& s) {
+  const long long BH = (long long)s.B * s.H, Tqp = padT(s.Tq), Tkp = padT(s.Tk);
+  return al256(BH * Tqp * 4) + 2 * al256(BH * Tkp * 4) + al256(BH * (Tqp / kBN) * 16) +
+         al256(BH * (Tkp / kBN) * 16);
+}
+
+long long tc_bwd_partials(const AttnShape& s) {
+  return (long long)s.B * ((s.Tk + kBM - 1) / kBM);
+}
+
+void tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st) {
+  if (s.B == 0 || s.H == 0) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !g_bwd_attr[dev]) {
+    cudaFuncSetAttribute(tc_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)dq::SMEM);
+    cudaFuncSetAttribute(tc_bwd_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kv::SMEM);
+    g_bwd_attr[dev] = true;
+  }
+  const long long BH = (long long)s.B * s.H, Tqp = padT(s.Tq), Tkp = padT(s.Tk);
+  uint8_t* w8 = reinterpret_cast<uint8_t*>(aux_ws);
+  Aux ax;
+  float* iqT = reinterpret_cast<float*>(w8);
+  w8 += al256(BH * Tqp * 4);
+  float* ikT = reinterpret_cast<float*>(w8);
+  w8 += al256(BH * Tkp * 4);
+  float* ivT = reinterpret_cast<float*>(w8);
+  w8 += al256(BH * Tkp * 4);
+  float4* mq = reinterpret_cast<float4*>(w8);
+  w8 += al256(BH * (Tqp / kBN) * 16);
+  float4* mk = reinterpret_cast<float4*>(w8);
+  ax.iqT = iqT; ax.ikT = ikT; ax.ivT = ivT; ax.mq = mq; ax.mk = mk;
+  ax.Tqp = (int)Tqp; ax.Tkp = (int)Tkp;
+  const long long nblk = BH * ((Tqp > Tkp ? Tqp : Tkp) / kBN);
+  if (nblk > 0)
+    tc_bwd_aux_kernel<<<dim3((unsigned)nblk, 2), 64, 0, st>>>(
+        p.nq, p.nk, p.nv, s.kpm, s.kpm_sb, s.B, s.H, s.Tq, s.Tk, (int)Tqp, (int)Tkp, iqT, ikT,
+        ivT, mq, mk);
+  if (s.Tq > 0 && (stages & 2)) {
+    dim3 g1((s.Tq + kBM - 1) / kBM, s.B * s.H);
+    tc_bwd_dq_kernel<<<g1, kThreads, dq::SMEM, st>>>(s, p, ax);
+  }
+  if (s.Tk > 0 && (stages & 4)) {
+    dim3 g2((s.Tk + kBM - 1) / kBM, s.B * s.H);
+    tc_bwd_kv_kernel<<<g2, kThreads, kv::SMEM, st>>>(s, p, ax);
+  }
+}
+
+int tc_bwd_device_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_bwd_status, sizeof(int)) != cudaSuccess) return SCREEN_ERR_CUDA;
+  if (clear && v != 0) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_bwd_status, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace screen
