@@ -344,6 +344,14 @@ def main():
             e2e_ev.append((a, b))
     torch.cuda.synchronize()
     e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev) / len(e2e_ev)
+    # the host link on its own: pinned host -> device copy of one step's input
+    a, bb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(3):
+        x_dev.copy_(x_host, non_blocking=True)
+    bb.record()
+    torch.cuda.synchronize()
+    h2d_gbs = 3 * x.numel() * x.element_size() / (a.elapsed_time(bb) / 1e3) / 1e9
     clk.__exit__(None, None, None)
     if dist is not None:
         t = torch.tensor([e2e_ms], device=dev)
@@ -367,7 +375,8 @@ def main():
             "tile_stats": {"fwd_blocks_in_window": visited, "fwd_blocks_live": live},
             "cpu_baseline": cpu,
             "e2e": {"value": tokens_per_step / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4},
+                    "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
+                    "h2d_gbs_measured": h2d_gbs, "pinned": bool(x_host.is_pinned())},
             "clocks": clk.summary(),
             "gpu_launches": 6 * args.steps,
         }

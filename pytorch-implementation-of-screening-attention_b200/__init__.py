@@ -14,7 +14,7 @@ as `screening_b200`:
 import sys as _sys
 
 from .attention import ScreeningAttention
-from .functional import ScreenFn, screening_attention, tanh_norm
+from .functional import ScreenFn, ScreenPackedFn, screening_attention, screening_attention_packed, tanh_norm
 from .kv_cache import PagedKVCache
 from .layers import MultiscreenBlock, MultiscreenDecoderLayer
 from .model import MultiscreenLM

@@ -17,7 +17,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib
-from .functional import screening_attention
+from .functional import screening_attention, screening_attention_packed
 from .norm import TanhNorm
 
 
@@ -82,9 +82,19 @@ class ScreeningAttention(nn.Module):
         key_padding_mask (B,T_k) bool, True = ignore.  Returns (B,T_q,d_model)."""
         self._check_dropout()
         B, Tq, _ = query.shape
-        q, k, v = self._qkv(query, key, value)
-        y = screening_attention(q, k, v, self.sharpness(), self.window(), causal=self.causal,
-                                key_padding_mask=key_padding_mask, eps=self.eps)
+        if query is key and key is value:
+            # self-attention: one GEMM for the three projections; the kernels
+            # read q, k, v in place and write their gradients into one buffer
+            H, D = self.num_heads, self.head_dim
+            wqkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
+            qkv = F.linear(query, wqkv).view(B, Tq, 3, H, D)
+            y = screening_attention_packed(qkv, self.sharpness(), self.window(),
+                                           causal=self.causal,
+                                           key_padding_mask=key_padding_mask, eps=self.eps)
+        else:
+            q, k, v = self._qkv(query, key, value)
+            y = screening_attention(q, k, v, self.sharpness(), self.window(), causal=self.causal,
+                                    key_padding_mask=key_padding_mask, eps=self.eps)
         return self.out_proj(y.reshape(B, Tq, self.d_model))
 
     # ------------------------------------------------------------------

@@ -60,6 +60,49 @@ def screening_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, r: to
     return y if y.dtype == out_dtype else y.to(out_dtype)
 
 
+class ScreenPackedFn(torch.autograd.Function):
+    """Self-attention on a packed (B, T, 3, H, D) QKV projection: the kernels
+    read q, k, v as strided views and the backward writes dq, dk, dv straight
+    into one packed gradient, so no per-view gradient assembly follows."""
+
+    @staticmethod
+    def forward(ctx, qkv, r, w, causal, key_padding_mask, eps):
+        q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+        y, no, nq, nk, nv, qq, kk, vv = _lib.screen_fwd(q, k, v, r, w, causal, key_padding_mask,
+                                                        eps, 0)
+        ctx.save_for_backward(qkv, nq, nk, nv, y, no, r, w, key_padding_mask)
+        ctx.causal, ctx.eps = causal, eps
+        ctx.has_kpm = key_padding_mask is not None
+        ctx.views_ok = qq.data_ptr() == q.data_ptr() and kk.data_ptr() == k.data_ptr()
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        qkv, nq, nk, nv, y, no, r, w, kpm = ctx.saved_tensors
+        q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+        dqkv = torch.empty_like(qkv)
+        out = (dqkv[:, :, 0], dqkv[:, :, 1], dqkv[:, :, 2])
+        _, _, _, dr, dw = _lib.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, r, w, ctx.causal,
+                                          kpm if ctx.has_kpm else None, ctx.eps, 0, out=out)
+        return (dqkv, dr.to(r.dtype) if ctx.needs_input_grad[1] else None,
+                dw.to(w.dtype) if ctx.needs_input_grad[2] else None, None, None, None)
+
+
+def screening_attention_packed(qkv: torch.Tensor, r: torch.Tensor, w: torch.Tensor,
+                               causal: bool = True,
+                               key_padding_mask: torch.Tensor | None = None,
+                               eps: float = 1e-8) -> torch.Tensor:
+    """screening_attention for self-attention with q, k, v packed as one
+    contiguous (B, T, 3, H, D) projection output (the fused QKV GEMM)."""
+    if not qkv.is_cuda:
+        raise RuntimeError("screening_attention runs on CUDA tensors only (no CPU path)")
+    if qkv.dtype == torch.float16 or not qkv.is_contiguous():
+        q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+        return screening_attention(q, k, v, r, w, causal, key_padding_mask, eps)
+    return ScreenPackedFn.apply(qkv, r.float(), w.float(), bool(causal), key_padding_mask,
+                                float(eps))
+
+
 class TanhNormFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, eps):

@@ -130,3 +130,26 @@ def test_tanhnorm_module_grad(ms, oracle):
     y.backward(dy.to(DEV))
     assert rel_err(y, ref) <= 1e-5
     assert rel_err(xc.grad, xr.grad) <= 1e-4
+
+
+def test_packed_qkv_path_matches_separate_views(ms):
+    """Self-attention routes through the packed (B,T,3,H,D) Function; its
+    output and every gradient equal the three-view path's."""
+    torch.manual_seed(3)
+    attn = ms.ScreeningAttention(128, 2).to(DEV).to(torch.bfloat16)
+    with torch.no_grad():
+        attn.s_r.copy_(torch.log(torch.tensor([0.1, 0.4])))
+    x = torch.randn(2, 200, 128, device=DEV, dtype=torch.bfloat16)
+    x1 = x.clone().requires_grad_(True)
+    y1 = attn(x1, x1, x1)                       # packed path
+    y1.float().square().sum().backward()
+    g1 = [p.grad.clone() for p in attn.parameters()]
+    attn.zero_grad()
+    x2 = x.clone().requires_grad_(True)
+    y2 = attn(x2, x2.clone(), x2.clone())        # separate projections
+    y2.float().square().sum().backward()
+    g2 = [p.grad.clone() for p in attn.parameters()]
+    assert rel_err(y1, y2) <= 1e-2
+    assert rel_err(x1.grad, x2.grad) <= 2e-2
+    for a, b in zip(g1, g2):
+        assert rel_err(a, b) <= 2e-2
