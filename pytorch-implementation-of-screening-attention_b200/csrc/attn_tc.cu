@@ -243,8 +243,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     auto pair_alpha = [&](float s0, float s1, float ik0, float ik1, float c0, float c1, float n0,
                           float n1, bool k0, bool k1) -> uint32_t {
       const float2 x = __fmul2_rn(make_float2(s0, s1), make_float2(ik0, ik1));
-      const float2 t2 = __ffma2_rn(rq2, x, omr2);
-      const float2 a2 = make_float2(k0 ? fmaxf(t2.x, 0.f) : 0.f, k1 ? fmaxf(t2.y, 0.f) : 0.f);
+      // relu(t) = saturate(t): t = 1 - r (1 - S) <= 1, so the clamp is free
+      const float a0 = __saturatef(fmaf(rq, x.x, omr)), a1 = __saturatef(fmaf(rq, x.y, omr));
+      const float2 a2 = make_float2(k0 ? a0 : 0.f, k1 ? a1 : 0.f);
       const float2 m2 =
           __ffma2_rn(cr2, make_float2(c0, c1), __ffma2_rn(sr2, make_float2(n0, n1), half2));
       const float2 al = __fmul2_rn(__fmul2_rn(a2, m2), a2);

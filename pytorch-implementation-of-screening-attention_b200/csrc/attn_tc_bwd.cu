@@ -18,6 +18,7 @@
 //       plus the per-CTA dr / dw partials (summed in a fixed order later).
 // Every wait is bounded (global timer); on expiry the CTA drains and records
 // SCREEN_ERR_TIMEOUT in the device status word.
+#include <type_traits>
 #include "rowops.cuh"
 
 namespace screen {
@@ -337,29 +338,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float4* cc4 = reinterpret_cast<const float4*>(col + 2 * kBN + cb);
         const float4* sc4 = reinterpret_cast<const float4*>(col + 3 * kBN + cb);
         uint32_t pk[16];
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4) {
-          const float4 ikv = ik4[q4], ivv = iv4[q4], ccv = cc4[q4], scv = sc4[q4];
-#pragma unroll
-          for (int hp = 0; hp < 2; ++hp) {
-            const int c = 4 * q4 + 2 * hp;
-            const float2 ik2 = hp ? make_float2(ikv.z, ikv.w) : make_float2(ikv.x, ikv.y);
-            const float2 iv2 = hp ? make_float2(ivv.z, ivv.w) : make_float2(ivv.x, ivv.y);
-            const float2 cc2 = hp ? make_float2(ccv.z, ccv.w) : make_float2(ccv.x, ccv.y);
-            const float2 sc2 = hp ? make_float2(scv.z, scv.w) : make_float2(scv.x, scv.y);
-            const float2 x = __fmul2_rn(make_float2(__uint_as_float(sv[c]),
-                                                    __uint_as_float(sv[c + 1])), ik2);
-            const float2 t2 = __ffma2_rn(rq2, x, omr2);
-            const float2 a2 = make_float2((c >= iclo && c <= ichi) ? fmaxf(t2.x, 0.f) : 0.f,
-                                          (c + 1 >= iclo && c + 1 <= ichi) ? fmaxf(t2.y, 0.f) : 0.f);
-            const float2 m2 = __ffma2_rn(cr2, cc2, __ffma2_rn(sr2, sc2, half2));
-            const float2 dp2 = __fmul2_rn(make_float2(__uint_as_float(dv[c]),
-                                                      __uint_as_float(dv[c + 1])), iv2);
-            const float2 q2 = __fmul2_rn(__fmul2_rn(dp2, m2), a2);
-            const float2 ds = __fmul2_rn(q2, __fmul2_rn(ik2, twor2));
-            pk[2 * q4 + hp] = pack_bf16(ds.x, ds.y);
+        // interior tiles run without the window-edge selects
+        auto run = [&](auto edge) {
+          constexpr bool EDGE = decltype(edge)::value;
+  #pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 ikv = ik4[q4], ivv = iv4[q4], ccv = cc4[q4], scv = sc4[q4];
+  #pragma unroll
+            for (int hp = 0; hp < 2; ++hp) {
+              const int c = 4 * q4 + 2 * hp;
+              const float2 ik2 = hp ? make_float2(ikv.z, ikv.w) : make_float2(ikv.x, ikv.y);
+              const float2 iv2 = hp ? make_float2(ivv.z, ivv.w) : make_float2(ivv.x, ivv.y);
+              const float2 cc2 = hp ? make_float2(ccv.z, ccv.w) : make_float2(ccv.x, ccv.y);
+              const float2 sc2 = hp ? make_float2(scv.z, scv.w) : make_float2(scv.x, scv.y);
+              const float2 x = __fmul2_rn(make_float2(__uint_as_float(sv[c]),
+                                                      __uint_as_float(sv[c + 1])), ik2);
+              // relu(t) = saturate(t): t = 1 - r (1 - S) <= 1, so the clamp is free
+              float a0 = __saturatef(fmaf(rq, x.x, omr)), a1 = __saturatef(fmaf(rq, x.y, omr));
+              if (EDGE) {
+                a0 = (c >= iclo && c <= ichi) ? a0 : 0.f;
+                a1 = (c + 1 >= iclo && c + 1 <= ichi) ? a1 : 0.f;
+              }
+              const float2 a2 = make_float2(a0, a1);
+              const float2 m2 = __ffma2_rn(cr2, cc2, __ffma2_rn(sr2, sc2, half2));
+              const float2 dp2 = __fmul2_rn(make_float2(__uint_as_float(dv[c]),
+                                                        __uint_as_float(dv[c + 1])), iv2);
+              const float2 q2 = __fmul2_rn(__fmul2_rn(dp2, m2), a2);
+              const float2 ds = __fmul2_rn(q2, __fmul2_rn(ik2, twor2));
+              pk[2 * q4 + hp] = pack_bf16(ds.x, ds.y);
+            }
           }
-        }
+        };
+        if (inside)
+          run(std::false_type{});
+        else
+          run(std::true_type{});
         tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, pk);
         tmem_wait_st();
       }
@@ -662,35 +675,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float4* cv4 = reinterpret_cast<const float4*>(col + kBN + cb);
         const float4* sv4 = reinterpret_cast<const float4*>(col + 2 * kBN + cb);
         uint32_t pa[16], pd[16];
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4) {
-          const float4 iqv = iq4[q4], cvv = cv4[q4], svv = sv4[q4];
-#pragma unroll
-          for (int hp = 0; hp < 2; ++hp) {
-            const int c = 4 * q4 + 2 * hp;
-            const float2 iq2 = hp ? make_float2(iqv.z, iqv.w) : make_float2(iqv.x, iqv.y);
-            const float2 cv2 = hp ? make_float2(cvv.z, cvv.w) : make_float2(cvv.x, cvv.y);
-            const float2 sn2 = hp ? make_float2(svv.z, svv.w) : make_float2(svv.x, svv.y);
-            const float2 x = __fmul2_rn(make_float2(__uint_as_float(sv[c]),
-                                                    __uint_as_float(sv[c + 1])), iq2);
-            const float2 t2 = __ffma2_rn(rk2, x, omr2);
-            const float2 a2 = make_float2((c >= iclo && c <= ichi) ? fmaxf(t2.x, 0.f) : 0.f,
-                                          (c + 1 >= iclo && c + 1 <= ichi) ? fmaxf(t2.y, 0.f) : 0.f);
-            const float2 m2 = __ffma2_rn(cr2, cv2, __ffma2_rn(sr2, sn2, half2));
-            const float2 sinrel = __ffma2_rn(ncr2x2, sn2, __fmul2_rn(sr2x2, cv2));
-            const float2 dp2 = __fmul2_rn(make_float2(__uint_as_float(dv[c]),
-                                                      __uint_as_float(dv[c + 1])), iv2);
-            const float2 asq = __fmul2_rn(a2, a2);
-            const float2 al = __fmul2_rn(asq, m2);
-            const float2 q2 = __fmul2_rn(dp2, __fmul2_rn(a2, m2));  // dP m a
-            const float2 ds = __fmul2_rn(q2, __fmul2_rn(iq2, twor2));
-            pa[2 * q4 + hp] = pack_bf16(al.x, al.y);
-            pd[2 * q4 + hp] = pack_bf16(ds.x, ds.y);
-            accr2 = __ffma2_rn(q2, __ffma2_rn(x, ik2, m1), accr2);
-            const float2 rel = make_float2(relb - (float)c, relb - (float)(c + 1));
-            accw2 = __ffma2_rn(__fmul2_rn(dp2, asq), __fmul2_rn(rel, sinrel), accw2);
+        // interior tiles run without the window-edge selects
+        auto run = [&](auto edge) {
+          constexpr bool EDGE = decltype(edge)::value;
+  #pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 iqv = iq4[q4], cvv = cv4[q4], svv = sv4[q4];
+  #pragma unroll
+            for (int hp = 0; hp < 2; ++hp) {
+              const int c = 4 * q4 + 2 * hp;
+              const float2 iq2 = hp ? make_float2(iqv.z, iqv.w) : make_float2(iqv.x, iqv.y);
+              const float2 cv2 = hp ? make_float2(cvv.z, cvv.w) : make_float2(cvv.x, cvv.y);
+              const float2 sn2 = hp ? make_float2(svv.z, svv.w) : make_float2(svv.x, svv.y);
+              const float2 x = __fmul2_rn(make_float2(__uint_as_float(sv[c]),
+                                                      __uint_as_float(sv[c + 1])), iq2);
+              // relu(t) = saturate(t): t = 1 - r (1 - S) <= 1, so the clamp is free
+              float a0 = __saturatef(fmaf(rk, x.x, omr)), a1 = __saturatef(fmaf(rk, x.y, omr));
+              if (EDGE) {
+                a0 = (c >= iclo && c <= ichi) ? a0 : 0.f;
+                a1 = (c + 1 >= iclo && c + 1 <= ichi) ? a1 : 0.f;
+              }
+              const float2 a2 = make_float2(a0, a1);
+              const float2 m2 = __ffma2_rn(cr2, cv2, __ffma2_rn(sr2, sn2, half2));
+              const float2 sinrel = __ffma2_rn(ncr2x2, sn2, __fmul2_rn(sr2x2, cv2));
+              const float2 dp2 = __fmul2_rn(make_float2(__uint_as_float(dv[c]),
+                                                        __uint_as_float(dv[c + 1])), iv2);
+              const float2 asq = __fmul2_rn(a2, a2);
+              const float2 al = __fmul2_rn(asq, m2);
+              const float2 q2 = __fmul2_rn(dp2, __fmul2_rn(a2, m2));  // dP m a
+              const float2 ds = __fmul2_rn(q2, __fmul2_rn(iq2, twor2));
+              pa[2 * q4 + hp] = pack_bf16(al.x, al.y);
+              pd[2 * q4 + hp] = pack_bf16(ds.x, ds.y);
+              accr2 = __ffma2_rn(q2, __ffma2_rn(x, ik2, m1), accr2);
+              const float2 rel = make_float2(relb - (float)c, relb - (float)(c + 1));
+              accw2 = __ffma2_rn(__fmul2_rn(dp2, asq), __fmul2_rn(rel, sinrel), accw2);
+            }
           }
-        }
+        };
+        if (inside)
+          run(std::false_type{});
+        else
+          run(std::true_type{});
         tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, pa);
         tmem_st16(tmem + TM_P2 + 32 * bb + 16 * g + lane_off, pd);
         tmem_wait_st();
