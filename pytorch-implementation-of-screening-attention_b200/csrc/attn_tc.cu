@@ -242,6 +242,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     // alpha of columns (c, c+1) from the pair's S, 1/|k|, cos, sin
     auto pair_alpha = [&](float s0, float s1, float ik0, float ik1, float c0, float c1, float n0,
                           float n1, bool k0, bool k1) -> uint32_t {
+#ifdef SCREEN_SCALAR_EW
+      // relu(t) = saturate(t): t = 1 - r (1 - S) <= 1, so the clamp is free
+      float a0 = __saturatef(fmaf(rq, s0 * ik0, omr)), a1 = __saturatef(fmaf(rq, s1 * ik1, omr));
+      a0 = k0 ? a0 : 0.f;
+      a1 = k1 ? a1 : 0.f;
+      const float m0 = fmaf(crow, c0, fmaf(srow, n0, 0.5f));
+      const float m1 = fmaf(crow, c1, fmaf(srow, n1, 0.5f));
+      return pack_bf16(a0 * m0 * a0, a1 * m1 * a1);
+#else
       const float2 x = __fmul2_rn(make_float2(s0, s1), make_float2(ik0, ik1));
       // relu(t) = saturate(t): t = 1 - r (1 - S) <= 1, so the clamp is free
       const float a0 = __saturatef(fmaf(rq, x.x, omr)), a1 = __saturatef(fmaf(rq, x.y, omr));
@@ -250,6 +259,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           __ffma2_rn(cr2, make_float2(c0, c1), __ffma2_rn(sr2, make_float2(n0, n1), half2));
       const float2 al = __fmul2_rn(__fmul2_rn(a2, m2), a2);
       return pack_bf16(al.x, al.y);
+#endif
     };
     bool ok = true;
     unsigned long long live_tiles = 0;
