@@ -164,6 +164,79 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_decode(args, rank, world):
+    """Decode-kernel roofline: one new token per sequence, B=4 sequences per
+    GPU (cfg5: batch 32 over 8 GPUs), 16 heads x 64, bf16 paged cache with
+    `--decode-window` cached keys in every head's window (the cfg5 prompt is
+    100K tokens; at random init w <= 256, so the window is widened here to
+    make the kernel's HBM stream measurable).  Algorithmic bytes per launch =
+    keys in window x (K + V rows) + query + output."""
+    import importlib
+    ms = importlib.import_module(PKG)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, H, D, Wn = 4, HEADS, HEAD_DIM, args.decode_window
+    T = Wn + 1
+    cache = ms.PagedKVCache(1, B, H, D, max_len=T, max_window=float(T), dtype=torch.bfloat16,
+                            device=dev, page_size=64)
+    if args.decode_splits > 0:
+        cache.num_splits = args.decode_splits
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    for pg in (cache.k_pages[0], cache.v_pages[0]):
+        pg.copy_(torch.nn.functional.normalize(
+            torch.randn(pg.shape, device=dev, generator=g), dim=-1).to(torch.bfloat16))
+    q = torch.randn(B, H, D, device=dev, generator=g).to(torch.bfloat16)
+    # queries lean on random cached keys so alpha (and the V reads) are non-zero
+    seq = torch.full((B,), T, dtype=torch.int32, device=dev)
+    r = torch.full((H,), 1.02, device=dev)
+    w = torch.full((H,), float(T + 1), device=dev)
+    # inputs several times larger than L2 need no flush (and a 256 MiB write
+    # flush would leave L2 full of dirty lines the kernel then writes back)
+    window_bytes = B * H * T * D * 2 * 2
+    need_flush = window_bytes < 4 * 126 * 1024 * 1024
+    flush = torch.empty(256 * 1024 * 1024 // 4 if need_flush else 1, dtype=torch.float32,
+                        device=dev)
+    for _ in range(args.warmup):
+        cache.decode(0, q, seq, r, w)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    clk = ClockSampler(local)
+    clk.__enter__()
+    for a, b in evs:
+        if need_flush:
+            flush.zero_()
+        a.record()
+        cache.decode(0, q, seq, r, w)
+        b.record()
+    torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
+    ms_per = statistics.median(a.elapsed_time(b) for a, b in evs)
+    keys = B * H * T
+    alg_bytes = keys * D * 2 * 2 + 2 * B * H * D * 2
+    gbs = alg_bytes / (ms_per / 1e3) / 1e9
+    pk, kind = peaks()
+    peak = float(pk["hbm_gbs"])
+    if rank == 0:
+        print(json.dumps({
+            "metric": "screening decode attention, paged bf16 KV, HBM bandwidth",
+            "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"cfg5 decode kernel: B=4/GPU, H=16, D=64, {T} keys per "
+                                   f"(b,h) window, num_splits={cache.num_splits}",
+                       "l2": ("flushed (256 MiB write) between launches" if need_flush else
+                              f"inputs larger than L2 ({window_bytes / 2**30:.2f} GiB of K/V "
+                              "read per launch), no flush")},
+            "roofline": {"bound": "hbm", "kernel": "decode_split+finish", "achieved": gbs,
+                         "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind,
+                         "traffic": None},
+            "tokens_per_s_attention_only": B / (ms_per / 1e3),
+            "clocks": clk.summary(), "gpu_launches": 2 * args.steps,
+        }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -173,6 +246,12 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH, help="per-GPU batch (profiling: smaller)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-reps", type=int, default=5)
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "decode"],
+                    help="cfg3: the headline fwd+bwd step; decode: the paged-cache decode "
+                         "kernel's HBM roofline (cfg5 shapes, long window)")
+    ap.add_argument("--decode-window", type=int, default=100_000)
+    ap.add_argument("--decode-splits", type=int, default=0,
+                    help="override the cache's split count (0: its own heuristic)")
     ap.add_argument("--profile-only", action="store_true",
                     help="warm-up steps + one step, nothing else (for ncu captures)")
     args = ap.parse_args()
@@ -183,6 +262,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "decode":
+        run_decode(args, rank, world)
         return
 
     import importlib

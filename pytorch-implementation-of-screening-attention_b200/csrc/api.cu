@@ -176,7 +176,8 @@ size_t screen_fwd_workspace_size(const screen_fwd_args* a) {
 
 int screen_device_status(int clear) {
   const int a = tc_device_status(clear != 0), b = tc_bwd_device_status(clear != 0);
-  return a != 0 ? a : b;
+  const int c = decode_device_status(clear != 0);
+  return a != 0 ? a : (b != 0 ? b : c);
 }
 
 size_t screen_bwd_workspace_size(const screen_bwd_args* a) {

@@ -39,7 +39,14 @@ class PagedKVCache:
                  + (lb % self.pages_per_seq).unsqueeze(0))
         self.block_table = table.to(device)
         self._workspace = None
-        self.num_splits = max(1, min(32, math.ceil(self.keep / 256)))
+        # split each (b, h) window into runs of whole pages: at least one
+        # wave of CTAs (148 SMs x 3 resident decode CTAs), and about
+        # sqrt(pages) splits for long windows -- measured on B200 at 32K and
+        # 100K keys per window, fewer splits leave a wave tail, more pay the
+        # per-CTA pipeline fill; the split partials are summed
+        pages = math.ceil(self.keep / page_size)
+        fill = math.ceil(148 * 3 / max(1, batch * num_heads))
+        self.num_splits = max(1, min(256, pages, max(fill, round(1.1 * math.sqrt(pages)))))
 
     def nbytes(self) -> int:
         return sum(p.numel() * p.element_size() for p in self.k_pages + self.v_pages)

@@ -78,6 +78,37 @@ def test_decode_equals_forward_last_rows(ms, dtype, D):
         assert rel_err(y, y_full[:, t]) <= tol, t
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D,page_size,splits", [(64, 64, None), (64, 24, 5), (32, 16, 3),
+                                                (128, 64, 1), (16, 8, 7), (64, 64, 40)])
+def test_decode_long_prefix_page_sizes_and_splits(ms, dtype, D, page_size, splits):
+    """Decode of the newest token after a long prefix (the window wraps the
+    ring several times), for page sizes that are and are not multiples of 32
+    keys and for split counts that do not divide the window's pages."""
+    B, T, H = 2, 1500, 3
+    g = torch.Generator(device=DEV).manual_seed(1000 + D + page_size)
+    q = torch.randn(B, T, H, D, device=DEV, generator=g).to(dtype)
+    k = (q.float() + 0.5 * torch.randn(B, T, H, D, device=DEV, generator=g)).to(dtype)
+    v = torch.randn(B, T, H, D, device=DEV, generator=g).to(dtype)
+    r = torch.tensor([1.05, 1.3, 1.02], device=DEV)
+    w = torch.tensor([700.0, 90.5, 333.0], device=DEV)
+    y_full = ms.screening_attention(q, k, v, r, w, True)
+    cache = ms.PagedKVCache(1, B, H, D, max_len=T, max_window=700.0, dtype=dtype, device=DEV,
+                            page_size=page_size)
+    if splits is not None:
+        cache.num_splits = splits
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    step = 250
+    for t0 in range(0, T, step):
+        pos = torch.full((B,), t0, dtype=torch.int32, device=DEV)
+        cache.append(0, k[:, t0:t0 + step], v[:, t0:t0 + step], pos)
+        t = t0 + step - 1
+        y, _ = cache.decode(0, q[:, t], torch.full((B,), t + 1, dtype=torch.int32, device=DEV),
+                            r, w)
+        assert rel_err(y, y_full[:, t]) <= tol, t
+    assert ms._lib.device_status() == 0
+
+
 def test_bf16_lm_generate_matches_full_recompute(ms):
     """KV-cached generate == the reference's recompute-everything loop run on
     the same (bf16) model with the same kernels, token for token."""
