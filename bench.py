@@ -18,6 +18,7 @@ same workload (one sequence of T=4096 with all 16 heads per step).
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -237,6 +238,170 @@ def run_decode(args, rank, world):
         }), flush=True)
 
 
+PREFILL = dict(vocab=50257, d_model=1024, heads=16, layers=12, window=2048.0)
+
+
+def prefill_flops(T: int, n_layers: int, d_model: int, H: int, D: int, window: float,
+                  ffn: int) -> dict:
+    """Forward FLOPs of a prefill over T tokens: the windowed attention pairs
+    (2 GEMMs of 2*D flops per (i, j) pair) and the dense GEMMs of every block
+    (QKV 3d^2, out d^2, FFN 2*d*ffn; 2 flops/MAC) plus the last position's
+    lm_head."""
+    n = max(0, math.ceil(window) - 1) + 1
+    pairs = (T * (T + 1) // 2) if n >= T else (n * (n + 1) // 2 + (T - n) * n)
+    attn = n_layers * H * pairs * 2 * (2 * D)
+    gemm = n_layers * T * 2 * (4 * d_model * d_model + 2 * d_model * ffn)
+    return {"attention": float(attn), "gemm": float(gemm), "total": float(attn + gemm)}
+
+
+def cpu_prefill_sample(T_sample: int = 4096):
+    """One oracle MultiscreenBlock (windowed restatement, fp32, all host
+    threads) over T_sample tokens, no_grad; returns (seconds, threads).  The
+    whole prefill is this x layers x (T / T_sample): the windowed attention
+    and the GEMMs are both linear in T at a fixed window."""
+    from oracle import screening_oracle as oracle
+    nt = os.cpu_count() or 1
+    torch.set_num_threads(nt)
+    torch.manual_seed(0)
+    d, H = PREFILL["d_model"], PREFILL["heads"]
+    blk = oracle.OracleBlock(d, H, windowed=True)
+    with torch.no_grad():
+        blk.attn.s_v.fill_(math.log(PREFILL["window"] - 1.0))
+        for mod in blk.modules():
+            if isinstance(mod, torch.nn.Linear):
+                torch.nn.init.normal_(mod.weight, std=0.02)
+    x = torch.randn(1, T_sample, d, generator=torch.Generator().manual_seed(1)) * 0.02
+    with torch.no_grad():
+        blk(x)
+        t0 = time.perf_counter()
+        blk(x)
+        dt = time.perf_counter() - t0
+    return dt, nt
+
+
+def run_prefill(args, rank, world):
+    """cfg4: long-context prefill of MultiscreenLM(50257, 1024, 16, 12) over
+    T = --prefill-len tokens (batch 1, bf16, w = 2048 in every head, random
+    init), sequence-sharded over the ranks (T / world tokens each, K/V halo of
+    2047 rows per layer by NCCL P2P).  A step is the forward of every block
+    and the last position's logits (MultiscreenLM.prefill without a cache).
+    Strong scaling: T is fixed as the rank count grows."""
+    import importlib
+    ms = importlib.import_module(PKG)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    T = args.prefill_len
+    if T % world:
+        raise SystemExit(f"--prefill-len {T} is not divisible by {world} ranks")
+    Lb = T // world
+    cfg = PREFILL
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dt, nt = cpu_prefill_sample()
+        per_tok = dt / 4096 * cfg["layers"]
+        cpu = {"value": 1.0 / per_tok, "unit": "tokens/s", "cores": nt, "kind": "port",
+               "sample": f"one oracle MultiscreenBlock (windowed, fp32, no_grad) over 4096 "
+                         f"tokens in {dt:.2f} s, x {cfg['layers']} layers, linear in T"}
+    torch.manual_seed(0)
+    model = ms.MultiscreenLM(cfg["vocab"], d_model=cfg["d_model"], num_heads=cfg["heads"],
+                             num_layers=cfg["layers"], max_seq_len=T)
+    with torch.no_grad():
+        for blk in model.blocks:
+            blk.attn.s_v.fill_(math.log(cfg["window"] - 1.0))
+    model = model.to(dev).to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(1234)
+    ids_host = torch.randint(0, cfg["vocab"], (1, T), generator=g)
+    ids_local_host = ids_host[:, rank * Lb:(rank + 1) * Lb].contiguous().pin_memory()
+    ids = ids_local_host.to(dev)
+    ctx = (lambda: ms.sequence_parallel(Lb)) if dist is not None else contextlib.nullcontext
+
+    def step(inp):
+        with torch.no_grad(), ctx():
+            return model.prefill(inp, None)
+
+    for _ in range(args.warmup):
+        step(ids)
+    torch.cuda.synchronize()
+    if args.profile_only:
+        step(ids)
+        torch.cuda.synchronize()
+        return
+    clk = ClockSampler(local)
+    clk.__enter__()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for a, b in evs:
+        a.record()
+        step(ids)
+        b.record()
+    torch.cuda.synchronize()
+    total_ms = sum(a.elapsed_time(b) for a, b in evs)
+    # end to end: ids from pinned host memory, last logits back to the host
+    logit_host = torch.empty(1, cfg["vocab"], dtype=torch.bfloat16).pin_memory()
+    ids_dev = torch.empty_like(ids)
+    e2e = []
+    for i in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ids_dev.copy_(ids_local_host, non_blocking=True)
+        lg = step(ids_dev)
+        logit_host.copy_(lg, non_blocking=True)
+        b.record()
+        e2e.append((a, b))
+    torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e)
+    if dist is not None:
+        t = torch.tensor([total_ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = (float(x) for x in t.tolist())
+    ms_per = total_ms / args.steps
+    e2e_per = e2e_ms / args.steps
+    ffn = 4 * cfg["d_model"]
+    fl = prefill_flops(T, cfg["layers"], cfg["d_model"], cfg["heads"], HEAD_DIM, cfg["window"],
+                       ffn)
+    pk, kind = peaks()
+    peak = float(pk.get("bf16_tflops_sustained", pk["bf16_tflops"]))
+    tf = fl["total"] / (ms_per / 1e3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            "metric": "long-context prefill tokens/s (MultiscreenLM 1024x16x12, T=131072, w=2048)",
+            "value": T / (ms_per / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"cfg4 prefill: MultiscreenLM(50257, 1024, 16, 12), batch 1, "
+                                   f"T={T}, w=2048, random init, no_grad, last-position logits",
+                       "seq_len": T, "global_batch": 1,
+                       "parallelism": f"sequence-sharded x{world}, K/V halo 2047 rows/layer "
+                                      f"by NCCL P2P",
+                       "l2": f"inputs larger than L2 (activations of {Lb} tokens x 1024 bf16 "
+                             f"per layer plus 12 layers of weights)"},
+            "roofline": {"bound": "tensor", "kernel": "whole prefill step (attention + GEMMs)",
+                         "achieved": tf / world, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tf / world / peak, "peak_kind": kind + " sustained",
+                         "traffic": None, "per": "GPU (achieved = job FLOP/s / ranks)",
+                         "flops_basis": "windowed attention pairs + dense block GEMMs"},
+            "flops_per_step": fl,
+            "cpu_baseline": cpu,
+            "e2e": {"value": T / (e2e_per / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": ids_local_host.numel() * 8,
+                    "d2h_bytes_per_step": cfg["vocab"] * 2},
+            "clocks": clk.summary(),
+            "gpu_launches": 6 * cfg["layers"] * args.steps,
+        }), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -246,10 +411,11 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH, help="per-GPU batch (profiling: smaller)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-reps", type=int, default=5)
-    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "decode"],
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "decode", "prefill"],
                     help="cfg3: the headline fwd+bwd step; decode: the paged-cache decode "
                          "kernel's HBM roofline (cfg5 shapes, long window)")
     ap.add_argument("--decode-window", type=int, default=100_000)
+    ap.add_argument("--prefill-len", type=int, default=131072)
     ap.add_argument("--decode-splits", type=int, default=0,
                     help="override the cache's split count (0: its own heuristic)")
     ap.add_argument("--profile-only", action="store_true",
@@ -265,6 +431,9 @@ def main():
         return
     if args.workload == "decode":
         run_decode(args, rank, world)
+        return
+    if args.workload == "prefill":
+        run_prefill(args, rank, world)
         return
 
     import importlib

@@ -19,6 +19,8 @@ from .kv_cache import PagedKVCache
 from .layers import MultiscreenBlock, MultiscreenDecoderLayer
 from .model import MultiscreenLM
 from .norm import TanhNorm
+from .sequence_parallel import (SequenceShard, current_shard, screening_attention_sharded,
+                                sequence_parallel)
 from . import _lib
 
 _sys.modules.setdefault("screening_b200", _sys.modules[__name__])
@@ -33,6 +35,9 @@ __all__ = [
     "screening_attention",
     "tanh_norm",
     "PagedKVCache",
+    "sequence_parallel",
+    "screening_attention_sharded",
+    "SequenceShard",
 ]
 
 __version__ = "0.1.0"

@@ -19,6 +19,7 @@ import torch.nn.functional as F
 from . import _lib
 from .functional import screening_attention, screening_attention_packed
 from .norm import TanhNorm
+from .sequence_parallel import current_shard, screening_attention_sharded
 
 
 class ScreeningAttention(nn.Module):
@@ -82,7 +83,15 @@ class ScreeningAttention(nn.Module):
         key_padding_mask (B,T_k) bool, True = ignore.  Returns (B,T_q,d_model)."""
         self._check_dropout()
         B, Tq, _ = query.shape
-        if query is key and key is value:
+        shard = current_shard() if self.causal else None
+        if shard is not None and query is key and key is value:
+            # causal self-attention of one block of a sequence-sharded input:
+            # the K/V halo before the block comes from the previous ranks
+            q, k, v = self._qkv(query, key, value)
+            y = screening_attention_sharded(q, k, v, self.sharpness(), self.window(),
+                                            key_padding_mask=key_padding_mask, eps=self.eps,
+                                            shard=shard)
+        elif query is key and key is value:
             # self-attention: one GEMM for the three projections; the kernels
             # read q, k, v in place and write their gradients into one buffer
             H, D = self.num_heads, self.head_dim
@@ -103,15 +112,25 @@ class ScreeningAttention(nn.Module):
     @torch.no_grad()
     def prefill(self, x: torch.Tensor, cache, layer: int) -> torch.Tensor:
         """Causal self-attention over a whole prompt x (B,T,d) that also
-        writes the prompt's last `cache.keep` unit keys/values into `cache`."""
+        writes the prompt's last `cache.keep` unit keys/values into `cache`
+        (cache None: attention only).  Inside sequence_parallel(), x is this
+        rank's block of a sharded prompt."""
         B, T, _ = x.shape
         q, k, v = self._qkv(x, x, x)
-        keep = min(T, cache.keep)
-        if keep > 0:
-            pos = torch.full((B,), T - keep, dtype=torch.int32, device=x.device)
-            cache.append(layer, k[:, T - keep:], v[:, T - keep:], pos, eps=self.eps)
-        y = screening_attention(q, k, v, self.sharpness(), self.window(), causal=True,
-                                eps=self.eps)
+        shard = current_shard()
+        if cache is not None:
+            if shard is not None and shard.world > 1:
+                raise NotImplementedError("a KV cache fill from a sequence-sharded prefill")
+            keep = min(T, cache.keep)
+            if keep > 0:
+                pos = torch.full((B,), T - keep, dtype=torch.int32, device=x.device)
+                cache.append(layer, k[:, T - keep:], v[:, T - keep:], pos, eps=self.eps)
+        if shard is not None:
+            y = screening_attention_sharded(q, k, v, self.sharpness(), self.window(),
+                                            eps=self.eps, shard=shard)
+        else:
+            y = screening_attention(q, k, v, self.sharpness(), self.window(), causal=True,
+                                    eps=self.eps)
         return self.out_proj(y.reshape(B, T, self.d_model))
 
     @torch.no_grad()

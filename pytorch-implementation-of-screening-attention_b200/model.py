@@ -14,6 +14,22 @@ import torch.nn.functional as F
 
 from .kv_cache import PagedKVCache
 from .layers import MultiscreenBlock
+from .sequence_parallel import current_shard
+
+
+def _sharded_mean_ce(logits, labels, shard):
+    """Mean cross-entropy over the tokens of all ranks (model.py:103-107 on the
+    whole sequence).  Its value is the global mean on every rank; its gradient
+    is this rank's tokens' share only, so summing the parameter gradients over
+    the ranks (as data parallelism does) gives the full gradient."""
+    import torch.distributed as dist
+    lg = logits.reshape(-1, logits.size(-1))
+    if lg.dtype in (torch.float16, torch.bfloat16):
+        lg = lg.float()
+    s = F.cross_entropy(lg, labels.reshape(-1), ignore_index=-100, reduction="sum")
+    tot = torch.stack([s.detach(), (labels != -100).sum().to(s.dtype)])
+    dist.all_reduce(tot, group=shard.group)
+    return (s + (tot[0] - s.detach())) / tot[1]
 
 
 class MultiscreenLM(nn.Module):
@@ -47,7 +63,9 @@ class MultiscreenLM(nn.Module):
     def forward(self, input_ids: torch.Tensor, key_padding_mask: torch.Tensor | None = None,
                 labels: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
         B, T = input_ids.shape
-        positions = torch.arange(T, device=input_ids.device).unsqueeze(0)
+        shard = current_shard()
+        off = shard.start if shard is not None else 0
+        positions = torch.arange(off, off + T, device=input_ids.device).unsqueeze(0)
         x = self.emb_dropout(self.token_emb(input_ids) + self.pos_emb(positions))
         for block in self.blocks:
             x = block(x, key_padding_mask=key_padding_mask)
@@ -55,8 +73,11 @@ class MultiscreenLM(nn.Module):
         logits = self.lm_head(x)
         result = {"logits": logits}
         if labels is not None:
-            result["loss"] = F.cross_entropy(logits.view(-1, logits.size(-1)), labels.view(-1),
-                                             ignore_index=-100)
+            if shard is None or shard.world == 1:
+                result["loss"] = F.cross_entropy(logits.view(-1, logits.size(-1)),
+                                                 labels.view(-1), ignore_index=-100)
+            else:
+                result["loss"] = _sharded_mean_ce(logits, labels, shard)
         return result
 
     # ------------------------------------------------------------------
@@ -74,10 +95,15 @@ class MultiscreenLM(nn.Module):
                             self._max_window(), dt, self.token_emb.weight.device, page_size)
 
     @torch.no_grad()
-    def prefill(self, input_ids: torch.Tensor, cache: PagedKVCache) -> torch.Tensor:
-        """Run the prompt once, fill `cache`, return last-position logits (B,V)."""
+    def prefill(self, input_ids: torch.Tensor, cache: PagedKVCache | None) -> torch.Tensor:
+        """Run the prompt once, fill `cache` (if given), return the logits of
+        the last position (B,V).  Inside sequence_parallel(), input_ids is this
+        rank's block of the prompt and the logits are those of the block's last
+        position (the prompt's last on the last rank)."""
         B, T = input_ids.shape
-        positions = torch.arange(T, device=input_ids.device).unsqueeze(0)
+        shard = current_shard()
+        off = shard.start if shard is not None else 0
+        positions = torch.arange(off, off + T, device=input_ids.device).unsqueeze(0)
         x = self.emb_dropout(self.token_emb(input_ids) + self.pos_emb(positions))
         for li, blk in enumerate(self.blocks):
             x = x + blk.attn.prefill(blk.norm1(x), cache, li)
