@@ -158,7 +158,7 @@ int screen_fwd(const screen_fwd_args* a, screen_stream_t stream) {
     const size_t need = tc_fwd_workspace(sh);
     if (need > 0 && (!a->workspace || a->workspace_bytes < need || !al16(a->workspace)))
       return SCREEN_ERR_WORKSPACE;
-    tc_fwd(sh, p, a->workspace, a->norms_given || !(stages & 1), s);
+    if ((st = tc_fwd(sh, p, a->workspace, a->norms_given || !(stages & 1), s))) return st;
   } else if (use_mma(a->dtype, a->D))
     mma_fwd(a->D, sh, p, s);
   else

@@ -37,7 +37,17 @@ namespace {
 using namespace sm100;
 typedef __nv_bfloat16 bf16;
 
-constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 3, kThreads = 192;
+// kCG compute warpgroups split each key tile's 64 columns (32 / kCG each)
+#ifndef SCREEN_FWD_CG
+#define SCREEN_FWD_CG 2
+#endif
+constexpr int kCG = SCREEN_FWD_CG;
+constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 4;
+constexpr int kCW = 4 * kCG;                 // compute warps
+constexpr int kNC = kBN / kCG;               // columns per compute thread per tile
+constexpr int kCT = 32 * kCW;                // compute threads
+constexpr int kProdWarp = kCW, kMmaWarp = kCW + 1;
+constexpr int kThreads = 32 * (kCW + 2);
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
 
 // shared-memory layout (offsets from a 1024-byte aligned base)
@@ -52,7 +62,8 @@ constexpr int BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = BAR_KV_FULL + kNS,
               BAR_S_FULL = BAR_KV_EMPTY + kNS, BAR_S_FREE = BAR_S_FULL + 2,
               BAR_P_FULL = BAR_S_FREE + 2, BAR_O_FULL = BAR_P_FULL + 2;
 constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 16;
-constexpr uint32_t SMEM_USED = OFF_MISC + 64;
+constexpr uint32_t OFF_RED = OFF_MISC + 64;                // [kCG][kBM] epilogue sums
+constexpr uint32_t SMEM_USED = OFF_RED + kCG * kBM * 4;
 // at least 80 KB per CTA: at most two CTAs (2 x 256 TMEM columns) per SM
 constexpr uint32_t kSmemBytes = (SMEM_USED + 1024 > 80 * 1024) ? SMEM_USED + 1024 : 80 * 1024;
 
@@ -60,9 +71,22 @@ constexpr uint32_t TM_S = 0, TM_P = 128, TM_O = 192, TM_COLS = 256;
 
 __device__ int g_device_status = 0;
 
+// Wait-time instrumentation of the forward (variant builds with
+// -DSCREEN_FWD_PROFILE only): clock cycles each role spends in its waits.
+#ifdef SCREEN_FWD_PROFILE
+__device__ unsigned long long g_fwd_prof[16];
+#define PROF_T0() const long long _pt0 = clock64()
+#define PROF_ADD(slot) atomicAdd(&g_fwd_prof[slot], (unsigned long long)(clock64() - _pt0))
+#else
+#define PROF_T0() do {} while (0)
+#define PROF_ADD(slot) do {} while (0)
+#endif
+
 __global__ void __launch_bounds__(kThreads, 2)
-    tc_fwd_kernel(AttnShape s, FwdPtrs p, const bf16* __restrict__ vhat,
-                  const float* __restrict__ ikT, const float4* __restrict__ ikmeta, int Tkp) {
+    tc_fwd_kernel(AttnShape s, FwdPtrs p, const float* __restrict__ ikT,
+                  const float4* __restrict__ ikmeta, int Tkp,
+                  const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -92,15 +116,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int n = any ? (int)(hi / kBN) - kt0 + 1 : 0;
 
   if (tid == 0) {
-    mbar_init(bar(BAR_Q), 32);
+    mbar_init(bar(BAR_Q), 1);
     for (int i = 0; i < kNS; ++i) {
-      mbar_init(bar(BAR_KV_FULL + i), 33);
+      // one arrival with the TMA byte count, one after the column factors
+      mbar_init(bar(BAR_KV_FULL + i), 2);
       mbar_init(bar(BAR_KV_EMPTY + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(BAR_S_FULL + i), 1);
-      mbar_init(bar(BAR_S_FREE + i), 128);
-      mbar_init(bar(BAR_P_FULL + i), 128);
+      mbar_init(bar(BAR_S_FREE + i), kCT);
+      mbar_init(bar(BAR_P_FULL + i), kCT);
     }
     mbar_init(bar(BAR_O_FULL), 2);
     misc[1] = misc[2] = misc[3] = 0;
@@ -113,19 +138,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = misc[0];
 
-  if (warp == 4) {
+  if (warp == kProdWarp) {
     // ------------------------------------------------------------ producer
-    const bf16* qh = reinterpret_cast<const bf16*>(p.q.p) + (long long)b * p.q.sb + (long long)h * kD;
-    const bf16* kh = reinterpret_cast<const bf16*>(p.k.p) + (long long)b * p.k.sb + (long long)h * kD;
-    const bf16* vh = vhat + ((long long)b * s.Tk * s.H + h) * kD;
-    const long long vst = (long long)s.H * kD;
-    for (int c = lane; c < kBM * 8; c += 32) {
-      const int row = c >> 3, ch = c & 7;
-      const long long t = i0 + row;
-      const bool ok = t < s.Tq;
-      cp_async16(sQ + tile_off<kD>(row, ch), qh + (ok ? t * p.q.st : 0) + ch * 8, ok);
+    // lane 0 issues the TMA copies (Q once; per 64-key tile K, V^ and the
+    // 1/|k| run with its (min, max)); the warp computes the column (cos, sin)
+    // of the tile from one sincospif and a rotation of the per-CTA table
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar(BAR_Q), kBM * kD * 2);
+      tma_load_4d(sQ, &tmQ, 0, h, (int)i0, b, bar(BAR_Q));
     }
-    mbar_arrive_cp_async(bar(BAR_Q));
     // (cos, sin)(pi c / w) for the 64 column offsets of a tile
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -145,24 +166,26 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (j >= kNS) {
         // lane 0 waits, the whole warp follows its verdict (no divergent exit)
         int okw = 1;
-        if (lane == 0)
+        if (lane == 0) {
+          PROF_T0();
           okw = mbar_wait(bar(BAR_KV_EMPTY + st), ((j / kNS) - 1) & 1, abort_flag, kWaitLimitNs);
+          PROF_ADD(0);
+        }
         if (!__shfl_sync(0xffffffffu, okw, 0)) break;
       }
       const int kt = kt0 + j;
       const long long j0 = (long long)kt * kBN;
       const uint32_t kb = sK + st * kBN * kD * 2, vb = sV + st * kBN * kD * 2;
-      for (int c = lane; c < kBN * 8; c += 32) {
-        const int row = c >> 3, ch = c & 7;
-        const long long t = j0 + row;
-        const bool ok = t < s.Tk;
-        cp_async16(kb + tile_off<kD>(row, ch), kh + (ok ? t * p.k.st : 0) + ch * 8, ok);
-        cp_async16(vb + tile_off<kD>(row, ch), vh + (ok ? t * vst : 0) + ch * 8, ok);
-      }
       const uint32_t colb = base + OFF_COL + st * COL_BYTES;
       float* col = colp + st * (COL_BYTES / 4);
-      if (lane < 16) cp_async16(colb + lane * 16, ikh + j0 + lane * 4, true);
-      else if (lane == 16) cp_async16(colb + 3 * kBN * 4, mh + kt, true);
+      if (lane == 0) {
+        const uint32_t fb = bar(BAR_KV_FULL + st);
+        mbar_arrive_expect_tx(fb, 2 * kBN * kD * 2 + kBN * 4 + 16);
+        tma_load_4d(kb, &tmK, 0, h, (int)j0, b, fb);
+        tma_load_4d(vb, &tmV, 0, h, (int)j0, b, fb);
+        bulk_g2s(colb, ikh + j0, kBN * 4, fb);
+        bulk_g2s(colb + 3 * kBN * 4, mh + kt, 16, fb);
+      }
       // column angle pi (j0 + c - p0) / w = base + pi c / w, by rotation
       float sb = 0.f, cb = 0.f;
       if (lane == 0) sincospif((float)(j0 - p0) / w, &sb, &cb);
@@ -172,12 +195,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       col[2 * kBN + lane] = sb * cphi0 + cb * sphi0;
       col[kBN + lane + 32] = cb * cphi1 - sb * sphi1;
       col[2 * kBN + lane + 32] = sb * cphi1 + cb * sphi1;
-      mbar_arrive_cp_async(bar(BAR_KV_FULL + st));
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_KV_FULL + st));
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp == 5) {
+    if (lane == 0 && *abort_flag) {
+      // let the copies already issued land before the CTA's smem goes away
+      const uint64_t t0 = globaltimer();
+      for (int j = n > kNS ? n - kNS : 0; j < n; ++j)
+        while (!mbar_try_wait(bar(BAR_KV_FULL + j % kNS), (j / kNS) & 1) &&
+               globaltimer() - t0 < kWaitLimitNs) {
+        }
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(kBM, kBN, 0, 0);
@@ -185,7 +215,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       bool o_started = false, ok = mbar_wait(bar(BAR_Q), 0, abort_flag, kWaitLimitNs);
       auto issue_pv = [&](int jj) -> bool {
         const int bb = jj & 1, st = jj % kNS;
-        if (!mbar_wait(bar(BAR_P_FULL + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
+        {
+          PROF_T0();
+          const bool okp = mbar_wait(bar(BAR_P_FULL + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs);
+          PROF_ADD(3);
+          if (!okp) return false;
+        }
         tc_fence_after();
         if (!misc[1 + bb]) {
           const uint32_t vb = sV + st * kBN * kD * 2;
@@ -201,9 +236,16 @@ __global__ void __launch_bounds__(kThreads, 2)
       };
       for (int j = 0; j < n && ok; ++j) {
         const int st = j % kNS, bb = j & 1;
-        ok = mbar_wait(bar(BAR_KV_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
-        if (ok && j >= 2)
+        {
+          PROF_T0();
+          ok = mbar_wait(bar(BAR_KV_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
+          PROF_ADD(1);
+        }
+        if (ok && j >= 2) {
+          PROF_T0();
           ok = mbar_wait(bar(BAR_S_FREE + bb), ((j >> 1) - 1) & 1, abort_flag, kWaitLimitNs);
+          PROF_ADD(2);
+        }
         if (!ok) break;
         tc_fence_after();
         fence_proxy_async_smem();
@@ -223,8 +265,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ compute
-    const int t = tid;  // 0..127 = query row in tile = TMEM lane
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int t = tid & (kBM - 1);  // query row in tile = TMEM lane
+    const int g = tid / kBM;        // column group: columns [g * kNC, (g + 1) * kNC)
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const long long i = i0 + t;
     const float rq = (i < s.Tq) ? r / p.nq[((long long)b * s.Tq + i) * s.H + h] : 0.f;
     float crow, srow;
@@ -265,50 +308,57 @@ __global__ void __launch_bounds__(kThreads, 2)
     unsigned long long live_tiles = 0;
     for (int j = 0; j < n; ++j) {
       const int st = j % kNS, bb = j & 1;
-      ok = mbar_wait(bar(BAR_KV_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
-           mbar_wait(bar(BAR_S_FULL + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
+#ifdef SCREEN_FWD_PROFILE
+      const long long _tc0 = clock64();
+#endif
+      {
+        PROF_T0();
+        ok = mbar_wait(bar(BAR_KV_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
+             mbar_wait(bar(BAR_S_FULL + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
+        if (tid == 0) PROF_ADD(4);
+      }
       // all 128 threads take the same branch before the next named barrier
-      if (bar_red_or(1, 128, !ok)) {
+      if (bar_red_or(1, kCT, !ok)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sv[64];
-      {
-        uint32_t (&a0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
-        uint32_t (&a1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
-        tmem_ld32(tmem + TM_S + kBN * bb + lane_off, a0);
-        tmem_ld32(tmem + TM_S + kBN * bb + 32 + lane_off, a1);
-      }
+      static_assert(kNC == 32 || kNC == 64, "column split");
+      uint32_t sv[kNC];
+#pragma unroll
+      for (int h32 = 0; h32 < kNC / 32; ++h32)
+        tmem_ld32(tmem + TM_S + kBN * bb + kNC * g + 32 * h32 + lane_off,
+                  *reinterpret_cast<uint32_t(*)[32]>(&sv[32 * h32]));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar(BAR_S_FREE + bb));
 
-      const float* col = colp + st * (COL_BYTES / 4);
+      const float* colt = colp + st * (COL_BYTES / 4);   // whole-tile columns
+      const float* col = colt + kNC * g;                  // this group's columns
       // trim pre-test.  For r >= 1 the threshold (r-1)/r on S is >= 0, so
       // only positive scores can be live; positive floats order like their
       // int bit patterns and negative ones are negative ints, so an integer
       // max over the raw bits finds the largest score when it is positive.
       int imax = (int)sv[0];
 #pragma unroll
-      for (int c = 1; c + 1 < 64; c += 2) imax = __vimax3_s32(imax, (int)sv[c], (int)sv[c + 1]);
-      imax = max(imax, (int)sv[63]);
+      for (int c = 1; c + 1 < kNC; c += 2) imax = __vimax3_s32(imax, (int)sv[c], (int)sv[c + 1]);
+      imax = max(imax, (int)sv[kNC - 1]);
       const float smax = __int_as_float(imax);
-      const float ikmax = col[3 * kBN + 1];
+      const float ikmax = colt[3 * kBN + 1];
       const bool mine = r < 1.0f || (imax > 0 && fmaf(rq, smax * ikmax, omr) > 0.f);
-      const bool live = bar_red_or(1, 128, mine);
+      const bool live = bar_red_or(1, kCT, mine);
       if (live) {
         const long long j0 = (long long)(kt0 + j) * kBN;
         const bool inside = (causal ? (p0 - (j0 + kBN - 1) >= 0 && p0 + kBM - 1 - j0 <= dmax)
                                     : (p0 - (j0 + kBN - 1) >= -(long long)dmax &&
                                        p0 + kBM - 1 - j0 <= dmax));
-        uint32_t pk[32];
+        uint32_t pk[kNC / 2];
         const float4* ik4 = reinterpret_cast<const float4*>(col);
         const float4* cc4 = reinterpret_cast<const float4*>(col + kBN);
         const float4* sc4 = reinterpret_cast<const float4*>(col + 2 * kBN);
         if (inside) {
 #pragma unroll
-          for (int q4 = 0; q4 < 16; ++q4) {
+          for (int q4 = 0; q4 < kNC / 4; ++q4) {
             const float4 ikv = ik4[q4], ccv = cc4[q4], scv = sc4[q4];
             const int c = 4 * q4;
             pk[2 * q4] = pair_alpha(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), ikv.x,
@@ -318,11 +368,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         } else {
           // window edge: this row's valid columns are the interval [clo, chi]
-          const long long clo = pos - dmax - j0, chi = causal ? pos - j0 : pos + dmax - j0;
-          const int iclo = (int)(clo < 0 ? 0 : (clo > 64 ? 64 : clo));
-          const int ichi = (int)(chi < -1 ? -1 : (chi > 63 ? 63 : chi));
+          const long long jg = j0 + kNC * g;   // first key of this group's columns
+          const long long clo = pos - dmax - jg, chi = causal ? pos - jg : pos + dmax - jg;
+          const int iclo = (int)(clo < 0 ? 0 : (clo > kNC ? kNC : clo));
+          const int ichi = (int)(chi < -1 ? -1 : (chi > kNC - 1 ? kNC - 1 : chi));
 #pragma unroll
-          for (int q4 = 0; q4 < 16; ++q4) {
+          for (int q4 = 0; q4 < kNC / 4; ++q4) {
             const float4 ikv = ik4[q4], ccv = cc4[q4], scv = sc4[q4];
             const int c = 4 * q4;
             pk[2 * q4] = pair_alpha(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), ikv.x,
@@ -334,59 +385,80 @@ __global__ void __launch_bounds__(kThreads, 2)
                                         c + 3 >= iclo && c + 3 <= ichi);
           }
         }
-        tmem_st32(tmem + TM_P + 32 * bb + lane_off, pk);
+        if constexpr (kNC == 64) {
+          tmem_st32(tmem + TM_P + 32 * bb + lane_off, *reinterpret_cast<uint32_t(*)[32]>(pk));
+        } else {
+          tmem_st16(tmem + TM_P + 32 * bb + (kNC / 2) * g + lane_off, pk);
+        }
         tmem_wait_st();
       }
-      if (t == 0) {
+      if (tid == 0) {
         misc[1 + bb] = live ? 0u : 1u;
         live_tiles += live ? 1 : 0;
       }
       tc_fence_before();
       mbar_arrive(bar(BAR_P_FULL + bb));
+#ifdef SCREEN_FWD_PROFILE
+      if (tid == 0) atomicAdd(&g_fwd_prof[5], (unsigned long long)(clock64() - _tc0));
+      if (tid == 0) atomicAdd(&g_fwd_prof[7], 1ull);
+#endif
     }
-    if (p.tile_stats && t == 0) {
+    if (p.tile_stats && tid == 0) {
       // reported in 16x64 score blocks, the unit of the warp-level kernels
       atomicAdd((unsigned long long*)&p.tile_stats[0], 8ull * (unsigned long long)n);
       atomicAdd((unsigned long long*)&p.tile_stats[1], 8ull * live_tiles);
     }
     // epilogue: O -> TanhNorm -> y
-    ok = ok && mbar_wait(bar(BAR_O_FULL), 0, abort_flag, kWaitLimitNs);
+    {
+      PROF_T0();
+      ok = ok && mbar_wait(bar(BAR_O_FULL), 0, abort_flag, kWaitLimitNs);
+      if (tid == 0) PROF_ADD(6);
+    }
     // tcgen05.ld below is warp-collective: every lane takes the same branch
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
+    // each column group loads and stores its kD / kCG output columns; the
+    // row's |o|^2 is summed over the groups through shared memory
+    constexpr int kOC = kD / kCG;
+    float o[kOC];
+    if (ok && misc[3]) {
+      uint32_t ov[kOC];
+#pragma unroll
+      for (int h32 = 0; h32 < kOC / 32; ++h32)
+        tmem_ld32(tmem + TM_O + kOC * g + 32 * h32 + lane_off,
+                  *reinterpret_cast<uint32_t(*)[32]>(&ov[32 * h32]));
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < kOC; ++c) o[c] = __uint_as_float(ov[c]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < kOC; ++c) o[c] = 0.f;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kOC; ++c) ss = fmaf(o[c], o[c], ss);
+    float* red = reinterpret_cast<float*>(gbase + OFF_RED);
+    red[g * kBM + t] = ss;
+    asm volatile("bar.sync 2, %0;" ::"r"(kCT) : "memory");
     if (ok) {
-      float o[64];
-      if (misc[3]) {
-        uint32_t ov[64];
-        uint32_t (&a0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&ov[0]);
-        uint32_t (&a1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&ov[32]);
-        tmem_ld32(tmem + TM_O + lane_off, a0);
-        tmem_ld32(tmem + TM_O + 32 + lane_off, a1);
-        tmem_wait_ld();
+      float tot = 0.f;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) o[c] = __uint_as_float(ov[c]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) o[c] = 0.f;
-      }
-      float ss = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) ss = fmaf(o[c], o[c], ss);
-      const float nraw = sqrtf(ss);
-      const float g = tanhnorm_scale(nraw, s.eps);
+      for (int gg = 0; gg < kCG; ++gg) tot += red[gg * kBM + t];
+      const float nraw = sqrtf(tot);
+      const float gsc = tanhnorm_scale(nraw, s.eps);
       if (i < s.Tq) {
         const long long row = ((long long)b * s.Tq + i) * s.H + h;
-        uint4* yr = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(p.y) + row * kD);
+        uint4* yr = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(p.y) + row * kD + kOC * g);
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
+        for (int c8 = 0; c8 < kOC / 8; ++c8) {
           uint4 v;
-          v.x = pack_bf16(o[8 * c8 + 0] * g, o[8 * c8 + 1] * g);
-          v.y = pack_bf16(o[8 * c8 + 2] * g, o[8 * c8 + 3] * g);
-          v.z = pack_bf16(o[8 * c8 + 4] * g, o[8 * c8 + 5] * g);
-          v.w = pack_bf16(o[8 * c8 + 6] * g, o[8 * c8 + 7] * g);
+          v.x = pack_bf16(o[8 * c8 + 0] * gsc, o[8 * c8 + 1] * gsc);
+          v.y = pack_bf16(o[8 * c8 + 2] * gsc, o[8 * c8 + 3] * gsc);
+          v.z = pack_bf16(o[8 * c8 + 4] * gsc, o[8 * c8 + 5] * gsc);
+          v.w = pack_bf16(o[8 * c8 + 6] * gsc, o[8 * c8 + 7] * gsc);
           yr[c8] = v;
         }
-        p.no[row] = nraw;
+        if (g == 0) p.no[row] = nraw;
       }
     }
   }
@@ -509,9 +581,9 @@ size_t tc_fwd_workspace(const AttnShape& s) {
          al256((size_t)BH * (Tkp / kBN) * 16);
 }
 
-void tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
-            cudaStream_t st) {
-  if (s.B == 0 || s.H == 0) return;
+int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
+           cudaStream_t st) {
+  if (s.B == 0 || s.H == 0) return SCREEN_OK;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !g_tc_attr[dev]) {
@@ -538,10 +610,29 @@ void tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_gi
   if (mt > 0)
     tc_ik_meta_kernel<<<(unsigned)((mt + 255) / 256), 256, 0, st>>>(ikT, meta, (int)BH, s.Tk,
                                                                    (int)Tkp);
-  if (s.Tq == 0) return;
+  if (s.Tq == 0) return SCREEN_OK;
+  CUtensorMap tq, tk, tv;
+  if (!make_tmap_bthd(&tq, p.q.p, s.B, s.Tq, s.H, p.q.sb, p.q.st, kBM) ||
+      !make_tmap_bthd(&tk, p.k.p, s.B, s.Tk, s.H, p.k.sb, p.k.st, kBN) ||
+      !make_tmap_bthd(&tv, vhat, s.B, s.Tk, s.H, (long long)s.Tk * s.H * kD,
+                      (long long)s.H * kD, kBN))
+    return SCREEN_ERR_CUDA;
   dim3 grid((s.Tq + kBM - 1) / kBM, s.B * s.H);
-  tc_fwd_kernel<<<grid, kThreads, kSmemBytes, st>>>(s, p, vhat, ikT, meta, (int)Tkp);
+  tc_fwd_kernel<<<grid, kThreads, kSmemBytes, st>>>(s, p, ikT, meta, (int)Tkp, tq, tk, tv);
+  return SCREEN_OK;
 }
+
+#ifdef SCREEN_FWD_PROFILE
+extern "C" SCREEN_API int screen_debug_fwd_profile(unsigned long long* out, int clear) {
+  if (cudaMemcpyFromSymbol(out, g_fwd_prof, sizeof(unsigned long long) * 16) != cudaSuccess)
+    return -1;
+  if (clear) {
+    unsigned long long z[16] = {};
+    cudaMemcpyToSymbol(g_fwd_prof, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
 
 int tc_device_status(bool clear) {
   int v = 0;

@@ -1,6 +1,8 @@
 // Shared device helpers for the Screening Attention kernels (sm_100a).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include "../../include/screening_b200.h"
@@ -200,6 +202,16 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
+// TMA tile load of a 4-D tensor map (no multicast) into this CTA's shared
+// memory, completion counted in bytes on `bar`; c0 is the innermost coordinate
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -310,3 +322,37 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn_major, 
 
 }  // namespace sm100
 }  // namespace screen
+
+// ---------------------------------------------------------------------------
+// Host: TMA descriptor of a bf16 (B, T, H, 64) tensor with element strides
+// sb (batch) and st (time), unit stride over d and 64 over h.  The box is
+// 64 d x 1 head x `rows` times x 1 batch, 128-byte swizzled: in shared memory
+// it lands as `rows` rows of 128 B, 16-byte chunks XOR-swizzled by row % 8,
+// the canonical K-major SW128 layout of the tcgen05 smem descriptors.  Rows
+// at t >= T read as zeros.  The encoder comes from the driver at run time.
+// ---------------------------------------------------------------------------
+namespace screen {
+inline bool make_tmap_bthd(CUtensorMap* map, const void* base, long long B, long long T, int H,
+                           long long sb, long long st, int rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }();
+  if (!encode) return false;
+  const cuuint64_t dims[4] = {64, (cuuint64_t)H, (cuuint64_t)(T > 0 ? T : 1),
+                              (cuuint64_t)(B > 0 ? B : 1)};
+  const cuuint64_t strides[3] = {64 * 2, (cuuint64_t)st * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+}  // namespace screen
+

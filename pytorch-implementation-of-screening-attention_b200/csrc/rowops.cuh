@@ -67,7 +67,7 @@ void simt_bwd(int dtype, int D, const AttnShape& s, const BwdPtrs& p, int stages
 // tcgen05 / TMEM forward (bf16, D = 64).
 bool tc_supported(int dtype, int D);
 size_t tc_fwd_workspace(const AttnShape& s);
-void tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
+int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
             cudaStream_t st);
 int tc_device_status(bool clear);
 // tcgen05 / TMEM backward (bf16, D = 64); aux_ws holds tc_bwd_aux_bytes()
