@@ -216,9 +216,9 @@ int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
             Rows{a->v, a->v_sb, a->v_st}, a->nq, a->nk, a->nv, G,
             OutRows{a->dq, a->dq_sb, a->dq_st}, OutRows{a->dk, a->dk_sb, a->dk_st},
             OutRows{a->dv, a->dv_sb, a->dv_st}, pr, pw};
-  if (use_tc_fwd(a->dtype, a->D))
-    tc_bwd(sh, p, ws + L.aux_off, stages, s);
-  else if (use_mma(a->dtype, a->D))
+  if (use_tc_fwd(a->dtype, a->D)) {
+    if ((st = tc_bwd(sh, p, ws + L.aux_off, stages, s))) return st;
+  } else if (use_mma(a->dtype, a->D))
     mma_bwd(a->D, sh, p, stages, s);
   else
     simt_bwd(a->dtype, a->D, sh, p, stages, s);

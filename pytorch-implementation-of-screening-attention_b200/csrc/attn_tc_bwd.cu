@@ -9,7 +9,7 @@
 // see raw bf16 q / k / v; 1/|q|, 1/|k|, 1/|v| are fp32 row / column scales.
 //
 // Two kernels, both warp specialised (10 warps: 8 compute = two warpgroups
-// splitting every 64-column tile in halves, 1 cp.async producer, 1 MMA
+// splitting every 64-column tile in halves, 1 TMA producer, 1 MMA
 // issuer), 512 TMEM columns, one CTA per SM:
 //   tc_bwd_dq_kernel  (query-major, 128 queries, key tiles of 64):
 //       S = Q K^T, dP = G_hi V^T + G_lo V^T, dQ += dS K
@@ -27,7 +27,7 @@ namespace {
 using namespace sm100;
 typedef __nv_bfloat16 bf16;
 
-constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 3, kThreads = 320;
+constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 4, kThreads = 320;
 constexpr int kCompute = 256;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t TILE_A = kBM * kD * 2;  // 128-row operand tile, 16 KB
@@ -112,7 +112,9 @@ constexpr uint32_t SMEM = (OFF_MISC + 64 + 1024 > 120 * 1024) ? OFF_MISC + 64 + 
 }  // namespace dq
 
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_bwd_dq_kernel(AttnShape s, BwdPtrs p, Aux ax) {
+    tc_bwd_dq_kernel(AttnShape s, BwdPtrs p, Aux ax, const __grid_constant__ CUtensorMap tmQ,
+                     const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV) {
   using namespace dq;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -141,9 +143,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n = any ? (int)(hi / kBN) - kt0 + 1 : 0;
 
   if (tid == 0) {
-    mbar_init(bar(BAR_A), 32);
+    mbar_init(bar(BAR_A), 1);
     for (int i = 0; i < kNS; ++i) {
-      mbar_init(bar(BAR_FULL + i), 33);
+      // one arrival with the TMA byte count, one after the column factors
+      mbar_init(bar(BAR_FULL + i), 2);
       mbar_init(bar(BAR_EMPTY + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -163,22 +166,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 8) {
     // ---------------------------------------------------------- producer
-    const bf16* qh = reinterpret_cast<const bf16*>(p.q.p) + (long long)b * p.q.sb + (long long)h * kD;
-    const bf16* kh = reinterpret_cast<const bf16*>(p.k.p) + (long long)b * p.k.sb + (long long)h * kD;
-    const bf16* vh = reinterpret_cast<const bf16*>(p.v.p) + (long long)b * p.v.sb + (long long)h * kD;
-    const bf16* gh = reinterpret_cast<const bf16*>(p.G) + ((long long)b * s.Tq * s.H + h) * kD;
-    const bf16* gl = gh + (long long)s.B * s.Tq * s.H * kD;
-    const long long gst = (long long)s.H * kD;
-    for (int c = lane; c < kBM * 8; c += 32) {
-      const int row = c >> 3, ch = c & 7;
-      const long long t = i0 + row;
-      const bool ok = t < s.Tq;
-      const uint32_t off = tile_off<kD>(row, ch);
-      cp_async16(base + OFF_Q + off, qh + (ok ? t * p.q.st : 0) + ch * 8, ok);
-      cp_async16(base + OFF_GH + off, gh + (ok ? t * gst : 0) + ch * 8, ok);
-      cp_async16(base + OFF_GL + off, gl + (ok ? t * gst : 0) + ch * 8, ok);
+    // lane 0 issues the TMA copies: Q, G_hi, G_lo once (128 rows; G_lo is
+    // batch b + B of the two-plane G map), then per key tile K, V and the
+    // 1/|k|, 1/|v| runs with the tile's maxima; the warp fills the column
+    // (cos, sin) by rotation
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar(BAR_A), 3 * TILE_A);
+      tma_load_4d(base + OFF_Q, &tmQ, 0, h, (int)i0, b, bar(BAR_A));
+      tma_load_4d(base + OFF_GH, &tmG, 0, h, (int)i0, b, bar(BAR_A));
+      tma_load_4d(base + OFF_GL, &tmG, 0, h, (int)i0, b + s.B, bar(BAR_A));
     }
-    mbar_arrive_cp_async(bar(BAR_A));
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const int c = lane + 32 * hh;
@@ -193,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* ikh = ax.ikT + (long long)bh * ax.Tkp;
     const float* ivh = ax.ivT + (long long)bh * ax.Tkp;
     const float4* mh = ax.mk + (long long)bh * (ax.Tkp / kBN);
+    int issued = 0;
     for (int j = 0; j < n; ++j) {
       const int st = j % kNS;
       if (j >= kNS) {
@@ -203,18 +201,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int kt = kt0 + j;
       const long long j0 = (long long)kt * kBN;
       const uint32_t kb = base + OFF_K + st * TILE_B, vb = base + OFF_V + st * TILE_B;
-      for (int c = lane; c < kBN * 8; c += 32) {
-        const int row = c >> 3, ch = c & 7;
-        const long long t = j0 + row;
-        const bool ok = t < s.Tk;
-        cp_async16(kb + tile_off<kD>(row, ch), kh + (ok ? t * p.k.st : 0) + ch * 8, ok);
-        cp_async16(vb + tile_off<kD>(row, ch), vh + (ok ? t * p.v.st : 0) + ch * 8, ok);
-      }
       const uint32_t colb = base + OFF_COL + st * COLB;
       float* col = colp + st * (COLB / 4);
-      if (lane < 16) cp_async16(colb + lane * 16, ikh + j0 + lane * 4, true);
-      else cp_async16(colb + kBN * 4 + (lane - 16) * 16, ivh + j0 + (lane - 16) * 4, true);
-      if (lane == 0) cp_async16(colb + 4 * kBN * 4, mh + kt, true);
+      if (lane == 0) {
+        const uint32_t fb = bar(BAR_FULL + st);
+        mbar_arrive_expect_tx(fb, 2 * TILE_B + 2 * kBN * 4 + 16);
+        tma_load_4d(kb, &tmK, 0, h, (int)j0, b, fb);
+        tma_load_4d(vb, &tmV, 0, h, (int)j0, b, fb);
+        bulk_g2s(colb, ikh + j0, kBN * 4, fb);
+        bulk_g2s(colb + kBN * 4, ivh + j0, kBN * 4, fb);
+        bulk_g2s(colb + 4 * kBN * 4, mh + kt, 16, fb);
+      }
+      issued = j + 1;
       float sb = 0.f, cb = 0.f;
       if (lane == 0) sincospif((float)(j0 - p0) / w, &sb, &cb);
       sb = __shfl_sync(0xffffffffu, sb, 0);
@@ -223,11 +221,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       col[3 * kBN + lane] = sb * cphi0 + cb * sphi0;
       col[2 * kBN + lane + 32] = cb * cphi1 - sb * sphi1;
       col[3 * kBN + lane + 32] = sb * cphi1 + cb * sphi1;
-      mbar_arrive_cp_async(bar(BAR_FULL + st));
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_FULL + st));
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (lane == 0 && *abort_flag) {
+      // let the copies already issued land before the CTA's smem goes away
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(bar(BAR_A), 0) && globaltimer() - t0 < kWaitLimitNs) {
+      }
+      for (int j = issued > kNS ? issued - kNS : 0; j < issued; ++j)
+        while (!mbar_try_wait(bar(BAR_FULL + j % kNS), (j / kNS) & 1) &&
+               globaltimer() - t0 < kWaitLimitNs) {
+        }
+    }
+    __syncwarp();
   } else if (warp == 9) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -429,7 +436,9 @@ constexpr uint32_t SMEM = (OFF_MISC + 64 + 1024 > 120 * 1024) ? OFF_MISC + 64 + 
 }  // namespace kv
 
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_bwd_kv_kernel(AttnShape s, BwdPtrs p, Aux ax) {
+    tc_bwd_kv_kernel(AttnShape s, BwdPtrs p, Aux ax, const __grid_constant__ CUtensorMap tmQ,
+                     const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV) {
   using namespace kv;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -461,9 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n = any ? (int)(ihi / kBN) - qt0 + 1 : 0;
 
   if (tid == 0) {
-    mbar_init(bar(BAR_A), 32);
+    mbar_init(bar(BAR_A), 1);
     for (int i = 0; i < kNS; ++i) {
-      mbar_init(bar(BAR_FULL + i), 33);
+      // one arrival with the TMA byte count, one after the column factors
+      mbar_init(bar(BAR_FULL + i), 2);
       mbar_init(bar(BAR_EMPTY + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -487,19 +497,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 8) {
     // ---------------------------------------------------------- producer
-    const bf16* qh = reinterpret_cast<const bf16*>(p.q.p) + (long long)b * p.q.sb + (long long)h * kD;
-    const bf16* gh = reinterpret_cast<const bf16*>(p.G) + ((long long)b * s.Tq * s.H + h) * kD;
-    const bf16* gl = gh + (long long)s.B * s.Tq * s.H * kD;
-    const long long gst = (long long)s.H * kD;
-    for (int c = lane; c < kBM * 8; c += 32) {
-      const int row = c >> 3, ch = c & 7;
-      const long long t = j0 + row;
-      const bool ok = t < s.Tk;
-      const uint32_t off = tile_off<kD>(row, ch);
-      cp_async16(base + OFF_K + off, kh + (ok ? t * p.k.st : 0) + ch * 8, ok);
-      cp_async16(base + OFF_V + off, vh + (ok ? t * p.v.st : 0) + ch * 8, ok);
+    // lane 0 issues the TMA copies: K, V once (128 rows), then per query
+    // tile Q, G_hi, G_lo and the 1/|q| run with its maximum; the warp fills
+    // the column (cos, sin) by rotation
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar(BAR_A), 2 * TILE_A);
+      tma_load_4d(base + OFF_K, &tmK, 0, h, (int)j0, b, bar(BAR_A));
+      tma_load_4d(base + OFF_V, &tmV, 0, h, (int)j0, b, bar(BAR_A));
     }
-    mbar_arrive_cp_async(bar(BAR_A));
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const int c = lane + 32 * hh;
@@ -513,6 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cphi1 = tab[lane + 32], sphi1 = tab[kBN + lane + 32];
     const float* iqh = ax.iqT + (long long)bh * ax.Tqp;
     const float4* mh = ax.mq + (long long)bh * (ax.Tqp / kBN);
+    int issued = 0;
     for (int j = 0; j < n; ++j) {
       const int st = j % kNS;
       if (j >= kNS) {
@@ -523,19 +529,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int qt = qt0 + j;
       const long long iq0 = (long long)qt * kBN;
       const uint32_t sb_ = base + OFF_Q + st * STAGE;
-      for (int c = lane; c < kBN * 8; c += 32) {
-        const int row = c >> 3, ch = c & 7;
-        const long long t = iq0 + row;
-        const bool ok = t < s.Tq;
-        const uint32_t off = tile_off<kD>(row, ch);
-        cp_async16(sb_ + off, qh + (ok ? t * p.q.st : 0) + ch * 8, ok);
-        cp_async16(sb_ + TILE_B + off, gh + (ok ? t * gst : 0) + ch * 8, ok);
-        cp_async16(sb_ + 2 * TILE_B + off, gl + (ok ? t * gst : 0) + ch * 8, ok);
-      }
       const uint32_t colb = base + OFF_COL + st * COLB;
       float* col = colp + st * (COLB / 4);
-      if (lane < 16) cp_async16(colb + lane * 16, iqh + iq0 + lane * 4, true);
-      else if (lane == 16) cp_async16(colb + 3 * kBN * 4, mh + qt, true);
+      if (lane == 0) {
+        const uint32_t fb = bar(BAR_FULL + st);
+        mbar_arrive_expect_tx(fb, 3 * TILE_B + kBN * 4 + 16);
+        tma_load_4d(sb_, &tmQ, 0, h, (int)iq0, b, fb);
+        tma_load_4d(sb_ + TILE_B, &tmG, 0, h, (int)iq0, b, fb);
+        tma_load_4d(sb_ + 2 * TILE_B, &tmG, 0, h, (int)iq0, b + s.B, fb);
+        bulk_g2s(colb, iqh + iq0, kBN * 4, fb);
+        bulk_g2s(colb + 3 * kBN * 4, mh + qt, 16, fb);
+      }
+      issued = j + 1;
       // column angle pi (iq0 + c + q_offset - j0) / w by rotation
       float sb = 0.f, cbv = 0.f;
       if (lane == 0) sincospif((float)(iq0 + s.q_offset - j0) / w, &sb, &cbv);
@@ -545,11 +550,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       col[2 * kBN + lane] = sb * cphi0 + cbv * sphi0;
       col[kBN + lane + 32] = cbv * cphi1 - sb * sphi1;
       col[2 * kBN + lane + 32] = sb * cphi1 + cbv * sphi1;
-      mbar_arrive_cp_async(bar(BAR_FULL + st));
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_FULL + st));
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (lane == 0 && *abort_flag) {
+      // let the copies already issued land before the CTA's smem goes away
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(bar(BAR_A), 0) && globaltimer() - t0 < kWaitLimitNs) {
+      }
+      for (int j = issued > kNS ? issued - kNS : 0; j < issued; ++j)
+        while (!mbar_try_wait(bar(BAR_FULL + j % kNS), (j / kNS) & 1) &&
+               globaltimer() - t0 < kWaitLimitNs) {
+        }
+    }
+    __syncwarp();
   } else if (warp == 9) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -836,8 +850,8 @@ long long tc_bwd_partials(const AttnShape& s) {
   return (long long)s.B * ((s.Tk + kBM - 1) / kBM);
 }
 
-void tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st) {
-  if (s.B == 0 || s.H == 0) return;
+int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st) {
+  if (s.B == 0 || s.H == 0) return SCREEN_OK;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !g_bwd_attr[dev]) {
@@ -866,14 +880,28 @@ void tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cuda
     tc_bwd_aux_kernel<<<dim3((unsigned)nblk, 2), 64, 0, st>>>(
         p.nq, p.nk, p.nv, s.kpm, s.kpm_sb, s.B, s.H, s.Tq, s.Tk, (int)Tqp, (int)Tkp, iqT, ikT,
         ivT, mq, mk);
+  // TMA descriptors: q, k, v as given (raw, strided); G as two stacked
+  // planes [2][B][Tq][H][D] (batch b + B is the low plane)
+  CUtensorMap tq128, tq64, tg128, tg64, tk128, tk64, tv128, tv64;
+  const long long gsb = (long long)s.Tq * s.H * kD, gst = (long long)s.H * kD;
+  if (!make_tmap_bthd(&tq128, p.q.p, s.B, s.Tq, s.H, p.q.sb, p.q.st, kBM) ||
+      !make_tmap_bthd(&tq64, p.q.p, s.B, s.Tq, s.H, p.q.sb, p.q.st, kBN) ||
+      !make_tmap_bthd(&tg128, p.G, 2LL * s.B, s.Tq, s.H, gsb, gst, kBM) ||
+      !make_tmap_bthd(&tg64, p.G, 2LL * s.B, s.Tq, s.H, gsb, gst, kBN) ||
+      !make_tmap_bthd(&tk128, p.k.p, s.B, s.Tk, s.H, p.k.sb, p.k.st, kBM) ||
+      !make_tmap_bthd(&tk64, p.k.p, s.B, s.Tk, s.H, p.k.sb, p.k.st, kBN) ||
+      !make_tmap_bthd(&tv128, p.v.p, s.B, s.Tk, s.H, p.v.sb, p.v.st, kBM) ||
+      !make_tmap_bthd(&tv64, p.v.p, s.B, s.Tk, s.H, p.v.sb, p.v.st, kBN))
+    return SCREEN_ERR_CUDA;
   if (s.Tq > 0 && (stages & 2)) {
     dim3 g1((s.Tq + kBM - 1) / kBM, s.B * s.H);
-    tc_bwd_dq_kernel<<<g1, kThreads, dq::SMEM, st>>>(s, p, ax);
+    tc_bwd_dq_kernel<<<g1, kThreads, dq::SMEM, st>>>(s, p, ax, tq128, tg128, tk64, tv64);
   }
   if (s.Tk > 0 && (stages & 4)) {
     dim3 g2((s.Tk + kBM - 1) / kBM, s.B * s.H);
-    tc_bwd_kv_kernel<<<g2, kThreads, kv::SMEM, st>>>(s, p, ax);
+    tc_bwd_kv_kernel<<<g2, kThreads, kv::SMEM, st>>>(s, p, ax, tq64, tg64, tk128, tv128);
   }
+  return SCREEN_OK;
 }
 
 int tc_bwd_device_status(bool clear) {

@@ -73,7 +73,7 @@ int tc_device_status(bool clear);
 // tcgen05 / TMEM backward (bf16, D = 64); aux_ws holds tc_bwd_aux_bytes()
 size_t tc_bwd_aux_bytes(const AttnShape& s);
 long long tc_bwd_partials(const AttnShape& s);
-void tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st);
+int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st);
 int tc_bwd_device_status(bool clear);
 
 // bf16 warp-level mma.sync kernels (D = 64).
