@@ -42,7 +42,10 @@ typedef __nv_bfloat16 bf16;
 #define SCREEN_FWD_CG 2
 #endif
 constexpr int kCG = SCREEN_FWD_CG;
-constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 4;
+constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 5;
+// S / P ring in TMEM: P (bf16) is written over the S (fp32) columns it came
+// from, so three 64-column buffers + O fit the 256 columns of a CTA
+constexpr int kSB = 3;
 constexpr int kCW = 4 * kCG;                 // compute warps
 constexpr int kNC = kBN / kCG;               // columns per compute thread per tile
 constexpr int kCT = 32 * kCW;                // compute threads
@@ -59,15 +62,17 @@ constexpr uint32_t COL_BYTES = 3 * kBN * 4 + 16;           // meta = (ik min, ik
 constexpr uint32_t OFF_TAB = OFF_COL + kNS * COL_BYTES;    // (cos, sin)(pi c / w), c < 64
 constexpr uint32_t OFF_BAR = OFF_TAB + 2 * kBN * 4;
 constexpr int BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = BAR_KV_FULL + kNS,
-              BAR_S_FULL = BAR_KV_EMPTY + kNS, BAR_S_FREE = BAR_S_FULL + 2,
-              BAR_P_FULL = BAR_S_FREE + 2, BAR_O_FULL = BAR_P_FULL + 2;
-constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 16;
+              BAR_S_FULL = BAR_KV_EMPTY + kNS, BAR_P_FULL = BAR_S_FULL + kSB,
+              BAR_O_FULL = BAR_P_FULL + kSB, BAR_COUNT = BAR_O_FULL + 1;
+constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 24;
+static_assert(BAR_COUNT <= 24, "barrier space");
 constexpr uint32_t OFF_RED = OFF_MISC + 64;                // [kCG][kBM] epilogue sums
 constexpr uint32_t SMEM_USED = OFF_RED + kCG * kBM * 4;
 // at least 80 KB per CTA: at most two CTAs (2 x 256 TMEM columns) per SM
 constexpr uint32_t kSmemBytes = (SMEM_USED + 1024 > 80 * 1024) ? SMEM_USED + 1024 : 80 * 1024;
 
-constexpr uint32_t TM_S = 0, TM_P = 128, TM_O = 192, TM_COLS = 256;
+constexpr uint32_t TM_S = 0, TM_O = kSB * kBN, TM_COLS = 256;
+static_assert(TM_O + kD <= TM_COLS, "TMEM budget");
 
 __device__ int g_device_status = 0;
 
@@ -96,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   float* tab = reinterpret_cast<float*>(gbase + OFF_TAB);
   const uint32_t bars = base + OFF_BAR;
   uint32_t* misc = reinterpret_cast<uint32_t*>(gbase + OFF_MISC);
-  // misc[0] tmem base, misc[1..2] skip flags, misc[3] O valid, misc[4] abort
+  // misc[0] tmem base, misc[4] abort, misc[5] O valid, misc[8..8+kSB) skip flags
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
   auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
 
@@ -122,14 +127,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(bar(BAR_KV_FULL + i), 2);
       mbar_init(bar(BAR_KV_EMPTY + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kSB; ++i) {
       mbar_init(bar(BAR_S_FULL + i), 1);
-      mbar_init(bar(BAR_S_FREE + i), kCT);
       mbar_init(bar(BAR_P_FULL + i), kCT);
+      misc[8 + i] = 0;
     }
     mbar_init(bar(BAR_O_FULL), 2);
-    misc[1] = misc[2] = misc[3] = 0;
     misc[4] = 0;
+    misc[5] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) tmem_alloc(base + OFF_MISC, TM_COLS);
@@ -213,52 +218,53 @@ __global__ void __launch_bounds__(kThreads, 2)
       constexpr uint32_t idS = idesc_bf16(kBM, kBN, 0, 0);
       constexpr uint32_t idPV = idesc_bf16(kBM, kD, 0, 1);
       bool o_started = false, ok = mbar_wait(bar(BAR_Q), 0, abort_flag, kWaitLimitNs);
-      auto issue_pv = [&](int jj) -> bool {
-        const int bb = jj & 1, st = jj % kNS;
+      // S_j = Q K_j^T into ring buffer j % kSB, kept kSB tiles ahead of the
+      // compute warps; buffer reuse is ordered by the tensor core's in-order
+      // execution (S_{j+kSB} is issued after PV_j, which read P_j there)
+      auto issue_s = [&](int jj) -> bool {
+        const int st = jj % kNS, bb = jj % kSB;
         {
           PROF_T0();
-          const bool okp = mbar_wait(bar(BAR_P_FULL + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs);
-          PROF_ADD(3);
-          if (!okp) return false;
-        }
-        tc_fence_after();
-        if (!misc[1 + bb]) {
-          const uint32_t vb = sV + st * kBN * kD * 2;
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)
-            mma_ts(tmem + TM_O, tmem + TM_P + 32 * bb + 8 * kk,
-                   desc_sw128(vb + kk * 16 * 128, kBN * kD * 2, 1024), idPV,
-                   (o_started || kk > 0) ? 1u : 0u);
-          o_started = true;
-        }
-        mma_commit(bar(BAR_KV_EMPTY + st));
-        return true;
-      };
-      for (int j = 0; j < n && ok; ++j) {
-        const int st = j % kNS, bb = j & 1;
-        {
-          PROF_T0();
-          ok = mbar_wait(bar(BAR_KV_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
+          const bool okk = mbar_wait(bar(BAR_KV_FULL + st), (jj / kNS) & 1, abort_flag, kWaitLimitNs);
           PROF_ADD(1);
+          if (!okk) return false;
         }
-        if (ok && j >= 2) {
-          PROF_T0();
-          ok = mbar_wait(bar(BAR_S_FREE + bb), ((j >> 1) - 1) & 1, abort_flag, kWaitLimitNs);
-          PROF_ADD(2);
-        }
-        if (!ok) break;
         tc_fence_after();
-        fence_proxy_async_smem();
         const uint32_t kb = sK + st * kBN * kD * 2;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
           mma_ss(tmem + TM_S + kBN * bb, desc_sw128(sQ + kk * 32, 16, 1024),
                  desc_sw128(kb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
         mma_commit(bar(BAR_S_FULL + bb));
-        if (j >= 1) ok = issue_pv(j - 1);
+        return true;
+      };
+      for (int j = 0; j < n && j < kSB && ok; ++j) ok = issue_s(j);
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j % kNS, bb = j % kSB;
+        {
+          PROF_T0();
+          ok = mbar_wait(bar(BAR_P_FULL + bb), (j / kSB) & 1, abort_flag, kWaitLimitNs);
+          PROF_ADD(3);
+        }
+        if (!ok) break;
+        tc_fence_after();
+        if (!misc[8 + bb]) {
+          // P_j sits in the first 16 columns of each compute group's half of
+          // the buffer: keys [32 g, 32 g + 32) at columns [32 g, 32 g + 16)
+          const uint32_t vb = sV + st * kBN * kD * 2;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            const uint32_t pcol = kCG == 2 ? (kk >> 1) * 32 + (kk & 1) * 8 : 8 * kk;
+            mma_ts(tmem + TM_O, tmem + TM_S + kBN * bb + pcol,
+                   desc_sw128(vb + kk * 16 * 128, kBN * kD * 2, 1024), idPV,
+                   (o_started || kk > 0) ? 1u : 0u);
+          }
+          o_started = true;
+        }
+        mma_commit(bar(BAR_KV_EMPTY + st));
+        if (j + kSB < n) ok = issue_s(j + kSB);
       }
-      if (ok && n >= 1) ok = issue_pv(n - 1);
-      misc[3] = o_started ? 1u : 0u;
+      misc[5] = o_started ? 1u : 0u;
       mma_commit(bar(BAR_O_FULL));
       mbar_arrive(bar(BAR_O_FULL));
     }
@@ -307,14 +313,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     bool ok = true;
     unsigned long long live_tiles = 0;
     for (int j = 0; j < n; ++j) {
-      const int st = j % kNS, bb = j & 1;
+      const int st = j % kNS, bb = j % kSB;
 #ifdef SCREEN_FWD_PROFILE
       const long long _tc0 = clock64();
 #endif
       {
         PROF_T0();
         ok = mbar_wait(bar(BAR_KV_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
-             mbar_wait(bar(BAR_S_FULL + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
+             mbar_wait(bar(BAR_S_FULL + bb), (j / kSB) & 1, abort_flag, kWaitLimitNs);
         if (tid == 0) PROF_ADD(4);
       }
       // all 128 threads take the same branch before the next named barrier
@@ -330,8 +336,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_ld32(tmem + TM_S + kBN * bb + kNC * g + 32 * h32 + lane_off,
                   *reinterpret_cast<uint32_t(*)[32]>(&sv[32 * h32]));
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar(BAR_S_FREE + bb));
 
       const float* colt = colp + st * (COL_BYTES / 4);   // whole-tile columns
       const float* col = colt + kNC * g;                  // this group's columns
@@ -385,15 +389,16 @@ __global__ void __launch_bounds__(kThreads, 2)
                                         c + 3 >= iclo && c + 3 <= ichi);
           }
         }
+        // P over this group's own S columns (already in registers)
         if constexpr (kNC == 64) {
-          tmem_st32(tmem + TM_P + 32 * bb + lane_off, *reinterpret_cast<uint32_t(*)[32]>(pk));
+          tmem_st32(tmem + TM_S + kBN * bb + lane_off, *reinterpret_cast<uint32_t(*)[32]>(pk));
         } else {
-          tmem_st16(tmem + TM_P + 32 * bb + (kNC / 2) * g + lane_off, pk);
+          tmem_st16(tmem + TM_S + kBN * bb + kNC * g + lane_off, pk);
         }
         tmem_wait_st();
       }
       if (tid == 0) {
-        misc[1 + bb] = live ? 0u : 1u;
+        misc[8 + bb] = live ? 0u : 1u;
         live_tiles += live ? 1 : 0;
       }
       tc_fence_before();
@@ -421,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // row's |o|^2 is summed over the groups through shared memory
     constexpr int kOC = kD / kCG;
     float o[kOC];
-    if (ok && misc[3]) {
+    if (ok && misc[5]) {
       uint32_t ov[kOC];
 #pragma unroll
       for (int h32 = 0; h32 < kOC / 32; ++h32)
