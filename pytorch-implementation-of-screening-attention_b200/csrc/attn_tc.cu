@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   float* tab = reinterpret_cast<float*>(gbase + OFF_TAB);
   const uint32_t bars = base + OFF_BAR;
   uint32_t* misc = reinterpret_cast<uint32_t*>(gbase + OFF_MISC);
-  // misc[0] tmem base, misc[4] abort, misc[5] O valid, misc[8..8+kSB) skip flags
+  // misc[0] tmem base, misc[4] abort, misc[5] O valid
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
   auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
 
@@ -130,7 +130,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int i = 0; i < kSB; ++i) {
       mbar_init(bar(BAR_S_FULL + i), 1);
       mbar_init(bar(BAR_P_FULL + i), kCT);
-      misc[8 + i] = 0;
     }
     mbar_init(bar(BAR_O_FULL), 2);
     misc[4] = 0;
@@ -248,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         if (!ok) break;
         tc_fence_after();
-        if (!misc[8 + bb]) {
+        {
           // P_j sits in the first 16 columns of each compute group's half of
           // the buffer: keys [32 g, 32 g + 32) at columns [32 g, 32 g + 16)
           const uint32_t vb = sV + st * kBN * kD * 2;
@@ -304,8 +303,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       // relu(t) = saturate(t): t = 1 - r (1 - S) <= 1, so the clamp is free
       const float a0 = __saturatef(fmaf(rq, x.x, omr)), a1 = __saturatef(fmaf(rq, x.y, omr));
       const float2 a2 = make_float2(k0 ? a0 : 0.f, k1 ? a1 : 0.f);
+#ifdef SCREEN_EXP_NOMASK
+      const float2 m2 = half2;
+#else
       const float2 m2 =
           __ffma2_rn(cr2, make_float2(c0, c1), __ffma2_rn(sr2, make_float2(n0, n1), half2));
+#endif
       const float2 al = __fmul2_rn(__fmul2_rn(a2, m2), a2);
       return pack_bf16(al.x, al.y);
 #endif
@@ -323,11 +326,11 @@ __global__ void __launch_bounds__(kThreads, 2)
              mbar_wait(bar(BAR_S_FULL + bb), (j / kSB) & 1, abort_flag, kWaitLimitNs);
         if (tid == 0) PROF_ADD(4);
       }
-      // all 128 threads take the same branch before the next named barrier
-      if (bar_red_or(1, kCT, !ok)) {
-        ok = false;
-        break;
-      }
+      // warp-uniform verdict (the TMEM accesses below are warp-collective);
+      // a warp that gives up leaves the loop alone -- every other wait on its
+      // arrivals is bounded and sees the abort flag
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
       tc_fence_after();
       static_assert(kNC == 32 || kNC == 64, "column split");
       uint32_t sv[kNC];
@@ -349,14 +352,20 @@ __global__ void __launch_bounds__(kThreads, 2)
       imax = max(imax, (int)sv[kNC - 1]);
       const float smax = __int_as_float(imax);
       const float ikmax = colt[3 * kBN + 1];
+#ifdef SCREEN_EXP_NOPRETEST
+      const bool mine = true;
+#else
       const bool mine = r < 1.0f || (imax > 0 && fmaf(rq, smax * ikmax, omr) > 0.f);
-      const bool live = bar_red_or(1, kCT, mine);
+#endif
+      // liveness per warp block (32 rows x kNC columns): a dead block stores
+      // P = 0, so the warps never wait on one another within a tile
+      const bool live = __any_sync(0xffffffffu, mine);
+      uint32_t pk[kNC / 2];
       if (live) {
         const long long j0 = (long long)(kt0 + j) * kBN;
         const bool inside = (causal ? (p0 - (j0 + kBN - 1) >= 0 && p0 + kBM - 1 - j0 <= dmax)
                                     : (p0 - (j0 + kBN - 1) >= -(long long)dmax &&
                                        p0 + kBM - 1 - j0 <= dmax));
-        uint32_t pk[kNC / 2];
         const float4* ik4 = reinterpret_cast<const float4*>(col);
         const float4* cc4 = reinterpret_cast<const float4*>(col + kBN);
         const float4* sc4 = reinterpret_cast<const float4*>(col + 2 * kBN);
@@ -389,18 +398,18 @@ __global__ void __launch_bounds__(kThreads, 2)
                                         c + 3 >= iclo && c + 3 <= ichi);
           }
         }
-        // P over this group's own S columns (already in registers)
-        if constexpr (kNC == 64) {
-          tmem_st32(tmem + TM_S + kBN * bb + lane_off, *reinterpret_cast<uint32_t(*)[32]>(pk));
-        } else {
-          tmem_st16(tmem + TM_S + kBN * bb + kNC * g + lane_off, pk);
-        }
-        tmem_wait_st();
+      } else {
+#pragma unroll
+        for (int c = 0; c < kNC / 2; ++c) pk[c] = 0u;
       }
-      if (tid == 0) {
-        misc[8 + bb] = live ? 0u : 1u;
-        live_tiles += live ? 1 : 0;
+      // P over this group's own S columns (already in registers)
+      if constexpr (kNC == 64) {
+        tmem_st32(tmem + TM_S + kBN * bb + lane_off, *reinterpret_cast<uint32_t(*)[32]>(pk));
+      } else {
+        tmem_st16(tmem + TM_S + kBN * bb + kNC * g + lane_off, pk);
       }
+      tmem_wait_st();
+      if (lane == 0) live_tiles += live ? 1 : 0;
       tc_fence_before();
       mbar_arrive(bar(BAR_P_FULL + bb));
 #ifdef SCREEN_FWD_PROFILE
@@ -408,10 +417,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (tid == 0) atomicAdd(&g_fwd_prof[7], 1ull);
 #endif
     }
-    if (p.tile_stats && tid == 0) {
-      // reported in 16x64 score blocks, the unit of the warp-level kernels
-      atomicAdd((unsigned long long*)&p.tile_stats[0], 8ull * (unsigned long long)n);
-      atomicAdd((unsigned long long*)&p.tile_stats[1], 8ull * live_tiles);
+    if (p.tile_stats && lane == 0) {
+      // in 16x64 score blocks (the unit of the warp-level kernels): a tile is
+      // 8 of them, a warp block of 32 rows x kNC columns kNC / 32
+      if (tid == 0)
+        atomicAdd((unsigned long long*)&p.tile_stats[0], 8ull * (unsigned long long)n);
+      atomicAdd((unsigned long long*)&p.tile_stats[1], (unsigned long long)(kNC / 32) * live_tiles);
     }
     // epilogue: O -> TanhNorm -> y
     {

@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bb = jj & 1, st = jj % kNS;
         if (!mbar_wait(bar(BAR_P + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
         tc_fence_after();
-        if (!misc[1 + bb]) {
+        {
           const uint32_t kb = base + OFF_K + st * TILE_B;
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)
@@ -313,10 +313,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int st = j % kNS, bb = j & 1;
       ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
            mbar_wait(bar(BAR_SD + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
-      if (bar_red_or(1, kCompute, !ok)) {
-        ok = false;
-        break;
-      }
+      // warp-uniform verdict (the TMEM accesses below are warp-collective);
+      // a warp that gives up leaves the loop alone -- every other wait on its
+      // arrivals is bounded and sees the abort flag
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
       tc_fence_after();
       uint32_t sv[32], dv[32];
       tmem_ld32(tmem + TM_S + kBN * bb + cb + lane_off, sv);
@@ -331,7 +332,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       imax = max(imax, (int)sv[31]);
       const bool mine = r < 1.0f ||
                         (imax > 0 && fmaf(rq, __int_as_float(imax) * col[4 * kBN], omr) > 0.f);
-      const bool live = bar_red_or(1, kCompute, mine);
+      // liveness per warp block (32 rows x 32 columns): a dead block stores
+      // zeros, so the warps never wait on one another within a tile
+      const bool live = __any_sync(0xffffffffu, mine);
       if (live) {
         const long long j0 = (long long)(kt0 + j) * kBN;
         const bool inside = (causal ? (p0 - (j0 + kBN - 1) >= 0 && p0 + kBM - 1 - j0 <= dmax)
@@ -381,9 +384,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         else
           run(std::true_type{});
         tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, pk);
-        tmem_wait_st();
+      } else {
+        const uint32_t zero[16] = {};
+        tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, zero);
       }
-      if (tid == 0) misc[1 + bb] = live ? 0u : 1u;
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(BAR_P + bb));
     }
@@ -574,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bb = jj & 1, st = jj % kNS;
         if (!mbar_wait(bar(BAR_P + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
         tc_fence_after();
-        if (!misc[1 + bb]) {
+        {
           const uint32_t qb = base + OFF_Q + st * STAGE, ghb = qb + TILE_B;
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -654,10 +659,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int st = j % kNS, bb = j & 1;
       ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
            mbar_wait(bar(BAR_SD + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
-      if (bar_red_or(1, kCompute, !ok)) {
-        ok = false;
-        break;
-      }
+      // warp-uniform verdict (the TMEM accesses below are warp-collective);
+      // a warp that gives up leaves the loop alone -- every other wait on its
+      // arrivals is bounded and sees the abort flag
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
       tc_fence_after();
       uint32_t sv[32], dv[32];
       tmem_ld32(tmem + TM_S + kBN * bb + cb + lane_off, sv);
@@ -672,7 +678,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       imax = max(imax, (int)sv[31]);
       const bool mine = (r < 1.0f && keep) ||
                         (imax > 0 && fmaf(rk, __int_as_float(imax) * col[3 * kBN], omr) > 0.f);
-      const bool live = bar_red_or(1, kCompute, mine);
+      // liveness per warp block (32 rows x 32 columns): a dead block stores
+      // zeros, so the warps never wait on one another within a tile
+      const bool live = __any_sync(0xffffffffu, mine);
       if (live) {
         const long long pq0 = (long long)(qt0 + j) * kBN + s.q_offset;
         // d = p - j over the tile: [pq0 - (j0 + 127), pq0 + 63 - j0]
@@ -732,9 +740,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           run(std::true_type{});
         tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, pa);
         tmem_st16(tmem + TM_P2 + 32 * bb + 16 * g + lane_off, pd);
-        tmem_wait_st();
+      } else {
+        const uint32_t zero[16] = {};
+        tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, zero);
+        tmem_st16(tmem + TM_P2 + 32 * bb + 16 * g + lane_off, zero);
       }
-      if (tid == 0) misc[1 + bb] = live ? 0u : 1u;
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(BAR_P + bb));
     }
