@@ -38,7 +38,7 @@ constexpr uint32_t TM_S = 0, TM_DP = 128, TM_P1 = 256, TM_P2 = 320, TM_ACC1 = 38
 struct Aux {
   const float* iqT;   // [B*H][Tqp] 1/|q| (0 past Tq)
   const float* ikT;   // [B*H][Tkp] 1/|k| (0 past Tk)
-  const float* ivT;   // [B*H][Tkp] 1/|v| (0 past Tk and for padded keys)
+  const float* ivT;   // [B*H][Tkp] 1/(|v| |k|) (0 past Tk and for padded keys)
   const float4* mq;   // [B*H][Tqp/64] (max 1/|q| of the tile, -, -, -)
   const float4* mk;   // [B*H][Tkp/64] (max 1/|k| of the tile, -, -, -)
   int Tqp, Tkp;
@@ -371,10 +371,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               const float2 a2 = make_float2(a0, a1);
               const float2 m2 = __ffma2_rn(cr2, cc2, __ffma2_rn(sr2, sc2, half2));
-              const float2 dp2 = __fmul2_rn(make_float2(__uint_as_float(dv[c]),
-                                                        __uint_as_float(dv[c + 1])), iv2);
-              const float2 q2 = __fmul2_rn(__fmul2_rn(dp2, m2), a2);
-              const float2 ds = __fmul2_rn(q2, __fmul2_rn(ik2, twor2));
+              // dS / (2 r) = (G v) (1/|v| 1/|k|) m a; the 2 r goes to the epilogue
+              const float2 am = __fmul2_rn(a2, m2);
+              const float2 ds = __fmul2_rn(__fmul2_rn(make_float2(__uint_as_float(dv[c]),
+                                                                  __uint_as_float(dv[c + 1])),
+                                                      iv2),
+                                           am);
               pk[2 * q4 + hp] = pack_bf16(ds.x, ds.y);
             }
           }
@@ -410,6 +412,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                            i * p.q.st + (long long)h * kD;
         bf16* orow = reinterpret_cast<bf16*>(p.dq.p) + (long long)b * p.dq.sb + i * p.dq.st +
                      (long long)h * kD;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) acc[c] *= 2.0f * r;
         store_unit_jacobian(acc, qrow, iq, orow);
       }
     }
@@ -720,12 +724,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float2 a2 = make_float2(a0, a1);
               const float2 m2 = __ffma2_rn(cr2, cv2, __ffma2_rn(sr2, sn2, half2));
               const float2 sinrel = __ffma2_rn(ncr2x2, sn2, __fmul2_rn(sr2x2, cv2));
-              const float2 dp2 = __fmul2_rn(make_float2(__uint_as_float(dv[c]),
-                                                        __uint_as_float(dv[c + 1])), iv2);
+              // G v without this row's 1/|v|: it and the 2 r of dS are row
+              // constants applied in the epilogue and to the dr / dw sums
+              const float2 dp2 = make_float2(__uint_as_float(dv[c]), __uint_as_float(dv[c + 1]));
               const float2 asq = __fmul2_rn(a2, a2);
               const float2 al = __fmul2_rn(asq, m2);
-              const float2 q2 = __fmul2_rn(dp2, __fmul2_rn(a2, m2));  // dP m a
-              const float2 ds = __fmul2_rn(q2, __fmul2_rn(iq2, twor2));
+              const float2 q2 = __fmul2_rn(dp2, __fmul2_rn(a2, m2));  // dP m a / (1/|v|)
+              const float2 ds = __fmul2_rn(q2, iq2);
               pa[2 * q4 + hp] = pack_bf16(al.x, al.y);
               pd[2 * q4 + hp] = pack_bf16(ds.x, ds.y);
               accr2 = __ffma2_rn(q2, __ffma2_rn(x, ik2, m1), accr2);
@@ -749,8 +754,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(bar(BAR_P + bb));
     }
-    acc_r = 2.f * (accr2.x + accr2.y);   // dr = sum dP m 2a (S - 1)
-    acc_w = accw2.x + accw2.y;
+    acc_r = 2.f * iv * (accr2.x + accr2.y);   // dr = sum dP m 2a (S - 1)
+    acc_w = iv * (accw2.x + accw2.y);
     // epilogue: warpgroup 0 -> dk, warpgroup 1 -> dv (normalisation Jacobians)
     ok = ok && mbar_wait(bar(BAR_DONE), 0, abort_flag, kWaitLimitNs);
     // tcgen05.ld is warp-collective: every lane takes the same branch
@@ -765,6 +770,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok && valid) {
       if (g == 0) {
+        // dS was stored without this key's 2 r / |v|
+#pragma unroll
+        for (int c = 0; c < 64; ++c) acc[c] *= 2.0f * r * iv;
         store_unit_jacobian(acc, kh + jrow * p.k.st, ik,
                             reinterpret_cast<bf16*>(p.dk.p) + (long long)b * p.dk.sb +
                                 jrow * p.dk.st + (long long)h * kD);
@@ -827,7 +835,7 @@ __global__ void tc_bwd_aux_kernel(const float* __restrict__ nq, const float* __r
       x = 1.0f / nk[idx];
       ikT[bhh * Tp + t] = x;
       const bool masked = kpm && kpm[(long long)bb * kpm_sb + t];
-      ivT[bhh * Tp + t] = masked ? 0.f : 1.0f / nv[idx];
+      ivT[bhh * Tp + t] = masked ? 0.f : x / nv[idx];   // 1/|v| * 1/|k|
     }
   } else {
     if (!isk) iqT[bhh * Tp + t] = 0.f;
