@@ -82,6 +82,68 @@ __device__ __forceinline__ void store_unit_jacobian(const float (&acc)[64], cons
   }
 }
 
+// store_unit_jacobian with the accumulator row read from TMEM 32 columns at a
+// time (scaled by `scale`), in two passes (x . acc, then the output), so at
+// most 32 accumulators and 8 raw values are live.  `ok` false: acc = 0.
+// Warp-collective (tcgen05.ld): call it with the whole warp.
+__device__ __forceinline__ void store_unit_jacobian_tmem(uint32_t taddr, bool ok, float scale,
+                                                         const bf16* xrow, float inv, bf16* out,
+                                                         bool store) {
+  float dot = 0.f;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t u[32];
+    if (ok) {
+      tmem_ld32(taddr + 32 * h, u);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) u[c] = 0u;
+    }
+    if (store) {
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        const uint4 xv = reinterpret_cast<const uint4*>(xrow)[4 * h + c8];
+        const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16(w4[e]);
+          dot = fmaf(f.x, __uint_as_float(u[8 * c8 + 2 * e]), dot);
+          dot = fmaf(f.y, __uint_as_float(u[8 * c8 + 2 * e + 1]), dot);
+        }
+      }
+    }
+  }
+  const float cf = inv * inv * dot * scale;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t u[32];
+    if (ok) {
+      tmem_ld32(taddr + 32 * h, u);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) u[c] = 0u;
+    }
+    if (store) {
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        const uint4 xv = reinterpret_cast<const uint4*>(xrow)[4 * h + c8];
+        const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
+        uint32_t o4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16(w4[e]);
+          const float a0 = __uint_as_float(u[8 * c8 + 2 * e]) * scale;
+          const float a1 = __uint_as_float(u[8 * c8 + 2 * e + 1]) * scale;
+          o4[e] = pack_bf16(inv * (a0 - cf * f.x), inv * (a1 - cf * f.y));
+        }
+        reinterpret_cast<uint4*>(out)[4 * h + c8] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&o)[64]) {
   uint32_t u[64];
   uint32_t (&a0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&u[0]);
@@ -97,21 +159,25 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&o)[64]) {
 // dq kernel
 // ===========================================================================
 namespace dq {
+// two CTAs per SM: 3 K/V stages, single S / dP buffers with dS written over
+// the dP columns it came from, dQ accumulator -> 192 of 256 TMEM columns
+constexpr int kNSq = 3;
+constexpr uint32_t TMq_S = 0, TMq_DP = 64, TMq_ACC = 128, TMq_COLS = 256;
 constexpr uint32_t OFF_Q = 0, OFF_GH = TILE_A, OFF_GL = 2 * TILE_A;
 constexpr uint32_t OFF_K = 3 * TILE_A;
-constexpr uint32_t OFF_V = OFF_K + kNS * TILE_B;
-constexpr uint32_t OFF_COL = OFF_V + kNS * TILE_B;  // ik | iv | cos | sin [64] + meta
+constexpr uint32_t OFF_V = OFF_K + kNSq * TILE_B;
+constexpr uint32_t OFF_COL = OFF_V + kNSq * TILE_B;  // ik | iv | cos | sin [64] + meta
 constexpr uint32_t COLB = 4 * kBN * 4 + 16;
-constexpr uint32_t OFF_TAB = OFF_COL + kNS * COLB;
+constexpr uint32_t OFF_TAB = OFF_COL + kNSq * COLB;
 constexpr uint32_t OFF_BAR = OFF_TAB + 2 * kBN * 4;
-constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNS, BAR_SD = BAR_EMPTY + kNS,
-              BAR_SDFREE = BAR_SD + 2, BAR_P = BAR_SDFREE + 2, BAR_DONE = BAR_P + 2;
+constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNSq, BAR_SD = BAR_EMPTY + kNSq,
+              BAR_P = BAR_SD + 1, BAR_DONE = BAR_P + 1;
 constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 16;
-// >= 120 KB: one CTA per SM (each allocates all 512 TMEM columns)
-constexpr uint32_t SMEM = (OFF_MISC + 64 + 1024 > 120 * 1024) ? OFF_MISC + 64 + 1024 : 120 * 1024;
+constexpr uint32_t SMEM = OFF_MISC + 64 + 1024;
+static_assert(2 * (SMEM + 1024) <= 228 * 1024, "two CTAs per SM");
 }  // namespace dq
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     tc_bwd_dq_kernel(AttnShape s, BwdPtrs p, Aux ax, const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV) {
@@ -144,21 +210,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     mbar_init(bar(BAR_A), 1);
-    for (int i = 0; i < kNS; ++i) {
+    for (int i = 0; i < kNSq; ++i) {
       // one arrival with the TMA byte count, one after the column factors
       mbar_init(bar(BAR_FULL + i), 2);
       mbar_init(bar(BAR_EMPTY + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(BAR_SD + i), 1);
-      mbar_init(bar(BAR_SDFREE + i), kCompute);
-      mbar_init(bar(BAR_P + i), kCompute);
-    }
+    mbar_init(bar(BAR_SD), 1);
+    mbar_init(bar(BAR_P), kCompute);
     mbar_init(bar(BAR_DONE), 2);
     misc[1] = misc[2] = misc[3] = misc[4] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 0) tmem_alloc(base + OFF_MISC, TM_COLS);
+  if (warp == 0) tmem_alloc(base + OFF_MISC, TMq_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -192,10 +255,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float4* mh = ax.mk + (long long)bh * (ax.Tkp / kBN);
     int issued = 0;
     for (int j = 0; j < n; ++j) {
-      const int st = j % kNS;
-      if (j >= kNS) {
+      const int st = j % kNSq;
+      if (j >= kNSq) {
         int okw = 1;
-        if (lane == 0) okw = mbar_wait(bar(BAR_EMPTY + st), ((j / kNS) - 1) & 1, abort_flag, kWaitLimitNs);
+        if (lane == 0) okw = mbar_wait(bar(BAR_EMPTY + st), ((j / kNSq) - 1) & 1, abort_flag, kWaitLimitNs);
         if (!__shfl_sync(0xffffffffu, okw, 0)) break;
       }
       const int kt = kt0 + j;
@@ -229,8 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(bar(BAR_A), 0) && globaltimer() - t0 < kWaitLimitNs) {
       }
-      for (int j = issued > kNS ? issued - kNS : 0; j < issued; ++j)
-        while (!mbar_try_wait(bar(BAR_FULL + j % kNS), (j / kNS) & 1) &&
+      for (int j = issued > kNSq ? issued - kNSq : 0; j < issued; ++j)
+        while (!mbar_try_wait(bar(BAR_FULL + j % kNSq), (j / kNSq) & 1) &&
                globaltimer() - t0 < kWaitLimitNs) {
         }
     }
@@ -241,47 +304,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idS = idesc_bf16(kBM, kBN, 0, 0);
       constexpr uint32_t idQ = idesc_bf16(kBM, kD, 0, 1);
       bool started = false, ok = mbar_wait(bar(BAR_A), 0, abort_flag, kWaitLimitNs);
-      auto issue_dq = [&](int jj) -> bool {
-        const int bb = jj & 1, st = jj % kNS;
-        if (!mbar_wait(bar(BAR_P + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
+      // S_j, dP_j into the single S / dP buffers; the next pair is issued
+      // after dQ_j, which reads dS_j from the dP columns (in-order execution)
+      auto issue_sd = [&](int jj) -> bool {
+        const int st = jj % kNSq;
+        if (!mbar_wait(bar(BAR_FULL + st), (jj / kNSq) & 1, abort_flag, kWaitLimitNs)) return false;
         tc_fence_after();
-        {
-          const uint32_t kb = base + OFF_K + st * TILE_B;
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)
-            mma_ts(tmem + TM_ACC1, tmem + TM_P1 + 32 * bb + 8 * kk,
-                   desc_sw128(kb + kk * 16 * 128, TILE_B, 1024), idQ,
-                   (started || kk > 0) ? 1u : 0u);
-          started = true;
-        }
-        mma_commit(bar(BAR_EMPTY + st));
-        return true;
-      };
-      for (int j = 0; j < n && ok; ++j) {
-        const int st = j % kNS, bb = j & 1;
-        ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
-        if (ok && j >= 2)
-          ok = mbar_wait(bar(BAR_SDFREE + bb), ((j >> 1) - 1) & 1, abort_flag, kWaitLimitNs);
-        if (!ok) break;
-        tc_fence_after();
-        fence_proxy_async_smem();
         const uint32_t kb = base + OFF_K + st * TILE_B, vb = base + OFF_V + st * TILE_B;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TM_S + kBN * bb, desc_sw128(base + OFF_Q + kk * 32, 16, 1024),
+          mma_ss(tmem + TMq_S, desc_sw128(base + OFF_Q + kk * 32, 16, 1024),
                  desc_sw128(kb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TM_DP + kBN * bb, desc_sw128(base + OFF_GH + kk * 32, 16, 1024),
+          mma_ss(tmem + TMq_DP, desc_sw128(base + OFF_GH + kk * 32, 16, 1024),
                  desc_sw128(vb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TM_DP + kBN * bb, desc_sw128(base + OFF_GL + kk * 32, 16, 1024),
+          mma_ss(tmem + TMq_DP, desc_sw128(base + OFF_GL + kk * 32, 16, 1024),
                  desc_sw128(vb + kk * 32, 16, 1024), idS, 1u);
-        mma_commit(bar(BAR_SD + bb));
-        if (j >= 1) ok = issue_dq(j - 1);
+        mma_commit(bar(BAR_SD));
+        return true;
+      };
+      if (n > 0) ok = issue_sd(0);
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j % kNSq;
+        ok = mbar_wait(bar(BAR_P), j & 1, abort_flag, kWaitLimitNs);
+        if (!ok) break;
+        tc_fence_after();
+        // dS_j (bf16) sits in the first 16 columns of each compute group's
+        // 32-column half of the dP buffer
+        const uint32_t kb = base + OFF_K + st * TILE_B;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_ts(tmem + TMq_ACC, tmem + TMq_DP + (kk >> 1) * 32 + (kk & 1) * 8,
+                 desc_sw128(kb + kk * 16 * 128, TILE_B, 1024), idQ,
+                 (started || kk > 0) ? 1u : 0u);
+        started = true;
+        mma_commit(bar(BAR_EMPTY + st));
+        if (j + 1 < n) ok = issue_sd(j + 1);
       }
-      if (ok && n >= 1) ok = issue_dq(n - 1);
       misc[3] = started ? 1u : 0u;
       mma_commit(bar(BAR_DONE));
       mbar_arrive(bar(BAR_DONE));
@@ -310,9 +372,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float2 half2 = make_float2(0.5f, 0.5f), twor2 = make_float2(2.f * r, 2.f * r);
     bool ok = true;
     for (int j = 0; j < n; ++j) {
-      const int st = j % kNS, bb = j & 1;
-      ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
-           mbar_wait(bar(BAR_SD + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
+      const int st = j % kNSq;
+      ok = mbar_wait(bar(BAR_FULL + st), (j / kNSq) & 1, abort_flag, kWaitLimitNs) &&
+           mbar_wait(bar(BAR_SD), j & 1, abort_flag, kWaitLimitNs);
       // warp-uniform verdict (the TMEM accesses below are warp-collective);
       // a warp that gives up leaves the loop alone -- every other wait on its
       // arrivals is bounded and sees the abort flag
@@ -320,11 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       uint32_t sv[32], dv[32];
-      tmem_ld32(tmem + TM_S + kBN * bb + cb + lane_off, sv);
-      tmem_ld32(tmem + TM_DP + kBN * bb + cb + lane_off, dv);
+      tmem_ld32(tmem + TMq_S + cb + lane_off, sv);
+      tmem_ld32(tmem + TMq_DP + cb + lane_off, dv);
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar(BAR_SDFREE + bb));
       const float* col = colp + st * (COLB / 4);
       int imax = (int)sv[0];
 #pragma unroll
@@ -385,14 +445,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           run(std::false_type{});
         else
           run(std::true_type{});
-        tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, pk);
+        tmem_st16(tmem + TMq_DP + cb + lane_off, pk);   // over this group's dP
       } else {
         const uint32_t zero[16] = {};
-        tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, zero);
+        tmem_st16(tmem + TMq_DP + cb + lane_off, zero);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(BAR_P + bb));
+      mbar_arrive(bar(BAR_P));
     }
     // epilogue (warpgroup 0): dQ -> normalisation Jacobian -> dq
     if (g == 0) {
@@ -400,29 +460,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       // tcgen05.ld is warp-collective: every lane takes the same branch
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
-      float acc[64];
-      if (ok && misc[3]) {
-        tmem_ld64(tmem + TM_ACC1 + lane_off, acc);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) acc[c] = 0.f;
-      }
-      if (ok && i < s.Tq) {
-        const bf16* qrow = reinterpret_cast<const bf16*>(p.q.p) + (long long)b * p.q.sb +
-                           i * p.q.st + (long long)h * kD;
-        bf16* orow = reinterpret_cast<bf16*>(p.dq.p) + (long long)b * p.dq.sb + i * p.dq.st +
-                     (long long)h * kD;
-#pragma unroll
-        for (int c = 0; c < 64; ++c) acc[c] *= 2.0f * r;
-        store_unit_jacobian(acc, qrow, iq, orow);
-      }
+      const bool st_row = ok && i < s.Tq;
+      const long long ii = st_row ? i : 0;
+      const bf16* qrow = reinterpret_cast<const bf16*>(p.q.p) + (long long)b * p.q.sb +
+                         ii * p.q.st + (long long)h * kD;
+      bf16* orow = reinterpret_cast<bf16*>(p.dq.p) + (long long)b * p.dq.sb + ii * p.dq.st +
+                   (long long)h * kD;
+      // dS was stored without its 2 r
+      store_unit_jacobian_tmem(tmem + TMq_ACC + lane_off, ok && misc[3], 2.0f * r, qrow, iq,
+                               orow, st_row);
     }
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, TM_COLS);
+  if (warp == 0) tmem_dealloc(tmem, TMq_COLS);
   if (tid == 0 && *abort_flag) atomicExch(status_word(), (int)SCREEN_ERR_TIMEOUT);
 }
 
