@@ -315,15 +315,22 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     bool ok = true;
     unsigned long long live_tiles = 0;
-    for (int j = 0; j < n; ++j) {
-      const int st = j % kNS, bb = j % kSB;
+    // ring positions kept incrementally (no per-tile division); positions
+    // in 32-bit (key / query indices and offsets are < 2^31)
+    int st = 0, st_ph = 0, bb = 0, bb_ph = 0;
+    const int p0i = (int)p0, posi = (int)pos;
+    int j0i = kt0 * kBN;
+    // a tile is inside the window for every row iff its keys all lie in
+    // [p0 + kBM - 1 - dmax, p0] (causal) / [.. , p0 + dmax] (non-causal)
+    const int in_lo = p0i + kBM - 1 - dmax;
+    for (int j = 0; j < n; ++j, j0i += kBN) {
 #ifdef SCREEN_FWD_PROFILE
       const long long _tc0 = clock64();
 #endif
       {
         PROF_T0();
-        ok = mbar_wait(bar(BAR_KV_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
-             mbar_wait(bar(BAR_S_FULL + bb), (j / kSB) & 1, abort_flag, kWaitLimitNs);
+        ok = mbar_wait(bar(BAR_KV_FULL + st), st_ph, abort_flag, kWaitLimitNs) &&
+             mbar_wait(bar(BAR_S_FULL + bb), bb_ph, abort_flag, kWaitLimitNs);
         if (tid == 0) PROF_ADD(4);
       }
       // warp-uniform verdict (the TMEM accesses below are warp-collective);
@@ -362,10 +369,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool live = __any_sync(0xffffffffu, mine);
       uint32_t pk[kNC / 2];
       if (live) {
-        const long long j0 = (long long)(kt0 + j) * kBN;
-        const bool inside = (causal ? (p0 - (j0 + kBN - 1) >= 0 && p0 + kBM - 1 - j0 <= dmax)
-                                    : (p0 - (j0 + kBN - 1) >= -(long long)dmax &&
-                                       p0 + kBM - 1 - j0 <= dmax));
+        const bool inside = j0i >= in_lo && j0i + kBN - 1 <= (causal ? p0i : p0i + dmax);
         const float4* ik4 = reinterpret_cast<const float4*>(col);
         const float4* cc4 = reinterpret_cast<const float4*>(col + kBN);
         const float4* sc4 = reinterpret_cast<const float4*>(col + 2 * kBN);
@@ -381,10 +385,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         } else {
           // window edge: this row's valid columns are the interval [clo, chi]
-          const long long jg = j0 + kNC * g;   // first key of this group's columns
-          const long long clo = pos - dmax - jg, chi = causal ? pos - jg : pos + dmax - jg;
-          const int iclo = (int)(clo < 0 ? 0 : (clo > kNC ? kNC : clo));
-          const int ichi = (int)(chi < -1 ? -1 : (chi > kNC - 1 ? kNC - 1 : chi));
+          const int jg = j0i + kNC * g;   // first key of this group's columns
+          const int clo = posi - dmax - jg, chi = causal ? posi - jg : posi + dmax - jg;
+          const int iclo = clo < 0 ? 0 : (clo > kNC ? kNC : clo);
+          const int ichi = chi < -1 ? -1 : (chi > kNC - 1 ? kNC - 1 : chi);
 #pragma unroll
           for (int q4 = 0; q4 < kNC / 4; ++q4) {
             const float4 ikv = ik4[q4], ccv = cc4[q4], scv = sc4[q4];
@@ -412,6 +416,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane == 0) live_tiles += live ? 1 : 0;
       tc_fence_before();
       mbar_arrive(bar(BAR_P_FULL + bb));
+      if (++st == kNS) { st = 0; st_ph ^= 1; }
+      if (++bb == kSB) { bb = 0; bb_ph ^= 1; }
 #ifdef SCREEN_FWD_PROFILE
       if (tid == 0) atomicAdd(&g_fwd_prof[5], (unsigned long long)(clock64() - _tc0));
       if (tid == 0) atomicAdd(&g_fwd_prof[7], 1ull);

@@ -371,9 +371,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     const float2 cr2 = make_float2(crow, crow), sr2 = make_float2(srow, srow);
     const float2 half2 = make_float2(0.5f, 0.5f), twor2 = make_float2(2.f * r, 2.f * r);
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      const int st = j % kNSq;
-      ok = mbar_wait(bar(BAR_FULL + st), (j / kNSq) & 1, abort_flag, kWaitLimitNs) &&
+    // stage / phase kept incrementally; positions in 32-bit
+    int st = 0, st_ph = 0;
+    const int p0i = (int)p0, posi = (int)pos;
+    const int in_lo = p0i + kBM - 1 - dmax, in_hi = causal ? p0i : p0i + dmax;
+    int j0i = kt0 * kBN;
+    for (int j = 0; j < n; ++j, j0i += kBN) {
+      ok = mbar_wait(bar(BAR_FULL + st), st_ph, abort_flag, kWaitLimitNs) &&
            mbar_wait(bar(BAR_SD), j & 1, abort_flag, kWaitLimitNs);
       // warp-uniform verdict (the TMEM accesses below are warp-collective);
       // a warp that gives up leaves the loop alone -- every other wait on its
@@ -396,13 +400,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       // zeros, so the warps never wait on one another within a tile
       const bool live = __any_sync(0xffffffffu, mine);
       if (live) {
-        const long long j0 = (long long)(kt0 + j) * kBN;
-        const bool inside = (causal ? (p0 - (j0 + kBN - 1) >= 0 && p0 + kBM - 1 - j0 <= dmax)
-                                    : (p0 - (j0 + kBN - 1) >= -(long long)dmax &&
-                                       p0 + kBM - 1 - j0 <= dmax));
-        const long long clo_ = pos - dmax - j0 - cb, chi_ = (causal ? pos : pos + dmax) - j0 - cb;
-        const int iclo = inside ? 0 : (int)(clo_ < 0 ? 0 : (clo_ > 32 ? 32 : clo_));
-        const int ichi = inside ? 31 : (int)(chi_ < -1 ? -1 : (chi_ > 31 ? 31 : chi_));
+        const bool inside = j0i >= in_lo && j0i + kBN - 1 <= in_hi;
+        const int clo_ = posi - dmax - j0i - cb, chi_ = (causal ? posi : posi + dmax) - j0i - cb;
+        const int iclo = inside ? 0 : (clo_ < 0 ? 0 : (clo_ > 32 ? 32 : clo_));
+        const int ichi = inside ? 31 : (chi_ < -1 ? -1 : (chi_ > 31 ? 31 : chi_));
         const float4* ik4 = reinterpret_cast<const float4*>(col + cb);
         const float4* iv4 = reinterpret_cast<const float4*>(col + kBN + cb);
         const float4* cc4 = reinterpret_cast<const float4*>(col + 2 * kBN + cb);
@@ -453,6 +454,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(BAR_P));
+      if (++st == kNSq) { st = 0; st_ph ^= 1; }
     }
     // epilogue (warpgroup 0): dQ -> normalisation Jacobian -> dq
     if (g == 0) {
@@ -739,17 +741,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       // zeros, so the warps never wait on one another within a tile
       const bool live = __any_sync(0xffffffffu, mine);
       if (live) {
-        const long long pq0 = (long long)(qt0 + j) * kBN + s.q_offset;
+        // positions in 32-bit (key / query indices and offsets are < 2^31)
+        const int pq0 = (qt0 + j) * kBN + (int)s.q_offset, j0i = (int)j0, jr = (int)jrow;
         // d = p - j over the tile: [pq0 - (j0 + 127), pq0 + 63 - j0]
-        const long long dlo = pq0 - (j0 + kBM - 1), dhi = pq0 + kBN - 1 - j0;
-        const bool inside = causal ? (dlo >= 0 && dhi <= dmax)
-                                   : (dlo >= -(long long)dmax && dhi <= dmax);
+        const int dlo = pq0 - (j0i + kBM - 1), dhi = pq0 + kBN - 1 - j0i;
+        const bool inside = causal ? (dlo >= 0 && dhi <= dmax) : (dlo >= -dmax && dhi <= dmax);
         // this row's valid query columns: p - j in [0, dmax] (causal) or [-dmax, dmax]
-        const long long clo_ = (causal ? jrow : jrow - dmax) - pq0 - cb;
-        const long long chi_ = jrow + dmax - pq0 - cb;
-        const int iclo = inside ? 0 : (int)(clo_ < 0 ? 0 : (clo_ > 32 ? 32 : clo_));
-        const int ichi = inside ? 31 : (int)(chi_ < -1 ? -1 : (chi_ > 31 ? 31 : chi_));
-        const float relb = (float)(jrow - pq0 - cb);   // rel = j - p = relb - c
+        const int clo_ = (causal ? jr : jr - dmax) - pq0 - cb;
+        const int chi_ = jr + dmax - pq0 - cb;
+        const int iclo = inside ? 0 : (clo_ < 0 ? 0 : (clo_ > 32 ? 32 : clo_));
+        const int ichi = inside ? 31 : (chi_ < -1 ? -1 : (chi_ > 31 ? 31 : chi_));
+        const float relb = (float)(jr - pq0 - cb);   // rel = j - p = relb - c
         const float4* iq4 = reinterpret_cast<const float4*>(col + cb);
         const float4* cv4 = reinterpret_cast<const float4*>(col + kBN + cb);
         const float4* sv4 = reinterpret_cast<const float4*>(col + 2 * kBN + cb);
