@@ -402,6 +402,207 @@ def run_prefill(args, rank, world):
         dist.destroy_process_group()
 
 
+def run_lm(args, rank, world):
+    """cfg2: one training step of MultiscreenLM(50257, d_model=256, 4 heads,
+    4 layers, max_seq_len=512) on batch 16 x T=512 synthetic token ids per
+    GPU: bf16 autocast forward + backward, fp32 master weights, fused AdamW;
+    data parallel (DDP, NCCL all-reduce of the gradients) for N > 1."""
+    import importlib
+    ms = importlib.import_module(PKG)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    B, T, V = 16, 512, 50257
+    torch.manual_seed(0)
+    model = ms.MultiscreenLM(V, d_model=256, num_heads=4, num_layers=4, max_seq_len=T).to(dev)
+    n_params = sum(p.numel() for p in model.parameters())
+    net = model
+    if dist is not None:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local])
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, fused=True)
+    g = torch.Generator().manual_seed(100 + rank)
+    ids_host = torch.randint(0, V, (B, T), generator=g).pin_memory()
+    ids = ids_host.to(dev)
+
+    def step(inp):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = net(inp, labels=inp)
+        out["loss"].backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return out["loss"]
+
+    for _ in range(args.warmup):
+        step(ids)
+    torch.cuda.synchronize()
+    clk = ClockSampler(local)
+    clk.__enter__()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for a, b in evs:
+        a.record()
+        step(ids)
+        b.record()
+    torch.cuda.synchronize()
+    total = sum(a.elapsed_time(b) for a, b in evs)
+    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    ids_dev = torch.empty_like(ids)
+    e2e = []
+    for _ in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ids_dev.copy_(ids_host, non_blocking=True)
+        loss = step(ids_dev)
+        loss_host.copy_(loss.detach().float().view(1), non_blocking=True)
+        b.record()
+        e2e.append((a, b))
+    torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e)
+    if dist is not None:
+        t = torch.tensor([total, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total, e2e_ms = (float(x) for x in t.tolist())
+    ms_per = total / args.steps
+    toks = B * T * world
+    # training FLOPs per step: 6 x parameters x tokens for the dense layers
+    # (lm_head tied to the embedding counts once) + windowed attention x 3
+    w_def = torch.exp(torch.linspace(0, math.log(255), 4)) + 1.0
+    attn = 3 * 4 * windowed_pairs(w_def, T) * B * 2 * (2 * 64)
+    dense = 6.0 * (n_params - 512 * 256) * B * T
+    pk, kind = peaks()
+    peak = float(pk.get("bf16_tflops_sustained", pk["bf16_tflops"]))
+    tf = (dense + attn) / (ms_per / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import screening_oracle as oracle
+        nt = os.cpu_count() or 1
+        torch.set_num_threads(nt)
+        torch.manual_seed(0)
+        om = oracle.OracleLM(V, d_model=256, num_heads=4, num_layers=4, max_seq_len=T,
+                             windowed=True)
+        oopt = torch.optim.AdamW(om.parameters(), lr=3e-4)
+        oid = ids_host[:1].clone()
+        t0 = time.perf_counter()
+        out = om(oid, labels=oid)
+        out["loss"].backward()
+        oopt.step()
+        dt = time.perf_counter() - t0
+        cpu = {"value": T / dt, "unit": "tokens/s", "cores": nt, "kind": "port",
+               "sample": f"oracle LM training step, 1 sequence x T={T} fp32, {dt:.2f} s"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MultiscreenLM training step tokens/s (cfg2: 50257 x 256 x 4 heads x 4 "
+                      "layers, B=16, T=512, bf16)",
+            "value": toks / (ms_per / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"cfg2: MultiscreenLM(50257, 256, 4, 4, max_seq_len=512), "
+                                   f"{n_params} parameters, batch 16/GPU, T=512, bf16 autocast, "
+                                   f"fp32 master weights, fused AdamW",
+                       "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
+                       "l2": "no flush: weights + optimizer state + activations > L2"},
+            "roofline": {"bound": "tensor", "kernel": "whole training step", "achieved": tf / world,
+                         "peak": peak, "unit": "TFLOP/s", "frac": tf / world / peak,
+                         "peak_kind": kind + " sustained", "traffic": None,
+                         "per": "GPU"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": toks / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": ids_host.numel() * 8, "d2h_bytes_per_step": 4},
+            "clocks": clk.summary(),
+        }), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_generate(args, rank, world):
+    """cfg5: MultiscreenLM(50257, 1024, 16, 12) at random init (w = 2..256 per
+    head), 4 prompts of --prompt-len random tokens per GPU, 256 greedy new
+    tokens through the paged KV cache.  Prefill and decode are timed apart
+    (CUDA events); the decode loop is one CUDA-graph replay per token plus
+    greedy sampling, exactly as generate() runs it.  No collective: every rank
+    serves its own 4 sequences."""
+    import importlib
+    ms = importlib.import_module(PKG)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    B, T0, NEW, V = 4, args.prompt_len, 256, 50257
+    torch.manual_seed(0)
+    model = ms.MultiscreenLM(V, d_model=1024, num_heads=16, num_layers=12,
+                             max_seq_len=T0 + NEW).to(dev).to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(7 + rank)
+    prompt = torch.randint(0, V, (B, T0), generator=g).to(dev)
+
+    def one():
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        with torch.no_grad():
+            ev[0].record()
+            cache = model.make_cache(B, T0 + NEW)
+            state = model._decode_state()
+            logits = model.prefill(prompt, cache)
+            ev[1].record()
+            graph, g_tok, g_pos, g_logits = model._capture_decode(B, T0, cache, state)
+            ev[2].record()
+            toks = []
+            for step in range(NEW):
+                nxt = logits.argmax(-1, keepdim=True)
+                toks.append(nxt)
+                if step + 1 < NEW:
+                    g_tok.copy_(nxt)
+                    g_pos.fill_(T0 + step)
+                    graph.replay()
+                    logits = g_logits
+            ev[3].record()
+        torch.cuda.synchronize()
+        return ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3]), torch.cat(toks, 1)
+
+    for _ in range(args.warmup):
+        one()
+    clk = ClockSampler(local)
+    clk.__enter__()
+    if dist is not None:
+        dist.barrier()
+    runs = [one() for _ in range(args.steps)]
+    clk.__exit__(None, None, None)
+    pre = sum(r[0] for r in runs) / len(runs)
+    dec = sum(r[1] for r in runs) / len(runs)
+    if dist is not None:
+        t = torch.tensor([pre, dec], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pre, dec = (float(x) for x in t.tolist())
+    if rank == 0:
+        print(json.dumps({
+            "metric": "generate() decode tokens/s (cfg5: MultiscreenLM 1024 x 16 x 12, 100K-token "
+                      "prompts, 256 greedy tokens, bf16 paged KV cache)",
+            "value": B * NEW * world / (dec / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dec,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"cfg5: 4 sequences/GPU x {T0}-token random prompts, "
+                                   f"{NEW} new tokens (top_k=1), random init (w = 2..256)",
+                       "global_batch": B * world, "seq_len": T0, "parallelism": f"batch x{world}",
+                       "decode": "one CUDA-graph replay per token (12 layers + lm_head)"},
+            "prefill_ms": pre, "prefill_tokens_per_s": B * T0 * world / (pre / 1e3),
+            "decode_ms_per_token": dec / NEW,
+            "clocks": clk.summary(),
+        }), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -411,11 +612,12 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH, help="per-GPU batch (profiling: smaller)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-reps", type=int, default=5)
-    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "decode", "prefill"],
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "decode", "prefill", "lm", "generate"],
                     help="cfg3: the headline fwd+bwd step; decode: the paged-cache decode "
                          "kernel's HBM roofline (cfg5 shapes, long window)")
     ap.add_argument("--decode-window", type=int, default=100_000)
     ap.add_argument("--prefill-len", type=int, default=131072)
+    ap.add_argument("--prompt-len", type=int, default=100_000)
     ap.add_argument("--decode-splits", type=int, default=0,
                     help="override the cache's split count (0: its own heuristic)")
     ap.add_argument("--profile-only", action="store_true",
@@ -434,6 +636,12 @@ def main():
         return
     if args.workload == "prefill":
         run_prefill(args, rank, world)
+        return
+    if args.workload == "lm":
+        run_lm(args, rank, world)
+        return
+    if args.workload == "generate":
+        run_generate(args, rank, world)
         return
 
     import importlib

@@ -111,20 +111,47 @@ class MultiscreenLM(nn.Module):
         return self.lm_head(self.norm(x[:, -1:]))[:, -1]
 
     @torch.no_grad()
-    def decode_step(self, tokens: torch.Tensor, position: int, cache: PagedKVCache,
+    def decode_step(self, tokens: torch.Tensor, position, cache: PagedKVCache,
                     state: dict | None = None) -> torch.Tensor:
-        """tokens (B,1) at absolute `position`; returns logits (B,V)."""
+        """tokens (B,1) at absolute `position` (an int, or an int32 (B,) device
+        tensor); returns logits (B,V).  With a tensor position the step has no
+        host-side dependence on the position, so it can be captured once in a
+        CUDA graph and replayed for every generated token."""
         B = tokens.shape[0]
         dev = tokens.device
         if state is None:
             state = self._decode_state()
-        pos_t = torch.full((B,), position, dtype=torch.int32, device=dev)
-        x = self.token_emb(tokens) + self.pos_emb.weight[position].view(1, 1, -1)
+        if isinstance(position, torch.Tensor):
+            pos_t = position
+        else:
+            pos_t = torch.full((B,), position, dtype=torch.int32, device=dev)
+        x = self.token_emb(tokens) + self.pos_emb(pos_t.long()).unsqueeze(1)
         for li, blk in enumerate(self.blocks):
             wqkv, r, w = state["layers"][li]
             x = x + blk.attn.decode_step(blk.norm1(x), cache, li, pos_t, pos_t + 1, wqkv, r, w)
             x = x + blk.ffn(blk.norm2(x))
         return self.lm_head(self.norm(x))[:, -1]
+
+    @torch.no_grad()
+    def _capture_decode(self, batch: int, first_position: int, cache: PagedKVCache,
+                        state: dict):
+        """One decode step (every layer + lm_head) captured in a CUDA graph with
+        static inputs `tokens` (B,1) and `pos` (B,) int32.  The warm-up steps
+        run at `first_position`, whose cache slot the first real step
+        overwrites before reading it."""
+        dev = self.token_emb.weight.device
+        tokens = torch.zeros(batch, 1, dtype=torch.long, device=dev)
+        pos = torch.full((batch,), first_position, dtype=torch.int32, device=dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                self.decode_step(tokens, pos, cache, state)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            logits = self.decode_step(tokens, pos, cache, state)
+        return graph, tokens, pos, logits
 
     def _decode_state(self) -> dict:
         layers = []
@@ -136,8 +163,11 @@ class MultiscreenLM(nn.Module):
 
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 100,
-                 temperature: float = 1.0, top_k: int | None = None) -> torch.Tensor:
-        """(B,T) prompt -> (B, T + max_new_tokens), sampling as model.py:134-140."""
+                 temperature: float = 1.0, top_k: int | None = None,
+                 cuda_graph: bool = True) -> torch.Tensor:
+        """(B,T) prompt -> (B, T + max_new_tokens), sampling as model.py:134-140.
+        On CUDA the per-token decode step is one CUDA-graph replay
+        (`cuda_graph=False`: eager launches, same numbers)."""
         self.eval()
         if max_new_tokens <= 0:
             return input_ids
@@ -148,6 +178,9 @@ class MultiscreenLM(nn.Module):
         cache = self.make_cache(B, T0 + max_new_tokens)
         state = self._decode_state()
         logits = self.prefill(input_ids, cache)
+        graph = None
+        if cuda_graph and input_ids.is_cuda and max_new_tokens > 1:
+            graph, g_tok, g_pos, g_logits = self._capture_decode(B, T0, cache, state)
         for step in range(max_new_tokens):
             logits = logits / temperature
             if top_k is not None:
@@ -157,5 +190,11 @@ class MultiscreenLM(nn.Module):
             next_token = torch.multinomial(probs, num_samples=1)
             input_ids = torch.cat([input_ids, next_token], dim=1)
             if step + 1 < max_new_tokens:
-                logits = self.decode_step(next_token, T0 + step, cache, state)
+                if graph is not None:
+                    g_tok.copy_(next_token)
+                    g_pos.fill_(T0 + step)
+                    graph.replay()
+                    logits = g_logits.clone()
+                else:
+                    logits = self.decode_step(next_token, T0 + step, cache, state)
         return input_ids
