@@ -744,7 +744,6 @@ def main():
         return statistics.median(out)
 
     kt = {
-        "norms": time_call(lambda: L.screen_fwd(q, k, v, rr, ww, True, stages=1), args.kernel_reps),
         "fwd": time_call(lambda: L.screen_fwd(q, k, v, rr, ww, True, norms=(nq, nk, nv), stages=2),
                          args.kernel_reps),
         "bwd_prologue": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww,

@@ -515,7 +515,18 @@ __global__ void tc_prep_kernel(Rows q, Rows k, Rows v, int B, int Tq, int Tk, in
     const bool isq = row < rows_q;
     const long long rr = !valid ? 0 : (isq ? row : row - rows_q);
     const int T = isq ? Tq : Tk;
-    const long long hh = rr % H, t = (rr / H) % T, bb = rr / ((long long)H * T);
+    long long hh, t, bb;
+    if (total < (1ll << 31)) {
+      // 32-bit division: a 64-bit one per row costs more than the row's bytes
+      const unsigned r32 = (unsigned)rr, bt = r32 / (unsigned)H;
+      hh = r32 - bt * (unsigned)H;
+      t = bt % (unsigned)T;
+      bb = bt / (unsigned)T;
+    } else {
+      hh = rr % H;
+      t = (rr / H) % T;
+      bb = rr / ((long long)H * T);
+    }
     // a = the q row (q part) or the k row; c = the v row (k part) or zeros
     uint4 ua = make_uint4(0, 0, 0, 0), uc = make_uint4(0, 0, 0, 0);
     if (valid && isq) {

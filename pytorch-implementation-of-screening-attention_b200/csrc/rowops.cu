@@ -181,10 +181,22 @@ __global__ void tanhnorm_grad_from_y_kernel(const T* __restrict__ y, const float
   long long rows = (long long)B * T_ * H;
   bool valid = row < rows;
   long long rr = valid ? row : 0;
-  long long h = rr % H, t = (rr / H) % T_, b = rr / ((long long)H * T_);
+  // dy row offset: rr * D when dy is contiguous (the usual case), else
+  // (b, t, h) from rr -- in 32-bit when the row count allows (a 64-bit
+  // division per thread costs more than the row's memory traffic)
+  long long doff;
+  if (dy_st == (long long)H * D && dy_sb == (long long)T_ * H * D) {
+    doff = rr * D;
+  } else if (rows < (1ll << 31)) {
+    const unsigned r32 = (unsigned)rr, hh = r32 % (unsigned)H, bt = r32 / (unsigned)H;
+    doff = (long long)(bt / (unsigned)T_) * dy_sb + (long long)(bt % (unsigned)T_) * dy_st +
+           (long long)hh * D;
+  } else {
+    const long long h = rr % H, t = (rr / H) % T_, b = rr / ((long long)H * T_);
+    doff = b * dy_sb + t * dy_st + h * D;
+  }
   float4 yv = valid ? Vec4<T>::load(y + rr * D + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 d = valid ? Vec4<T>::load(dy + b * dy_sb + t * dy_st + h * D + lane * 4)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 d = valid ? Vec4<T>::load(dy + doff + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
   float yd = group_sum<Gl>(yv.x * d.x + yv.y * d.y + yv.z * d.z + yv.w * d.w);
   float nraw = valid ? no[rr] : 0.f;
   float g = tanhnorm_scale(nraw, eps);
@@ -206,6 +218,53 @@ __global__ void tanhnorm_grad_from_y_kernel(const T* __restrict__ y, const float
   }
 }
 
+// bf16 rows split into hi / lo planes (the tensor-core path): 16-byte
+// accesses, D / 8 lanes per row, contiguous dy
+template <int D>
+__global__ void __launch_bounds__(256) tanhnorm_grad_split_bf16_kernel(
+    const __nv_bfloat16* __restrict__ y, const float* __restrict__ no,
+    const __nv_bfloat16* __restrict__ dy, __nv_bfloat16* __restrict__ G, long long rows,
+    float eps) {
+  constexpr int L = D / 8;
+  constexpr int RPB = 256 / L;
+  const long long row = (long long)blockIdx.x * RPB + threadIdx.x / L;
+  const int lane = threadIdx.x % L;
+  const bool valid = row < rows;
+  const long long off = (valid ? row : 0) * D + lane * 8;
+  uint4 yu = make_uint4(0, 0, 0, 0), du = make_uint4(0, 0, 0, 0);
+  if (valid) {
+    yu = *reinterpret_cast<const uint4*>(y + off);
+    du = *reinterpret_cast<const uint4*>(dy + off);
+  }
+  const uint32_t yw[4] = {yu.x, yu.y, yu.z, yu.w}, dw[4] = {du.x, du.y, du.z, du.w};
+  float yf[8], df[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 a = unpack_bf16(yw[e]), b = unpack_bf16(dw[e]);
+    yf[2 * e] = a.x; yf[2 * e + 1] = a.y;
+    df[2 * e] = b.x; df[2 * e + 1] = b.y;
+  }
+  float yd = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) yd = fmaf(yf[e], df[e], yd);
+  yd = group_sum<L>(yd);
+  const float nraw = valid ? no[row] : 0.f;
+  const float g = tanhnorm_scale(nraw, eps);
+  const float k = (nraw > eps) ? tanhnorm_bwd_coef(nraw) * yd : 0.f;
+  if (!valid) return;
+  uint32_t hw[4], lw[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float g0 = fmaf(g, df[2 * e], k * yf[2 * e]);
+    const float g1 = fmaf(g, df[2 * e + 1], k * yf[2 * e + 1]);
+    hw[e] = pack_bf16(g0, g1);
+    const float2 hf = unpack_bf16(hw[e]);
+    lw[e] = pack_bf16(g0 - hf.x, g1 - hf.y);
+  }
+  *reinterpret_cast<uint4*>(G + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  *reinterpret_cast<uint4*>(G + rows * D + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+}
+
 template <typename T, int D>
 static void launch_grad_from_y(const void* y, const float* no, const void* dy, long long sb,
                                long long st, void* G, bool split, int B, int T_, int H, float eps,
@@ -213,6 +272,15 @@ static void launch_grad_from_y(const void* y, const float* no, const void* dy, l
   constexpr int RPB = 256 / (D / 4);
   long long rows = (long long)B * T_ * H;
   if (rows == 0) return;
+  if constexpr (sizeof(T) == 2 && D % 8 == 0 && D <= 256) {
+    if (split && st == (long long)H * D && sb == (long long)T_ * H * D &&
+        (reinterpret_cast<uintptr_t>(dy) & 15) == 0) {
+      constexpr int RPB8 = 256 / (D / 8);
+      tanhnorm_grad_split_bf16_kernel<D><<<(unsigned)((rows + RPB8 - 1) / RPB8), 256, 0, s>>>(
+          (const __nv_bfloat16*)y, no, (const __nv_bfloat16*)dy, (__nv_bfloat16*)G, rows, eps);
+      return;
+    }
+  }
   tanhnorm_grad_from_y_kernel<T, D><<<(unsigned)((rows + RPB - 1) / RPB), 256, 0, s>>>(
       (const T*)y, no, (const T*)dy, sb, st, G, split, B, T_, H, eps);
 }
