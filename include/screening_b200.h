@@ -108,6 +108,9 @@ SCREEN_API size_t screen_fwd_workspace_size(const screen_fwd_args* a);
  * here the unit-normalisation and TanhNorm are fused in. */
 SCREEN_API int screen_fwd(const screen_fwd_args* a, screen_stream_t stream);
 
+/* screen_bwd stage flag: fixed-order (bitwise reproducible) dq */
+#define SCREEN_BWD_DETERMINISTIC 16
+
 /* ------------------------------------------------------------------------ */
 /* Backward.                                                                 */
 /* ------------------------------------------------------------------------ */
@@ -116,7 +119,12 @@ typedef struct screen_bwd_args {
   int32_t B, H, Tq, Tk, D;
   int32_t causal;
   int32_t stages;                /* 0 = all; else bitmask: 1 TanhNorm grad,   */
-                                 /*   2 dq, 4 dk/dv, 8 dr/dw reduce           */
+                                 /*   2 dq, 4 dk/dv, 8 dr/dw reduce; with    */
+                                 /*   SCREEN_BWD_DETERMINISTIC (16) set, dq  */
+                                 /*   is summed in a fixed order (else the   */
+                                 /*   bf16 D=64 path forms dq inside the     */
+                                 /*   dk/dv kernel with fp32 reductions, run */
+                                 /*   by stage 4; stage 2 then adds nothing) */
   int64_t q_offset;
   float eps;
   int32_t _pad0;

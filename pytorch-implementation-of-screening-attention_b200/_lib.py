@@ -253,6 +253,11 @@ def row_norms(x, eps=1e-8):
     return nx
 
 
+# screen_bwd stage flag (include/screening_b200.h): fixed-order dq.  Set
+# whenever torch.use_deterministic_algorithms(True) is in effect.
+SCREEN_BWD_DETERMINISTIC = 16
+
+
 def screen_bwd(q, k, v, nq, nk, nv, y, no, dy, r, w, causal=True, key_padding_mask=None,
                eps=1e-8, q_offset=0, out=None, stages=0):
     """Backward of screen_fwd.  Returns dq, dk, dv ((B,T,H,D); written into
@@ -275,7 +280,9 @@ def screen_bwd(q, k, v, nq, nk, nv, y, no, dy, r, w, causal=True, key_padding_ma
     dr = torch.empty(H, dtype=torch.float32, device=dev)
     dw = torch.empty(H, dtype=torch.float32, device=dev)
     a = BwdArgs(dtype=_dtype_code(q), B=B, H=H, Tq=Tq, Tk=Tk, D=D, causal=int(bool(causal)),
-                stages=int(stages), q_offset=int(q_offset), eps=float(eps),
+                stages=int(stages) | (SCREEN_BWD_DETERMINISTIC
+                                      if torch.are_deterministic_algorithms_enabled() else 0),
+                q_offset=int(q_offset), eps=float(eps),
                 q=_ptr(q), q_sb=q.stride(0), q_st=q.stride(1),
                 k=_ptr(k), k_sb=k.stride(0), k_st=k.stride(1),
                 v=_ptr(v), v_sb=v.stride(0), v_st=v.stride(1),

@@ -189,7 +189,9 @@ int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
   if (!a) return SCREEN_ERR_INVALID_ARG;
   int st = common_checks(a->dtype, a->B, a->H, a->Tq, a->Tk, a->D);
   if (st) return st;
-  const int stages = a->stages ? a->stages : 15;
+  int stages = a->stages & 15;
+  if (!stages) stages = 15;
+  stages |= a->stages & SCREEN_BWD_DETERMINISTIC;
   if (a->H > 0 && (!a->r || !a->w || !a->dr || !a->dw)) return SCREEN_ERR_INVALID_ARG;
   const bool nq = (long long)a->B * a->H * a->Tq > 0, nk = (long long)a->B * a->H * a->Tk > 0;
   if (nq && (!a->q || !a->nq || !a->y || !a->no || !a->dy || !a->dq)) return SCREEN_ERR_INVALID_ARG;

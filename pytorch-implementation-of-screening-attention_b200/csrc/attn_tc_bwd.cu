@@ -32,8 +32,7 @@ constexpr int kCompute = 256;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t TILE_A = kBM * kD * 2;  // 128-row operand tile, 16 KB
 constexpr uint32_t TILE_B = kBN * kD * 2;  // 64-row tile, 8 KB
-constexpr uint32_t TM_S = 0, TM_DP = 128, TM_P1 = 256, TM_P2 = 320, TM_ACC1 = 384,
-                   TM_ACC2 = 448, TM_COLS = 512;
+constexpr uint32_t TM_COLS = 512;
 
 struct Aux {
   const float* iqT;   // [B*H][Tqp] 1/|q| (0 past Tq)
@@ -488,17 +487,31 @@ namespace kv {
 constexpr uint32_t OFF_K = 0, OFF_V = TILE_A;
 constexpr uint32_t OFF_Q = 2 * TILE_A;                 // per stage: Q | G_hi | G_lo (8 KB each)
 constexpr uint32_t STAGE = 3 * TILE_B;
-constexpr uint32_t OFF_COL = OFF_Q + kNS * STAGE;       // per stage iq | cos | sin [64] + meta
+// dS^T staging for the fused dQ MMA: two buffers, each a pair of query tiles
+// [128 keys][64 queries] bf16 (SW128), 16 KB apart (the operand's LBO)
+constexpr uint32_t OFF_STG = OFF_Q + kNS * STAGE;
+constexpr uint32_t STG_PAIR = 2 * TILE_A;
+constexpr uint32_t OFF_COL = OFF_STG + 2 * STG_PAIR;    // per stage iq | cos | sin [64] + meta
 constexpr uint32_t COLB = 3 * kBN * 4 + 16;
 constexpr uint32_t OFF_TAB = OFF_COL + kNS * COLB;
 constexpr uint32_t OFF_RED = OFF_TAB + 2 * kBN * 4;     // [2][8] dr / dw warp sums
 constexpr uint32_t OFF_BAR = OFF_RED + 64 * 4;
 constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNS, BAR_SD = BAR_EMPTY + kNS,
-              BAR_SDFREE = BAR_SD + 2, BAR_P = BAR_SDFREE + 2, BAR_DONE = BAR_P + 2;
-constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 16;
-constexpr uint32_t SMEM = (OFF_MISC + 64 + 1024 > 120 * 1024) ? OFF_MISC + 64 + 1024 : 120 * 1024;
+              BAR_P = BAR_SD + 2, BAR_DONE = BAR_P + 2, BAR_DQF = BAR_DONE + 1,
+              BAR_DQE = BAR_DQF + 2, BAR_COUNT = BAR_DQE + 2;
+constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 24;
+static_assert(BAR_COUNT <= 24, "barrier space");
+constexpr uint32_t SMEM = OFF_MISC + 64 + 1024;
+static_assert(SMEM <= 227 * 1024, "shared memory");
+// TMEM: S and dP double-buffered; alpha / dS (bf16) written over the S / dP
+// columns they came from; dV, dK and two dQ accumulators -> 512 columns
+constexpr uint32_t TK_S = 0, TK_DP = 128, TK_ACCV = 256, TK_ACCK = 320, TK_ACCQ = 384;
 }  // namespace kv
 
+// kFuse: dQ is computed here too (dQ += dS K on the tensor cores per pair of
+// query tiles, added into an fp32 accumulator with vector reductions);
+// otherwise tc_bwd_dq_kernel computes it (deterministic order)
+template <bool kFuse>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_bwd_kv_kernel(AttnShape s, BwdPtrs p, Aux ax, const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmK,
@@ -542,8 +555,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(BAR_SD + i), 1);
-      mbar_init(bar(BAR_SDFREE + i), kCompute);
       mbar_init(bar(BAR_P + i), kCompute);
+      mbar_init(bar(BAR_DQF + i), 1);
+      mbar_init(bar(BAR_DQE + i), kCompute);
     }
     mbar_init(bar(BAR_DONE), 2);
     misc[1] = misc[2] = misc[3] = misc[4] = 0;
@@ -633,47 +647,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(kBM, kBN, 0, 0);
       constexpr uint32_t idMN = idesc_bf16(kBM, kD, 0, 1);
+      constexpr uint32_t idQ = idesc_bf16(kBM, kD, 1, 1);   // A = dS^T staging, MN-major
       bool started = false, ok = mbar_wait(bar(BAR_A), 0, abort_flag, kWaitLimitNs);
+      int pair_i = 0;   // pairs of query tiles whose dQ has been issued
       auto issue_kv = [&](int jj) -> bool {
         const int bb = jj & 1, st = jj % kNS;
         if (!mbar_wait(bar(BAR_P + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
         tc_fence_after();
-        {
-          const uint32_t qb = base + OFF_Q + st * STAGE, ghb = qb + TILE_B;
+        // alpha_j / dS_j sit in the first 16 columns of each compute group's
+        // 32-column half of the S / dP buffer
+        const uint32_t qb = base + OFF_Q + st * STAGE, ghb = qb + TILE_B;
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            mma_ts(tmem + TM_ACC1, tmem + TM_P1 + 32 * bb + 8 * kk,
-                   desc_sw128(ghb + kk * 16 * 128, TILE_B, 1024), idMN,
-                   (started || kk > 0) ? 1u : 0u);
-            mma_ts(tmem + TM_ACC2, tmem + TM_P2 + 32 * bb + 8 * kk,
-                   desc_sw128(qb + kk * 16 * 128, TILE_B, 1024), idMN,
-                   (started || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint32_t pcol = 64 * bb + (kk >> 1) * 32 + (kk & 1) * 8;
+          mma_ts(tmem + TK_ACCV, tmem + TK_S + pcol, desc_sw128(ghb + kk * 16 * 128, TILE_B, 1024),
+                 idMN, (started || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + TK_ACCK, tmem + TK_DP + pcol, desc_sw128(qb + kk * 16 * 128, TILE_B, 1024),
+                 idMN, (started || kk > 0) ? 1u : 0u);
+        }
+        started = true;
+        if constexpr (kFuse) {
+          const int qt = qt0 + jj;
+          if ((qt & 1) || jj == n - 1) {
+            // the pair of query tiles (qt & ~1, qt | 1) is complete:
+            // dQ[128 q][64 d] = dS (A: [key][q] staging, MN-major, M = 128) x K
+            const int buf = pair_i & 1;
+            if (pair_i >= 2 &&
+                !mbar_wait(bar(BAR_DQE + buf), ((pair_i >> 1) - 1) & 1, abort_flag, kWaitLimitNs))
+              return false;
+            tc_fence_after();
+            const uint32_t stg = base + OFF_STG + buf * STG_PAIR;
+#pragma unroll
+            for (int kk = 0; kk < kBM / 16; ++kk)
+              mma_ss(tmem + TK_ACCQ + 64 * buf, desc_sw128(stg + kk * 16 * 128, TILE_A, 1024),
+                     desc_sw128(base + OFF_K + kk * 16 * 128, TILE_A, 1024), idQ,
+                     kk > 0 ? 1u : 0u);
+            mma_commit(bar(BAR_DQF + buf));
+            ++pair_i;
           }
-          started = true;
         }
         mma_commit(bar(BAR_EMPTY + st));
         return true;
       };
       for (int j = 0; j < n && ok; ++j) {
         const int st = j % kNS, bb = j & 1;
+        // buffer bb held alpha / dS of tile j - 2, read by MMAs issued
+        // before these (in-order execution)
         ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
-        if (ok && j >= 2)
-          ok = mbar_wait(bar(BAR_SDFREE + bb), ((j >> 1) - 1) & 1, abort_flag, kWaitLimitNs);
         if (!ok) break;
         tc_fence_after();
         fence_proxy_async_smem();
         const uint32_t qb = base + OFF_Q + st * STAGE, ghb = qb + TILE_B, glb = qb + 2 * TILE_B;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TM_S + kBN * bb, desc_sw128(base + OFF_K + kk * 32, 16, 1024),
+          mma_ss(tmem + TK_S + kBN * bb, desc_sw128(base + OFF_K + kk * 32, 16, 1024),
                  desc_sw128(qb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TM_DP + kBN * bb, desc_sw128(base + OFF_V + kk * 32, 16, 1024),
+          mma_ss(tmem + TK_DP + kBN * bb, desc_sw128(base + OFF_V + kk * 32, 16, 1024),
                  desc_sw128(ghb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TM_DP + kBN * bb, desc_sw128(base + OFF_V + kk * 32, 16, 1024),
+          mma_ss(tmem + TK_DP + kBN * bb, desc_sw128(base + OFF_V + kk * 32, 16, 1024),
                  desc_sw128(glb + kk * 32, 16, 1024), idS, 1u);
         mma_commit(bar(BAR_SD + bb));
         if (j >= 1) ok = issue_kv(j - 1);
@@ -712,10 +747,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float2 half2 = make_float2(0.5f, 0.5f), twor2 = make_float2(2.f * r, 2.f * r);
     const float2 iv2 = make_float2(iv, iv), ik2 = make_float2(ik, ik);
     const float2 m1 = make_float2(-1.f, -1.f);
+    // dS for the dQ MMA: dq^ = sum_j dS k^ = sum_j dS (1/|k|) K, dS = (G v)(1/|v|) m 2 a r
+    const float rq_f = 2.0f * r * iv * ik;
+    const float2 rqf2 = make_float2(rq_f, rq_f);
     float2 accr2 = make_float2(0.f, 0.f), accw2 = make_float2(0.f, 0.f);
     bool ok = true;
+    int pair_c = -1;    // pair of query tiles this tile belongs to (CTA-local count)
+    int todo = -1;      // a complete pair whose dQ is yet to be drained
+    int todo_qt = 0;
+    uint32_t* stg_words = reinterpret_cast<uint32_t*>(gbase + OFF_STG);
+    // drain pair pp: dQ accumulator rows (this thread: query row t of the
+    // pair, columns [32 g, 32 g + 32)) added into the fp32 accumulator
+    auto drain = [&](int pp, int pqt) -> bool {
+      const int buf = pp & 1;
+      bool okd = mbar_wait(bar(BAR_DQF + buf), (pp >> 1) & 1, abort_flag, kWaitLimitNs);
+      okd = __all_sync(0xffffffffu, okd);
+      if (!okd) return false;
+      tc_fence_after();
+      uint32_t dqv[32];
+      tmem_ld32(tmem + TK_ACCQ + 64 * buf + cb + lane_off, dqv);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(bar(BAR_DQE + buf));
+      const long long qrow = (long long)(pqt & ~1) * kBN + t;
+      if (qrow < s.Tq) {
+        float* dst = p.dq_acc + (((long long)b * s.Tq + qrow) * s.H + h) * kD + cb;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * e),
+                       "f"(__uint_as_float(dqv[4 * e])), "f"(__uint_as_float(dqv[4 * e + 1])),
+                       "f"(__uint_as_float(dqv[4 * e + 2])), "f"(__uint_as_float(dqv[4 * e + 3]))
+                       : "memory");
+      }
+      return true;
+    };
+    // this thread's 4 chunks (16 B each) of row t in half `hf` of staging buffer `buf`
+    auto stg_row = [&](int buf, int hf) -> uint4* {
+      return reinterpret_cast<uint4*>(gbase + OFF_STG + buf * STG_PAIR + hf * TILE_A + t * 128);
+    };
+    (void)stg_words;
     for (int j = 0; j < n; ++j) {
       const int st = j % kNS, bb = j & 1;
+      const int qt = qt0 + j;
+      if (kFuse && (j == 0 || (qt & 1) == 0)) ++pair_c;
       ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
            mbar_wait(bar(BAR_SD + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
       // warp-uniform verdict (the TMEM accesses below are warp-collective);
@@ -725,11 +799,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       uint32_t sv[32], dv[32];
-      tmem_ld32(tmem + TM_S + kBN * bb + cb + lane_off, sv);
-      tmem_ld32(tmem + TM_DP + kBN * bb + cb + lane_off, dv);
+      tmem_ld32(tmem + TK_S + kBN * bb + cb + lane_off, sv);
+      tmem_ld32(tmem + TK_DP + kBN * bb + cb + lane_off, dv);
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar(BAR_SDFREE + bb));
       const float* col = colp + st * (COLB / 4);
       int imax = (int)sv[0];
 #pragma unroll
@@ -740,6 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // liveness per warp block (32 rows x 32 columns): a dead block stores
       // zeros, so the warps never wait on one another within a tile
       const bool live = __any_sync(0xffffffffu, mine);
+      uint32_t pq[16];   // dS for the dQ MMA (bf16 pairs), zero for a dead block
       if (live) {
         // positions in 32-bit (key / query indices and offsets are < 2^31)
         const int pq0 = (qt0 + j) * kBN + (int)s.q_offset, j0i = (int)j0, jr = (int)jrow;
@@ -788,6 +861,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float2 ds = __fmul2_rn(q2, iq2);
               pa[2 * q4 + hp] = pack_bf16(al.x, al.y);
               pd[2 * q4 + hp] = pack_bf16(ds.x, ds.y);
+              if constexpr (kFuse) {
+                const float2 dq2 = __fmul2_rn(q2, rqf2);
+                pq[2 * q4 + hp] = pack_bf16(dq2.x, dq2.y);
+              }
               accr2 = __ffma2_rn(q2, __ffma2_rn(x, ik2, m1), accr2);
               const float2 rel = make_float2(relb - (float)c, relb - (float)(c + 1));
               accw2 = __ffma2_rn(__fmul2_rn(dp2, asq), __fmul2_rn(rel, sinrel), accw2);
@@ -798,17 +875,50 @@ __global__ void __launch_bounds__(kThreads, 1)
           run(std::false_type{});
         else
           run(std::true_type{});
-        tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, pa);
-        tmem_st16(tmem + TM_P2 + 32 * bb + 16 * g + lane_off, pd);
+        // alpha / dS over this group's own S / dP columns (already loaded)
+        tmem_st16(tmem + TK_S + kBN * bb + cb + lane_off, pa);
+        tmem_st16(tmem + TK_DP + kBN * bb + cb + lane_off, pd);
       } else {
         const uint32_t zero[16] = {};
-        tmem_st16(tmem + TM_P1 + 32 * bb + 16 * g + lane_off, zero);
-        tmem_st16(tmem + TM_P2 + 32 * bb + 16 * g + lane_off, zero);
+        tmem_st16(tmem + TK_S + kBN * bb + cb + lane_off, zero);
+        tmem_st16(tmem + TK_DP + kBN * bb + cb + lane_off, zero);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) pq[c] = 0u;
+      }
+      if constexpr (kFuse) {
+        // dS^T row t (this group's 32 queries) into half (qt & 1) of the
+        // pair's staging buffer, SW128 (16-byte chunk c of the row at c ^ (t % 8));
+        // a pair this CTA only half covers gets zeros in the other half
+        const int buf = pair_c & 1, hf = qt & 1;
+        uint4* row = stg_row(buf, hf);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          row[(4 * g + c) ^ (t & 7)] =
+              make_uint4(pq[4 * c], pq[4 * c + 1], pq[4 * c + 2], pq[4 * c + 3]);
+        if ((j == 0 && hf == 1) || (j == n - 1 && hf == 0)) {
+          uint4* other = stg_row(buf, hf ^ 1);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) other[(4 * g + c) ^ (t & 7)] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();   // generic-proxy writes -> tensor-core reads
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(BAR_P + bb));
+      if constexpr (kFuse) {
+        // drain the pair completed one tile ago (its dQ MMA has had a tile's
+        // time), then remember this one if it completes a pair
+        if (todo >= 0) {
+          if (!drain(todo, todo_qt)) { ok = false; break; }
+          todo = -1;
+        }
+        if ((qt & 1) || j == n - 1) {
+          todo = pair_c;
+          todo_qt = qt;
+        }
+      }
     }
+    if (kFuse && ok && todo >= 0) ok = drain(todo, todo_qt);
     acc_r = 2.f * iv * (accr2.x + accr2.y);   // dr = sum dP m 2a (S - 1)
     acc_w = iv * (accw2.x + accw2.y);
     // epilogue: warpgroup 0 -> dk, warpgroup 1 -> dv (normalisation Jacobians)
@@ -818,7 +928,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     float acc[64];
     if (ok && misc[3]) {
-      tmem_ld64(tmem + (g == 0 ? TM_ACC2 : TM_ACC1) + lane_off, acc);
+      tmem_ld64(tmem + (g == 0 ? TK_ACCK : TK_ACCV) + lane_off, acc);
     } else {
 #pragma unroll
       for (int c = 0; c < 64; ++c) acc[c] = 0.f;
@@ -914,10 +1024,39 @@ size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace
 
+// dq = (1/|q|) (dq^ - (1/|q|)^2 (q . dq^) q) from the fp32 accumulator of the
+// fused kernel; 16 lanes per row, 4 elements each
+__global__ void __launch_bounds__(256) tc_bwd_dq_finalize_kernel(
+    const float* __restrict__ acc, Rows q, const float* __restrict__ nq, OutRows dq, int B, int Tq,
+    int H) {
+  const long long rows = (long long)B * Tq * H;
+  const long long row = (long long)blockIdx.x * 16 + (threadIdx.x >> 4);
+  const int l = threadIdx.x & 15;
+  const bool valid = row < rows;
+  const long long rr = valid ? row : 0;
+  const unsigned r32 = (unsigned)rr, bt = r32 / (unsigned)H;
+  const unsigned hh = r32 - bt * (unsigned)H, t = bt % (unsigned)Tq, bb = bt / (unsigned)Tq;
+  const float4 a = *reinterpret_cast<const float4*>(acc + rr * kD + 4 * l);
+  const uint2 qu = *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(q.p) +
+                                                   bb * q.sb + t * q.st + hh * kD + 4 * l);
+  const float2 q0 = unpack_bf16(qu.x), q1 = unpack_bf16(qu.y);
+  float dot = a.x * q0.x + a.y * q0.y + a.z * q1.x + a.w * q1.y;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o, 16);
+  if (!valid) return;
+  const float inv = 1.0f / nq[rr];
+  const float cf = inv * inv * dot;
+  uint2 o;
+  o.x = pack_bf16(inv * (a.x - cf * q0.x), inv * (a.y - cf * q0.y));
+  o.y = pack_bf16(inv * (a.z - cf * q1.x), inv * (a.w - cf * q1.y));
+  *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(dq.p) + bb * dq.sb + t * dq.st + hh * kD +
+                            4 * l) = o;
+}
+
 size_t tc_bwd_aux_bytes(const AttnShape& s) {
   const long long BH = (long long)s.B * s.H, Tqp = padT(s.Tq), Tkp = padT(s.Tk);
   return al256(BH * Tqp * 4) + 2 * al256(BH * Tkp * 4) + al256(BH * (Tqp / kBN) * 16) +
-         al256(BH * (Tkp / kBN) * 16);
+         al256(BH * (Tkp / kBN) * 16) + al256((size_t)BH * s.Tq * kD * 4);
 }
 
 long long tc_bwd_partials(const AttnShape& s) {
@@ -931,7 +1070,9 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
   if (dev >= 0 && dev < 64 && !g_bwd_attr[dev]) {
     cudaFuncSetAttribute(tc_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)dq::SMEM);
-    cudaFuncSetAttribute(tc_bwd_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(tc_bwd_kv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kv::SMEM);
+    cudaFuncSetAttribute(tc_bwd_kv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kv::SMEM);
     g_bwd_attr[dev] = true;
   }
@@ -947,6 +1088,8 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
   float4* mq = reinterpret_cast<float4*>(w8);
   w8 += al256(BH * (Tqp / kBN) * 16);
   float4* mk = reinterpret_cast<float4*>(w8);
+  w8 += al256(BH * (Tkp / kBN) * 16);
+  float* dq_acc = reinterpret_cast<float*>(w8);
   ax.iqT = iqT; ax.ikT = ikT; ax.ivT = ivT; ax.mq = mq; ax.mk = mk;
   ax.Tqp = (int)Tqp; ax.Tkp = (int)Tkp;
   const long long nblk = BH * ((Tqp > Tkp ? Tqp : Tkp) / kBN);
@@ -967,13 +1110,35 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
       !make_tmap_bthd(&tv128, p.v.p, s.B, s.Tk, s.H, p.v.sb, p.v.st, kBM) ||
       !make_tmap_bthd(&tv64, p.v.p, s.B, s.Tk, s.H, p.v.sb, p.v.st, kBN))
     return SCREEN_ERR_CUDA;
-  if (s.Tq > 0 && (stages & 2)) {
-    dim3 g1((s.Tq + kBM - 1) / kBM, s.B * s.H);
-    tc_bwd_dq_kernel<<<g1, kThreads, dq::SMEM, st>>>(s, p, ax, tq128, tg128, tk64, tv64);
+  const bool deterministic = (stages & SCREEN_BWD_DETERMINISTIC) != 0;
+  if (deterministic) {
+    // dq by its own query-major kernel: every sum in a fixed order
+    if (s.Tq > 0 && (stages & 2)) {
+      dim3 g1((s.Tq + kBM - 1) / kBM, s.B * s.H);
+      tc_bwd_dq_kernel<<<g1, kThreads, dq::SMEM, st>>>(s, p, ax, tq128, tg128, tk64, tv64);
+    }
+    if (s.Tk > 0 && (stages & 4)) {
+      dim3 g2((s.Tk + kBM - 1) / kBM, s.B * s.H);
+      tc_bwd_kv_kernel<false><<<g2, kThreads, kv::SMEM, st>>>(s, p, ax, tq64, tg64, tk128, tv128);
+    }
+    return SCREEN_OK;
   }
-  if (s.Tk > 0 && (stages & 4)) {
-    dim3 g2((s.Tk + kBM - 1) / kBM, s.B * s.H);
-    tc_bwd_kv_kernel<<<g2, kThreads, kv::SMEM, st>>>(s, p, ax, tq64, tg64, tk128, tv128);
+  // fused: the key-major kernel also forms dq^ (fp32 vector reductions into
+  // dq_acc), the finalize pass applies the 1/|q| Jacobian; stage 4 runs both
+  // (dq with dk, dv), stage 2 alone runs nothing
+  if (stages & 4) {
+    const size_t acc_bytes = (size_t)BH * s.Tq * kD * 4;
+    if (acc_bytes && cudaMemsetAsync(dq_acc, 0, acc_bytes, st) != cudaSuccess) return SCREEN_ERR_CUDA;
+    BwdPtrs pf = p;
+    pf.dq_acc = dq_acc;
+    if (s.Tk > 0) {
+      dim3 g2((s.Tk + kBM - 1) / kBM, s.B * s.H);
+      tc_bwd_kv_kernel<true><<<g2, kThreads, kv::SMEM, st>>>(s, pf, ax, tq64, tg64, tk128, tv128);
+    }
+    const long long rows = BH * s.Tq;
+    if (rows > 0)
+      tc_bwd_dq_finalize_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(
+          dq_acc, p.q, p.nq, p.dq, s.B, s.Tq, s.H);
   }
   return SCREEN_OK;
 }

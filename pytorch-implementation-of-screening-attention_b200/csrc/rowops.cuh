@@ -56,6 +56,7 @@ struct BwdPtrs {
                           // bf16 hi plane followed by bf16 lo plane (tensor cores)
   OutRows dq, dk, dv;
   float* part_r; float* part_w;   // [H][P] partials
+  float* dq_acc = nullptr;        // fp32 (B,Tq,H,D) dq^ accumulator (fused tensor-core path)
 };
 
 // Generic SIMT kernels (fp32 math; any dtype, any supported D).

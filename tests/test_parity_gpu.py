@@ -154,6 +154,50 @@ def test_t4096_bf16_against_oracle(ms, oracle):
 
 
 def test_backward_is_deterministic(ms):
+    """With torch.use_deterministic_algorithms(True) the backward takes the
+    fixed-order path (dq by its own kernel): bitwise reproducible."""
+    prev = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True, warn_only=True)
+    try:
+        _backward_twice_equal(ms)
+    finally:
+        torch.use_deterministic_algorithms(prev)
+
+
+def test_fused_dq_backward_matches_fixed_order(ms):
+    """Default path (dq formed inside the dk/dv kernel, fp32 reductions) ==
+    the fixed-order path within the bf16 contract; dk, dv, dr, dw identical
+    in value up to summation order."""
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(13)
+    B, T, H, D = 2, 1100, 3, 64
+    q = torch.randn(B, T, H, D, device=dev, generator=g).bfloat16()
+    k = (q.float() + 0.5 * torch.randn(B, T, H, D, device=dev, generator=g)).bfloat16()
+    v = torch.randn(B, T, H, D, device=dev, generator=g).bfloat16()
+    r = torch.tensor([1.2, 1.05, 1.6], device=dev)
+    w = torch.tensor([70.0, 300.0, 1500.0], device=dev)
+    dy = torch.randn(B, T, H, D, device=dev, generator=g).bfloat16()
+
+    def run():
+        qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+        rr, ww = r.clone().requires_grad_(True), w.clone().requires_grad_(True)
+        y = ms.screening_attention(qq, kk, vv, rr, ww, True)
+        y.backward(dy)
+        return [qq.grad, kk.grad, vv.grad, rr.grad, ww.grad]
+
+    fused = run()
+    prev = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True, warn_only=True)
+    try:
+        fixed = run()
+    finally:
+        torch.use_deterministic_algorithms(prev)
+    for name, a, b in zip(("dq", "dk", "dv", "dr", "dw"), fused, fixed):
+        assert rel_err(a, b) <= 1e-2, name
+    assert ms._lib.device_status() == 0
+
+
+def _backward_twice_equal(ms):
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(3)
     B, T, H, D = 2, 1000, 4, 64
