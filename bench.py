@@ -748,14 +748,12 @@ def main():
                          args.kernel_reps),
         "bwd_prologue": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww,
                                                        stages=1), args.kernel_reps),
-        "bwd_dq": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww, stages=3),
-                            args.kernel_reps),
-        "bwd_dkdv": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww,
-                                                   stages=5), args.kernel_reps),
+        # stage 4: the fused key-major kernel (dk, dv and dq) + the dq finalize
+        "bwd": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww, stages=5),
+                         args.kernel_reps),
     }
-    # stages 3 / 5 include the prologue; isolate the attention kernels
-    kt["bwd_dq"] = max(kt["bwd_dq"] - kt["bwd_prologue"], 1e-6)
-    kt["bwd_dkdv"] = max(kt["bwd_dkdv"] - kt["bwd_prologue"], 1e-6)
+    # stage 5 includes the prologue; isolate the attention kernel
+    kt["bwd"] = max(kt["bwd"] - kt["bwd_prologue"], 1e-6)
     stats.zero_()
     L.screen_fwd(q, k, v, rr, ww, True, norms=(nq, nk, nv), stages=2, tile_stats=stats)
     torch.cuda.synchronize()
@@ -764,8 +762,8 @@ def main():
     pairs_w = windowed_pairs(ww.cpu(), SEQ) * B
     pairs_dense = H * SEQ * (SEQ + 1) / 2 * B
     gemm = 2.0 * Dh  # flops per (i, j) pair per GEMM
-    kernel_flops = {"fwd": 2 * gemm * pairs_w, "bwd_dq": 3 * gemm * pairs_w,
-                    "bwd_dkdv": 4 * gemm * pairs_w}
+    # algorithmic GEMMs per in-window pair: fwd S, alpha V; bwd S, dP, dV, dK, dQ
+    kernel_flops = {"fwd": 2 * gemm * pairs_w, "bwd": 5 * gemm * pairs_w}
     dom = max(kernel_flops, key=lambda n: kt[n])
     pk, pk_kind = peaks()
     peak = float(pk["bf16_tflops"])
