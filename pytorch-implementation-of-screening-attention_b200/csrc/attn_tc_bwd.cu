@@ -27,7 +27,10 @@ namespace {
 using namespace sm100;
 typedef __nv_bfloat16 bf16;
 
-constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 4, kThreads = 320;
+#ifndef SCREEN_KV_STAGES
+#define SCREEN_KV_STAGES 4
+#endif
+constexpr int kD = 64, kBM = 128, kBN = 64, kNS = SCREEN_KV_STAGES, kThreads = 320;
 constexpr int kCompute = 256;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t TILE_A = kBM * kD * 2;  // 128-row operand tile, 16 KB
