@@ -219,7 +219,8 @@ __global__ void tanhnorm_grad_from_y_kernel(const T* __restrict__ y, const float
 }
 
 // bf16 rows split into hi / lo planes (the tensor-core path): 16-byte
-// accesses, D / 8 lanes per row, contiguous dy
+// accesses, D / 8 lanes per row, contiguous dy; each thread handles kRows rows
+// (a block's row range, kRows apart) with all loads issued before any math
 template <int D>
 __global__ void __launch_bounds__(256) tanhnorm_grad_split_bf16_kernel(
     const __nv_bfloat16* __restrict__ y, const float* __restrict__ no,
@@ -227,42 +228,53 @@ __global__ void __launch_bounds__(256) tanhnorm_grad_split_bf16_kernel(
     float eps) {
   constexpr int L = D / 8;
   constexpr int RPB = 256 / L;
-  const long long row = (long long)blockIdx.x * RPB + threadIdx.x / L;
+  constexpr int kRows = 2;
   const int lane = threadIdx.x % L;
-  const bool valid = row < rows;
-  const long long off = (valid ? row : 0) * D + lane * 8;
-  uint4 yu = make_uint4(0, 0, 0, 0), du = make_uint4(0, 0, 0, 0);
-  if (valid) {
-    yu = *reinterpret_cast<const uint4*>(y + off);
-    du = *reinterpret_cast<const uint4*>(dy + off);
-  }
-  const uint32_t yw[4] = {yu.x, yu.y, yu.z, yu.w}, dw[4] = {du.x, du.y, du.z, du.w};
-  float yf[8], df[8];
+  const long long row0 = (long long)blockIdx.x * RPB * kRows + threadIdx.x / L;
+  uint4 yu[kRows], du[kRows];
+  float nr[kRows];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 a = unpack_bf16(yw[e]), b = unpack_bf16(dw[e]);
-    yf[2 * e] = a.x; yf[2 * e + 1] = a.y;
-    df[2 * e] = b.x; df[2 * e + 1] = b.y;
+  for (int u = 0; u < kRows; ++u) {
+    const long long row = row0 + (long long)u * RPB;
+    const bool valid = row < rows;
+    const long long off = (valid ? row : 0) * D + lane * 8;
+    yu[u] = valid ? *reinterpret_cast<const uint4*>(y + off) : make_uint4(0, 0, 0, 0);
+    du[u] = valid ? *reinterpret_cast<const uint4*>(dy + off) : make_uint4(0, 0, 0, 0);
+    nr[u] = valid ? no[row] : 0.f;
   }
-  float yd = 0.f;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) yd = fmaf(yf[e], df[e], yd);
-  yd = group_sum<L>(yd);
-  const float nraw = valid ? no[row] : 0.f;
-  const float g = tanhnorm_scale(nraw, eps);
-  const float k = (nraw > eps) ? tanhnorm_bwd_coef(nraw) * yd : 0.f;
-  if (!valid) return;
-  uint32_t hw[4], lw[4];
+  for (int u = 0; u < kRows; ++u) {
+    const long long row = row0 + (long long)u * RPB;
+    const bool valid = row < rows;
+    const uint32_t yw[4] = {yu[u].x, yu[u].y, yu[u].z, yu[u].w};
+    const uint32_t dw[4] = {du[u].x, du[u].y, du[u].z, du[u].w};
+    float yf[8], df[8];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float g0 = fmaf(g, df[2 * e], k * yf[2 * e]);
-    const float g1 = fmaf(g, df[2 * e + 1], k * yf[2 * e + 1]);
-    hw[e] = pack_bf16(g0, g1);
-    const float2 hf = unpack_bf16(hw[e]);
-    lw[e] = pack_bf16(g0 - hf.x, g1 - hf.y);
+    for (int e = 0; e < 4; ++e) {
+      const float2 a2 = unpack_bf16(yw[e]), b2 = unpack_bf16(dw[e]);
+      yf[2 * e] = a2.x; yf[2 * e + 1] = a2.y;
+      df[2 * e] = b2.x; df[2 * e + 1] = b2.y;
+    }
+    float yd = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) yd = fmaf(yf[e], df[e], yd);
+    yd = group_sum<L>(yd);
+    const float g = tanhnorm_scale(nr[u], eps);
+    const float k = (nr[u] > eps) ? tanhnorm_bwd_coef(nr[u]) * yd : 0.f;
+    if (!valid) continue;
+    const long long off = row * D + lane * 8;
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float g0 = fmaf(g, df[2 * e], k * yf[2 * e]);
+      const float g1 = fmaf(g, df[2 * e + 1], k * yf[2 * e + 1]);
+      hw[e] = pack_bf16(g0, g1);
+      const float2 hf = unpack_bf16(hw[e]);
+      lw[e] = pack_bf16(g0 - hf.x, g1 - hf.y);
+    }
+    *reinterpret_cast<uint4*>(G + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(G + rows * D + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
-  *reinterpret_cast<uint4*>(G + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-  *reinterpret_cast<uint4*>(G + rows * D + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
 }
 
 template <typename T, int D>
@@ -275,7 +287,7 @@ static void launch_grad_from_y(const void* y, const float* no, const void* dy, l
   if constexpr (sizeof(T) == 2 && D % 8 == 0 && D <= 256) {
     if (split && st == (long long)H * D && sb == (long long)T_ * H * D &&
         (reinterpret_cast<uintptr_t>(dy) & 15) == 0) {
-      constexpr int RPB8 = 256 / (D / 8);
+      constexpr int RPB8 = 256 / (D / 8) * 2;   // rows per block: 2 per thread
       tanhnorm_grad_split_bf16_kernel<D><<<(unsigned)((rows + RPB8 - 1) / RPB8), 256, 0, s>>>(
           (const __nv_bfloat16*)y, no, (const __nv_bfloat16*)dy, (__nv_bfloat16*)G, rows, eps);
       return;
