@@ -47,6 +47,17 @@ struct Aux {
 };
 
 __device__ int g_bwd_status = 0;
+
+// Cycle instrumentation of the key-major kernel (variant builds with
+// -DSCREEN_BWD_PROFILE only): clock cycles per role and phase, summed over CTAs.
+#ifdef SCREEN_BWD_PROFILE
+__device__ unsigned long long g_bwd_prof[16];
+#define BPROF_T(name) const long long name = clock64()
+#define BPROF_ADD(slot, t0) atomicAdd(&g_bwd_prof[slot], (unsigned long long)(clock64() - (t0)))
+#else
+#define BPROF_T(name) do {} while (0)
+#define BPROF_ADD(slot, t0) do {} while (0)
+#endif
 __device__ __forceinline__ int* status_word() { return &g_bwd_status; }
 
 __device__ __forceinline__ void store_unit_jacobian(const float (&acc)[64], const bf16* xrow,
@@ -501,11 +512,12 @@ constexpr uint32_t OFF_RED = OFF_TAB + 2 * kBN * 4;     // [2][8] dr / dw warp s
 constexpr uint32_t OFF_BAR = OFF_RED + 64 * 4;
 constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNS, BAR_SD = BAR_EMPTY + kNS,
               BAR_P = BAR_SD + 2, BAR_DONE = BAR_P + 2, BAR_DQF = BAR_DONE + 1,
-              BAR_DQE = BAR_DQF + 2, BAR_COUNT = BAR_DQE + 2;
+              BAR_DQE = BAR_DQF + 2, BAR_SF = BAR_DQE + 2, BAR_COUNT = BAR_SF + 2;
 constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 24;
 static_assert(BAR_COUNT <= 24, "barrier space");
 constexpr uint32_t SMEM = OFF_MISC + 64 + 1024;
 static_assert(SMEM <= 227 * 1024, "shared memory");
+static_assert(OFF_STG % 1024 == 0 && STG_PAIR == 8 * 4096, "dQ drain regions");
 // TMEM: S and dP double-buffered; alpha / dS (bf16) written over the S / dP
 // columns they came from; dV, dK and two dQ accumulators -> 512 columns
 constexpr uint32_t TK_S = 0, TK_DP = 128, TK_ACCV = 256, TK_ACCK = 320, TK_ACCQ = 384;
@@ -518,7 +530,8 @@ template <bool kFuse>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_bwd_kv_kernel(AttnShape s, BwdPtrs p, Aux ax, const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV) {
+                     const __grid_constant__ CUtensorMap tmV,
+                     const __grid_constant__ CUtensorMap tmDQ) {
   using namespace kv;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -561,6 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(BAR_P + i), kCompute);
       mbar_init(bar(BAR_DQF + i), 1);
       mbar_init(bar(BAR_DQE + i), kCompute);
+      mbar_init(bar(BAR_SF + i), kCompute / 32);
     }
     mbar_init(bar(BAR_DONE), 2);
     misc[1] = misc[2] = misc[3] = misc[4] = 0;
@@ -604,7 +618,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int st = j % kNS;
       if (j >= kNS) {
         int okw = 1;
+#ifdef SCREEN_BWD_PROFILE
+        BPROF_T(_p0);
+#endif
         if (lane == 0) okw = mbar_wait(bar(BAR_EMPTY + st), ((j / kNS) - 1) & 1, abort_flag, kWaitLimitNs);
+#ifdef SCREEN_BWD_PROFILE
+        if (lane == 0) BPROF_ADD(10, _p0);
+#endif
         if (!__shfl_sync(0xffffffffu, okw, 0)) break;
       }
       const int qt = qt0 + j;
@@ -652,10 +672,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idMN = idesc_bf16(kBM, kD, 0, 1);
       constexpr uint32_t idQ = idesc_bf16(kBM, kD, 1, 1);   // A = dS^T staging, MN-major
       bool started = false, ok = mbar_wait(bar(BAR_A), 0, abort_flag, kWaitLimitNs);
+#ifdef SCREEN_BWD_PROFILE
+      BPROF_T(_m3);
+#endif
       int pair_i = 0;   // pairs of query tiles whose dQ has been issued
       auto issue_kv = [&](int jj) -> bool {
         const int bb = jj & 1, st = jj % kNS;
+#ifdef SCREEN_BWD_PROFILE
+        BPROF_T(_m0);
+#endif
         if (!mbar_wait(bar(BAR_P + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
+        BPROF_ADD(7, _m0);
+#ifdef SCREEN_BWD_PROFILE
+        BPROF_T(_m4);
+#endif
         tc_fence_after();
         // alpha_j / dS_j sit in the first 16 columns of each compute group's
         // 32-column half of the S / dP buffer
@@ -669,15 +699,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                  idMN, (started || kk > 0) ? 1u : 0u);
         }
         started = true;
+        BPROF_ADD(11, _m4);
         if constexpr (kFuse) {
           const int qt = qt0 + jj;
           if ((qt & 1) || jj == n - 1) {
             // the pair of query tiles (qt & ~1, qt | 1) is complete:
             // dQ[128 q][64 d] = dS (A: [key][q] staging, MN-major, M = 128) x K
             const int buf = pair_i & 1;
+#ifdef SCREEN_BWD_PROFILE
+            BPROF_T(_m1);
+#endif
             if (pair_i >= 2 &&
                 !mbar_wait(bar(BAR_DQE + buf), ((pair_i >> 1) - 1) & 1, abort_flag, kWaitLimitNs))
               return false;
+            BPROF_ADD(8, _m1);
+#ifdef SCREEN_BWD_PROFILE
+            BPROF_T(_m6);
+#endif
             tc_fence_after();
             const uint32_t stg = base + OFF_STG + buf * STG_PAIR;
 #pragma unroll
@@ -686,6 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      desc_sw128(base + OFF_K + kk * 16 * 128, TILE_A, 1024), idQ,
                      kk > 0 ? 1u : 0u);
             mma_commit(bar(BAR_DQF + buf));
+            BPROF_ADD(15, _m6);
             ++pair_i;
           }
         }
@@ -696,7 +735,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % kNS, bb = j & 1;
         // buffer bb held alpha / dS of tile j - 2, read by MMAs issued
         // before these (in-order execution)
+#ifdef SCREEN_BWD_PROFILE
+        BPROF_T(_m2);
+#endif
         ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
+        BPROF_ADD(6, _m2);
+#ifdef SCREEN_BWD_PROFILE
+        BPROF_T(_m5);
+#endif
         if (!ok) break;
         tc_fence_after();
         fence_proxy_async_smem();
@@ -714,9 +760,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_ss(tmem + TK_DP + kBN * bb, desc_sw128(base + OFF_V + kk * 32, 16, 1024),
                  desc_sw128(glb + kk * 32, 16, 1024), idS, 1u);
         mma_commit(bar(BAR_SD + bb));
+        BPROF_ADD(13, _m5);
         if (j >= 1) ok = issue_kv(j - 1);
       }
       if (ok && n >= 1) ok = issue_kv(n - 1);
+#ifdef SCREEN_BWD_PROFILE
+      BPROF_ADD(9, _m3);
+      atomicAdd(&g_bwd_prof[12], (unsigned long long)n);
+      atomicAdd(&g_bwd_prof[14], 1ull);
+#endif
       misc[3] = started ? 1u : 0u;
       mma_commit(bar(BAR_DONE));
       mbar_arrive(bar(BAR_DONE));
@@ -759,8 +811,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     int todo = -1;      // a complete pair whose dQ is yet to be drained
     int todo_qt = 0;
     uint32_t* stg_words = reinterpret_cast<uint32_t*>(gbase + OFF_STG);
-    // drain pair pp: dQ accumulator rows (this thread: query row t of the
-    // pair, columns [32 g, 32 g + 32)) added into the fp32 accumulator
+    // drain pair pp: the dQ accumulator block of this warp (query rows
+    // 32 (warp % 4) .. + 32 of the pair, columns [32 g, 32 g + 32)) goes through
+    // its 4 KB region of the pair's staging buffer -- free once the dQ MMA that
+    // read it has completed -- into one TMA tensor reduce-add (fp32, SW128)
+    // onto the accumulator.  The region is written again for pair pp + 2 only
+    // after every warp has seen its reduce finish reading (BAR_SF).
+    int sf_pending = -1;   // staging buffer whose reduce this warp has not yet released
     auto drain = [&](int pp, int pqt) -> bool {
       const int buf = pp & 1;
       bool okd = mbar_wait(bar(BAR_DQF + buf), (pp >> 1) & 1, abort_flag, kWaitLimitNs);
@@ -772,17 +829,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar(BAR_DQE + buf));
-      const long long qrow = (long long)(pqt & ~1) * kBN + t;
-      if (qrow < s.Tq) {
-        float* dst = p.dq_acc + (((long long)b * s.Tq + qrow) * s.H + h) * kD + cb;
+      const uint32_t region = OFF_STG + buf * STG_PAIR + warp * 4096;
+      uint8_t* rrow = gbase + region + lane * 128;
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * e),
-                       "f"(__uint_as_float(dqv[4 * e])), "f"(__uint_as_float(dqv[4 * e + 1])),
-                       "f"(__uint_as_float(dqv[4 * e + 2])), "f"(__uint_as_float(dqv[4 * e + 3]))
-                       : "memory");
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(rrow + ((c ^ (lane & 7)) << 4)) =
+            make_uint4(dqv[4 * c], dqv[4 * c + 1], dqv[4 * c + 2], dqv[4 * c + 3]);
+      fence_proxy_async_smem();   // generic-proxy writes -> TMA reads
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_4d(&tmDQ, base + region, cb, h, (pqt & ~1) * kBN + 32 * (warp & 3), b);
+        bulk_commit();
       }
+      sf_pending = buf;
       return true;
+    };
+    // release the staging region of the last reduce once it has been read
+    auto release = [&]() {
+      if (sf_pending >= 0) {
+        if (lane == 0) {
+          bulk_wait_read<0>();
+          mbar_arrive(bar(BAR_SF + sf_pending));
+        }
+        sf_pending = -1;
+      }
     };
     // this thread's 4 chunks (16 B each) of row t in half `hf` of staging buffer `buf`
     auto stg_row = [&](int buf, int hf) -> uint4* {
@@ -793,6 +863,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int st = j % kNS, bb = j & 1;
       const int qt = qt0 + j;
       if (kFuse && (j == 0 || (qt & 1) == 0)) ++pair_c;
+#ifdef SCREEN_BWD_PROFILE
+      BPROF_T(_c0);
+#endif
       ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
            mbar_wait(bar(BAR_SD + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
       // warp-uniform verdict (the TMEM accesses below are warp-collective);
@@ -801,10 +874,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
+      if constexpr (kFuse) release();
+#ifdef SCREEN_BWD_PROFILE
+      if (tid == 0) BPROF_ADD(0, _c0);
+      BPROF_T(_c1);
+#endif
       uint32_t sv[32], dv[32];
       tmem_ld32(tmem + TK_S + kBN * bb + cb + lane_off, sv);
       tmem_ld32(tmem + TK_DP + kBN * bb + cb + lane_off, dv);
       tmem_wait_ld();
+#ifdef SCREEN_BWD_PROFILE
+      if (tid == 0) BPROF_ADD(1, _c1);
+      BPROF_T(_c2);
+#endif
       const float* col = colp + st * (COLB / 4);
       int imax = (int)sv[0];
 #pragma unroll
@@ -888,11 +970,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 16; ++c) pq[c] = 0u;
       }
+#ifdef SCREEN_BWD_PROFILE
+      if (tid == 0) BPROF_ADD(2, _c2);
+      BPROF_T(_c3);
+#endif
       if constexpr (kFuse) {
         // dS^T row t (this group's 32 queries) into half (qt & 1) of the
         // pair's staging buffer, SW128 (16-byte chunk c of the row at c ^ (t % 8));
         // a pair this CTA only half covers gets zeros in the other half
         const int buf = pair_c & 1, hf = qt & 1;
+        if (pair_c >= 2 && (j == 0 || hf == 0)) {
+          // first write of this pair: the reduce of pair pair_c - 2 must have
+          // finished reading the buffer in every warp
+          const int pv = pair_c - 2;
+          const bool okf = __all_sync(
+              0xffffffffu, mbar_wait(bar(BAR_SF + buf), (pv >> 1) & 1, abort_flag, kWaitLimitNs));
+          if (!okf) { ok = false; break; }
+        }
         uint4* row = stg_row(buf, hf);
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -908,6 +1002,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(BAR_P + bb));
+#ifdef SCREEN_BWD_PROFILE
+      if (tid == 0) BPROF_ADD(3, _c3);
+      BPROF_T(_c4);
+#endif
       if constexpr (kFuse) {
         // drain the pair completed one tile ago (its dQ MMA has had a tile's
         // time), then remember this one if it completes a pair
@@ -920,8 +1018,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           todo_qt = qt;
         }
       }
+#ifdef SCREEN_BWD_PROFILE
+      if (tid == 0) { BPROF_ADD(4, _c4); BPROF_ADD(5, _c0); }
+#endif
     }
     if (kFuse && ok && todo >= 0) ok = drain(todo, todo_qt);
+    // every reduce this warp issued completes before the CTA's shared memory goes away
+    if (kFuse && lane == 0) bulk_wait<0>();
     acc_r = 2.f * iv * (accr2.x + accr2.y);   // dr = sum dP m 2a (S - 1)
     acc_w = iv * (accw2.x + accw2.y);
     // epilogue: warpgroup 0 -> dk, warpgroup 1 -> dv (normalisation Jacobians)
@@ -1122,7 +1225,8 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
     }
     if (s.Tk > 0 && (stages & 4)) {
       dim3 g2((s.Tk + kBM - 1) / kBM, s.B * s.H);
-      tc_bwd_kv_kernel<false><<<g2, kThreads, kv::SMEM, st>>>(s, p, ax, tq64, tg64, tk128, tv128);
+      tc_bwd_kv_kernel<false><<<g2, kThreads, kv::SMEM, st>>>(s, p, ax, tq64, tg64, tk128, tv128,
+                                                              tq64);
     }
     return SCREEN_OK;
   }
@@ -1136,7 +1240,10 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
     pf.dq_acc = dq_acc;
     if (s.Tk > 0) {
       dim3 g2((s.Tk + kBM - 1) / kBM, s.B * s.H);
-      tc_bwd_kv_kernel<true><<<g2, kThreads, kv::SMEM, st>>>(s, pf, ax, tq64, tg64, tk128, tv128);
+      CUtensorMap tdq;
+      if (!make_tmap_dq(&tdq, dq_acc, s.B, s.Tq, s.H)) return SCREEN_ERR_CUDA;
+      tc_bwd_kv_kernel<true><<<g2, kThreads, kv::SMEM, st>>>(s, pf, ax, tq64, tg64, tk128, tv128,
+                                                             tdq);
     }
     const long long rows = BH * s.Tq;
     if (rows > 0)
@@ -1145,6 +1252,18 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
   }
   return SCREEN_OK;
 }
+
+#ifdef SCREEN_BWD_PROFILE
+extern "C" SCREEN_API int screen_debug_bwd_profile(unsigned long long* out, int clear) {
+  if (cudaMemcpyFromSymbol(out, g_bwd_prof, sizeof(unsigned long long) * 16) != cudaSuccess)
+    return -1;
+  if (clear) {
+    unsigned long long z[16] = {};
+    cudaMemcpyToSymbol(g_bwd_prof, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
 
 int tc_bwd_device_status(bool clear) {
   int v = 0;

@@ -220,6 +220,17 @@ __device__ __forceinline__ void bulk_reduce_add_f32(void* gdst, uint32_t ssrc, u
       "r"(ssrc), "r"(bytes)
       : "memory");
 }
+// TMA tensor reduce-add of a tile from this CTA's shared memory into the
+// global tensor of a 4-D tensor map (this thread's bulk async-group); rows
+// outside the tensor are not written
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, uint32_t src, int c0,
+                                                  int c1, int c2, int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3, %4, %5}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -385,6 +396,30 @@ inline bool make_tmap_bthd(CUtensorMap* map, const void* base, long long B, long
   const cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+// fp32 (B, T, H, 64) contiguous tensor (the backward's dq accumulator):
+// boxes of 32 d x 1 head x 32 times x 1 batch, 128-byte swizzled (each box row
+// is 128 B), the layout the reduce-add of a warp's 32 x 32 block is staged in
+inline bool make_tmap_dq(CUtensorMap* map, const void* base, long long B, long long T, int H) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }();
+  if (!encode) return false;
+  const cuuint64_t dims[4] = {64, (cuuint64_t)H, (cuuint64_t)(T > 0 ? T : 1),
+                              (cuuint64_t)(B > 0 ? B : 1)};
+  const cuuint64_t strides[3] = {64 * 4, (cuuint64_t)H * 64 * 4, (cuuint64_t)T * H * 64 * 4};
+  const cuuint32_t box[4] = {32, 1, 32, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), dims, strides,
                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
          CUDA_SUCCESS;
