@@ -675,6 +675,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef SCREEN_BWD_PROFILE
       BPROF_T(_m3);
 #endif
+      // shared-memory descriptors built once: an operand at byte offset x
+      // from a base is base_desc + x / 16 (the start-address field holds
+      // address / 16 in 14 bits; every address here is below 256 KB)
+      const uint64_t dK_k = desc_sw128(base + OFF_K, 16, 1024);       // K-major (S: A = K)
+      const uint64_t dV_k = desc_sw128(base + OFF_V, 16, 1024);       // K-major (dP: A = V)
+      const uint64_t dQ_k = desc_sw128(base + OFF_Q, 16, 1024);       // stage 0 Q, K-major
+      const uint64_t dQ_mn = desc_sw128(base + OFF_Q, TILE_B, 1024);  // stage 0 Q, MN-major
+      const uint64_t dStg = desc_sw128(base + OFF_STG, TILE_A, 1024); // dS^T staging, MN-major
+      const uint64_t dK_mn = desc_sw128(base + OFF_K, TILE_A, 1024);  // K, MN-major (dQ: B)
       int pair_i = 0;   // pairs of query tiles whose dQ has been issued
       auto issue_kv = [&](int jj) -> bool {
         const int bb = jj & 1, st = jj % kNS;
@@ -689,14 +698,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         // alpha_j / dS_j sit in the first 16 columns of each compute group's
         // 32-column half of the S / dP buffer
-        const uint32_t qb = base + OFF_Q + st * STAGE, ghb = qb + TILE_B;
+        const uint64_t qd = dQ_mn + (uint64_t)((st * STAGE) >> 4), gd = qd + (TILE_B >> 4);
+        const uint32_t s0 = started ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint32_t pcol = 64 * bb + (kk >> 1) * 32 + (kk & 1) * 8;
-          mma_ts(tmem + TK_ACCV, tmem + TK_S + pcol, desc_sw128(ghb + kk * 16 * 128, TILE_B, 1024),
-                 idMN, (started || kk > 0) ? 1u : 0u);
-          mma_ts(tmem + TK_ACCK, tmem + TK_DP + pcol, desc_sw128(qb + kk * 16 * 128, TILE_B, 1024),
-                 idMN, (started || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + TK_ACCV, tmem + TK_S + pcol, gd + kk * (16 * 128 / 16), idMN,
+                 kk > 0 ? 1u : s0);
+          mma_ts(tmem + TK_ACCK, tmem + TK_DP + pcol, qd + kk * (16 * 128 / 16), idMN,
+                 kk > 0 ? 1u : s0);
         }
         started = true;
         BPROF_ADD(11, _m4);
@@ -717,12 +727,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             BPROF_T(_m6);
 #endif
             tc_fence_after();
-            const uint32_t stg = base + OFF_STG + buf * STG_PAIR;
+            const uint64_t sd = dStg + (uint64_t)(buf * (STG_PAIR >> 4));
 #pragma unroll
             for (int kk = 0; kk < kBM / 16; ++kk)
-              mma_ss(tmem + TK_ACCQ + 64 * buf, desc_sw128(stg + kk * 16 * 128, TILE_A, 1024),
-                     desc_sw128(base + OFF_K + kk * 16 * 128, TILE_A, 1024), idQ,
-                     kk > 0 ? 1u : 0u);
+              mma_ss(tmem + TK_ACCQ + 64 * buf, sd + kk * (16 * 128 / 16),
+                     dK_mn + kk * (16 * 128 / 16), idQ, kk > 0 ? 1u : 0u);
             mma_commit(bar(BAR_DQF + buf));
             BPROF_ADD(15, _m6);
             ++pair_i;
@@ -746,19 +755,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_fence_after();
         fence_proxy_async_smem();
-        const uint32_t qb = base + OFF_Q + st * STAGE, ghb = qb + TILE_B, glb = qb + 2 * TILE_B;
+        const uint64_t qd = dQ_k + (uint64_t)((st * STAGE) >> 4), ghd = qd + (TILE_B >> 4),
+                       gld = qd + (2 * TILE_B >> 4);
+        // S and dP (hi) interleaved, then dP (lo)
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          mma_ss(tmem + TK_S + kBN * bb, dK_k + 2 * kk, qd + 2 * kk, idS, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + TK_DP + kBN * bb, dV_k + 2 * kk, ghd + 2 * kk, idS, kk > 0 ? 1u : 0u);
+        }
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TK_S + kBN * bb, desc_sw128(base + OFF_K + kk * 32, 16, 1024),
-                 desc_sw128(qb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TK_DP + kBN * bb, desc_sw128(base + OFF_V + kk * 32, 16, 1024),
-                 desc_sw128(ghb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TK_DP + kBN * bb, desc_sw128(base + OFF_V + kk * 32, 16, 1024),
-                 desc_sw128(glb + kk * 32, 16, 1024), idS, 1u);
+          mma_ss(tmem + TK_DP + kBN * bb, dV_k + 2 * kk, gld + 2 * kk, idS, 1u);
         mma_commit(bar(BAR_SD + bb));
         BPROF_ADD(13, _m5);
         if (j >= 1) ok = issue_kv(j - 1);
