@@ -89,7 +89,7 @@ __device__ unsigned long long g_fwd_prof[16];
 
 __global__ void __launch_bounds__(kThreads, 2)
     tc_fwd_kernel(AttnShape s, FwdPtrs p, const float* __restrict__ ikT,
-                  const float4* __restrict__ ikmeta, int Tkp,
+                  const float4* __restrict__ ikmeta, int Tkp, const int* __restrict__ order,
                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV) {
   extern __shared__ uint8_t smem_raw[];
@@ -106,8 +106,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.y, b = bh / s.H, h = bh % s.H;
-  const long long i0 = (long long)blockIdx.x * kBM;
+  // CTA -> (b, h, query tile) through the longest-first order
+  const int nqt = (s.Tq + kBM - 1) / kBM;
+  const long long item = order[blockIdx.x];
+  const int bh = (int)(item / nqt), b = bh / s.H, h = bh % s.H;
+  const long long i0 = (item % nqt) * kBM;
   const bool causal = s.causal != 0;
   const float r = s.r[h], w = s.w[h];
   const int dmax = window_dmax(w);
@@ -611,7 +614,7 @@ bool tc_supported(int dtype, int D) { return dtype == SCREEN_BF16 && D == kD; }
 size_t tc_fwd_workspace(const AttnShape& s) {
   const long long BH = (long long)s.B * s.H, Tkp = tk_pad(s.Tk);
   return al256((size_t)s.B * s.Tk * s.H * kD * 2) + al256((size_t)BH * Tkp * 4) +
-         al256((size_t)BH * (Tkp / kBN) * 16);
+         al256((size_t)BH * (Tkp / kBN) * 16) + al256((size_t)BH * ((s.Tq + kBM - 1) / kBM) * 4);
 }
 
 int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
@@ -630,6 +633,8 @@ int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_giv
   float* ikT = reinterpret_cast<float*>(ws + al256((size_t)s.B * s.Tk * s.H * kD * 2));
   float4* meta = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(ikT) +
                                            al256((size_t)BH * Tkp * 4));
+  int* order = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(meta) +
+                                      al256((size_t)BH * (Tkp / kBN) * 16));
   const long long rows = (long long)s.B * ((norms_given ? 0 : s.Tq) + s.Tk) * s.H;
   if (rows > 0) {
     long long blocks = (rows + 31) / 32;
@@ -650,8 +655,10 @@ int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_giv
       !make_tmap_bthd(&tv, vhat, s.B, s.Tk, s.H, (long long)s.Tk * s.H * kD,
                       (long long)s.H * kD, kBN))
     return SCREEN_ERR_CUDA;
-  dim3 grid((s.Tq + kBM - 1) / kBM, s.B * s.H);
-  tc_fwd_kernel<<<grid, kThreads, kSmemBytes, st>>>(s, p, ikT, meta, (int)Tkp, tq, tk, tv);
+  const int nqt = (s.Tq + kBM - 1) / kBM;
+  tile_order(s, 0, nqt, order, st);
+  tc_fwd_kernel<<<(unsigned)(BH * nqt), kThreads, kSmemBytes, st>>>(s, p, ikT, meta, (int)Tkp,
+                                                                    order, tq, tk, tv);
   return SCREEN_OK;
 }
 

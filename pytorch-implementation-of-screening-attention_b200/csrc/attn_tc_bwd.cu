@@ -43,6 +43,7 @@ struct Aux {
   const float* ivT;   // [B*H][Tkp] 1/(|v| |k|) (0 past Tk and for padded keys)
   const float4* mq;   // [B*H][Tqp/64] (max 1/|q| of the tile, -, -, -)
   const float4* mk;   // [B*H][Tkp/64] (max 1/|k| of the tile, -, -, -)
+  const int* order;   // [B*H*ceil(Tk/128)] key-major CTA order (longest first)
   int Tqp, Tkp;
 };
 
@@ -52,6 +53,7 @@ __device__ int g_bwd_status = 0;
 // -DSCREEN_BWD_PROFILE only): clock cycles per role and phase, summed over CTAs.
 #ifdef SCREEN_BWD_PROFILE
 __device__ unsigned long long g_bwd_prof[16];
+__device__ unsigned long long g_prof_lat[4];
 #define BPROF_T(name) const long long name = clock64()
 #define BPROF_ADD(slot, t0) atomicAdd(&g_bwd_prof[slot], (unsigned long long)(clock64() - (t0)))
 #else
@@ -546,8 +548,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.y, b = bh / s.H, h = bh % s.H;
-  const long long j0 = (long long)blockIdx.x * kBM;
+  // CTA -> (b, h, key tile) through the longest-first order
+  const int nkt = (s.Tk + kBM - 1) / kBM;
+  const long long item = ax.order[blockIdx.x];
+  const int bh = (int)(item / nkt), b = bh / s.H, h = bh % s.H;
+  const int kx = (int)(item % nkt);
+  const long long j0 = (long long)kx * kBM;
   const bool causal = s.causal != 0;
   const float r = s.r[h], w = s.w[h];
   const int dmax = window_dmax(w);
@@ -590,6 +596,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bf16* vh = reinterpret_cast<const bf16*>(p.v.p) + (long long)b * p.v.sb + (long long)h * kD;
   float acc_r = 0.f, acc_w = 0.f;
 
+#ifdef SCREEN_VAR_PREFETCH
+  if (warp == 8 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmG)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
+    if (kFuse) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmDQ)) : "memory");
+  }
+#endif
   if (warp == 8) {
     // ---------------------------------------------------------- producer
     // lane 0 issues the TMA copies: K, V once (128 rows), then per query
@@ -640,6 +655,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(sb_ + 2 * TILE_B, &tmG, 0, h, (int)iq0, b + s.B, fb);
         bulk_g2s(colb, iqh + iq0, kBN * 4, fb);
         bulk_g2s(colb + 3 * kBN * 4, mh + qt, 16, fb);
+#ifdef SCREEN_BWD_PROFILE
+        reinterpret_cast<volatile long long*>(red + 16)[st] = clock64();
+#endif
       }
       issued = j + 1;
       // column angle pi (iq0 + c + q_offset - j0) / w by rotation
@@ -653,6 +671,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       col[2 * kBN + lane + 32] = sb * cphi1 + cbv * sphi1;
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_FULL + st));
+#ifdef SCREEN_BWD_PROFILE
+      if (lane == 0) {
+        atomicAdd(&g_prof_lat[2], (unsigned long long)(clock64() - reinterpret_cast<volatile long long*>(red + 16)[st]));
+        atomicAdd(&g_prof_lat[3], 1ull);
+      }
+#endif
     }
     if (lane == 0 && *abort_flag) {
       // let the copies already issued land before the CTA's smem goes away
@@ -750,6 +774,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
         BPROF_ADD(6, _m2);
 #ifdef SCREEN_BWD_PROFILE
+        {
+          const long long now = clock64();
+          if (now - _m2 > 64) {
+            atomicAdd(&g_prof_lat[0], (unsigned long long)(now - reinterpret_cast<volatile long long*>(red + 16)[st]));
+            atomicAdd(&g_prof_lat[1], 1ull);
+          }
+        }
+#endif
+#ifdef SCREEN_BWD_PROFILE
         BPROF_T(_m5);
 #endif
         if (!ok) break;
@@ -845,7 +878,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();   // generic-proxy writes -> TMA reads
       __syncwarp();
       if (lane == 0) {
+#ifndef SCREEN_VAR_NORED
         tma_reduce_add_4d(&tmDQ, base + region, cb, h, (pqt & ~1) * kBN + 32 * (warp & 3), b);
+#endif
         bulk_commit();
       }
       sf_pending = buf;
@@ -963,10 +998,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         };
+#ifdef SCREEN_VAR_NOEDGE
+        run(std::true_type{});
+#else
         if (inside)
           run(std::false_type{});
         else
           run(std::true_type{});
+#endif
         // alpha / dS over this group's own S / dP columns (already loaded)
         tmem_st16(tmem + TK_S + kBN * bb + cb + lane_off, pa);
         tmem_st16(tmem + TK_DP + kBN * bb + cb + lane_off, pd);
@@ -1077,8 +1116,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       sr += red[k2];
       sw += red[8 + k2];
     }
-    const long long P = (long long)s.B * gridDim.x;
-    const long long idx = (long long)h * P + (long long)b * gridDim.x + blockIdx.x;
+    const long long P = (long long)s.B * nkt;
+    const long long idx = (long long)h * P + (long long)b * nkt + kx;
     p.part_r[idx] = sr;
     p.part_w[idx] = sw;
     if (*abort_flag) atomicExch(status_word(), (int)SCREEN_ERR_TIMEOUT);
@@ -1169,7 +1208,8 @@ __global__ void __launch_bounds__(256) tc_bwd_dq_finalize_kernel(
 size_t tc_bwd_aux_bytes(const AttnShape& s) {
   const long long BH = (long long)s.B * s.H, Tqp = padT(s.Tq), Tkp = padT(s.Tk);
   return al256(BH * Tqp * 4) + 2 * al256(BH * Tkp * 4) + al256(BH * (Tqp / kBN) * 16) +
-         al256(BH * (Tkp / kBN) * 16) + al256((size_t)BH * s.Tq * kD * 4);
+         al256(BH * (Tkp / kBN) * 16) + al256((size_t)BH * s.Tq * kD * 4) +
+         al256((size_t)BH * ((s.Tk + kBM - 1) / kBM) * 4);
 }
 
 long long tc_bwd_partials(const AttnShape& s) {
@@ -1203,7 +1243,9 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
   float4* mk = reinterpret_cast<float4*>(w8);
   w8 += al256(BH * (Tkp / kBN) * 16);
   float* dq_acc = reinterpret_cast<float*>(w8);
-  ax.iqT = iqT; ax.ikT = ikT; ax.ivT = ivT; ax.mq = mq; ax.mk = mk;
+  w8 += al256((size_t)BH * s.Tq * kD * 4);
+  int* order = reinterpret_cast<int*>(w8);
+  ax.iqT = iqT; ax.ikT = ikT; ax.ivT = ivT; ax.mq = mq; ax.mk = mk; ax.order = order;
   ax.Tqp = (int)Tqp; ax.Tkp = (int)Tkp;
   const long long nblk = BH * ((Tqp > Tkp ? Tqp : Tkp) / kBN);
   if (nblk > 0)
@@ -1231,8 +1273,9 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
       tc_bwd_dq_kernel<<<g1, kThreads, dq::SMEM, st>>>(s, p, ax, tq128, tg128, tk64, tv64);
     }
     if (s.Tk > 0 && (stages & 4)) {
-      dim3 g2((s.Tk + kBM - 1) / kBM, s.B * s.H);
-      tc_bwd_kv_kernel<false><<<g2, kThreads, kv::SMEM, st>>>(s, p, ax, tq64, tg64, tk128, tv128,
+      const int nkt = (s.Tk + kBM - 1) / kBM;
+      tile_order(s, 1, nkt, order, st);
+      tc_bwd_kv_kernel<false><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(s, p, ax, tq64, tg64, tk128, tv128,
                                                               tq64);
     }
     return SCREEN_OK;
@@ -1246,10 +1289,11 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
     BwdPtrs pf = p;
     pf.dq_acc = dq_acc;
     if (s.Tk > 0) {
-      dim3 g2((s.Tk + kBM - 1) / kBM, s.B * s.H);
+      const int nkt = (s.Tk + kBM - 1) / kBM;
+      tile_order(s, 1, nkt, order, st);
       CUtensorMap tdq;
       if (!make_tmap_dq(&tdq, dq_acc, s.B, s.Tq, s.H)) return SCREEN_ERR_CUDA;
-      tc_bwd_kv_kernel<true><<<g2, kThreads, kv::SMEM, st>>>(s, pf, ax, tq64, tg64, tk128, tv128,
+      tc_bwd_kv_kernel<true><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(s, pf, ax, tq64, tg64, tk128, tv128,
                                                              tdq);
     }
     const long long rows = BH * s.Tq;
@@ -1264,9 +1308,15 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
 extern "C" SCREEN_API int screen_debug_bwd_profile(unsigned long long* out, int clear) {
   if (cudaMemcpyFromSymbol(out, g_bwd_prof, sizeof(unsigned long long) * 16) != cudaSuccess)
     return -1;
+  unsigned long long lat[4];
+  cudaMemcpyFromSymbol(lat, g_prof_lat, sizeof(lat));
+  out[18] = lat[3] ? lat[2] / lat[3] : 0;   // producer: TMA issue -> its plain arrival
+  out[16] = lat[1] ? lat[0] / lat[1] : 0;   // mean load latency when the MMA warp waited
+  out[17] = lat[1];
   if (clear) {
     unsigned long long z[16] = {};
     cudaMemcpyToSymbol(g_bwd_prof, z, sizeof(z));
+    cudaMemcpyToSymbol(g_prof_lat, z, 4 * sizeof(unsigned long long));
   }
   return 0;
 }

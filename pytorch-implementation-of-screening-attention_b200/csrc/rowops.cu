@@ -357,4 +357,87 @@ void reduce_param_grads(const float* part_r, const float* part_w, long long P, i
   reduce_param_grads_kernel<<<H, 256, 0, s>>>(part_r, part_w, P, w, dr, dw);
 }
 
+// ---------------------------------------------------------------------------
+// Longest-processing-time-first CTA order.  Under a causal window the CTAs of
+// one launch carry very different numbers of tiles (a head with w = 4096 at
+// the end of the sequence: 66 tiles; a head with w = 256: 6); launched in
+// index order the longest ones can start last and leave the GPU idle at the
+// tail.  The hardware dispatches CTAs roughly in blockIdx order, so a launch
+// through perm runs the longest first.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kOrderBuckets = 1024;
+__device__ __forceinline__ int item_tiles(const AttnShape& s, int kind, int ntiles, long long id) {
+  const long long bh = id / ntiles;
+  const int x = (int)(id % ntiles), h = (int)(bh % s.H);
+  const int dmax = window_dmax(s.w[h]);
+  if (dmax < 0) return 0;
+  const bool causal = s.causal != 0;
+  long long lo, hi;
+  if (kind == 0) {
+    const long long i0 = (long long)x * 128;
+    long long il = i0 + 127;
+    if (il > s.Tq - 1) il = s.Tq - 1;
+    key_range(i0 + s.q_offset, il + s.q_offset, dmax, causal, s.Tk, lo, hi);
+  } else {
+    const long long j0 = (long long)x * 128;
+    long long jl = j0 + 127;
+    if (jl > s.Tk - 1) jl = s.Tk - 1;
+    query_pos_range(j0, jl, dmax, causal, lo, hi);
+    lo -= s.q_offset;
+    hi -= s.q_offset;
+    if (lo < 0) lo = 0;
+    if (hi > s.Tq - 1) hi = s.Tq - 1;
+  }
+  if (lo > hi) return 0;
+  const long long n = hi / 64 - lo / 64 + 1;
+  return n > kOrderBuckets - 1 ? kOrderBuckets - 1 : (int)n;
+}
+__global__ void __launch_bounds__(1024) tile_order_kernel(AttnShape s, int kind, int ntiles,
+                                                          long long N, int* perm) {
+  __shared__ int cnt[kOrderBuckets];
+  __shared__ int wsum[32];
+  const int t = threadIdx.x;
+  cnt[t] = 0;
+  __syncthreads();
+  for (long long id = t; id < N; id += blockDim.x)
+    atomicAdd(&cnt[kOrderBuckets - 1 - item_tiles(s, kind, ntiles, id)], 1);
+  __syncthreads();
+  // exclusive prefix sum over the buckets (bucket 0 = most tiles)
+  const int v = cnt[t];
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, o);
+    if ((t & 31) >= o) incl += u;
+  }
+  if ((t & 31) == 31) wsum[t >> 5] = incl;
+  __syncthreads();
+  if (t < 32) {
+    int x = wsum[t];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, x, o);
+      if (t >= o) x += u;
+    }
+    wsum[t] = x;   // inclusive over warps
+  }
+  __syncthreads();
+  const int base = (t >> 5) ? wsum[(t >> 5) - 1] : 0;
+  __syncthreads();
+  cnt[t] = base + incl - v;
+  __syncthreads();
+  for (long long id = t; id < N; id += blockDim.x) {
+    const int pos = atomicAdd(&cnt[kOrderBuckets - 1 - item_tiles(s, kind, ntiles, id)], 1);
+    perm[pos] = (int)id;
+  }
+}
+}  // namespace
+
+void tile_order(const AttnShape& s, int kind, int ntiles, int* perm, cudaStream_t st) {
+  const long long N = (long long)s.B * s.H * ntiles;
+  if (N <= 0) return;
+  tile_order_kernel<<<1, kOrderBuckets, 0, st>>>(s, kind, ntiles, N, perm);
+}
+
 }  // namespace screen

@@ -74,6 +74,11 @@ int tc_device_status(bool clear);
 // tcgen05 / TMEM backward (bf16, D = 64); aux_ws holds tc_bwd_aux_bytes()
 size_t tc_bwd_aux_bytes(const AttnShape& s);
 long long tc_bwd_partials(const AttnShape& s);
+// Longest-first launch order of the tcgen05 kernels' CTAs: perm[i] is the
+// work item (bh * ntiles + tile) that CTA i runs, sorted by decreasing tile
+// count.  kind 0: query tiles of 128 (forward), kind 1: key tiles of 128
+// (key-major backward).  One CTA, counting sort; perm holds B*H*ntiles ints.
+void tile_order(const AttnShape& s, int kind, int ntiles, int* perm, cudaStream_t st);
 int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st);
 int tc_bwd_device_status(bool clear);
 
