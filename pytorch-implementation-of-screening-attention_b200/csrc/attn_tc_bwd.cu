@@ -952,6 +952,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int iclo = inside ? 0 : (clo_ < 0 ? 0 : (clo_ > 32 ? 32 : clo_));
         const int ichi = inside ? 31 : (chi_ < -1 ? -1 : (chi_ > 31 ? 31 : chi_));
         const float relb = (float)(jr - pq0 - cb);   // rel = j - p = relb - c
+        const float2 relb2 = make_float2(relb, relb);
         const float4* iq4 = reinterpret_cast<const float4*>(col + cb);
         const float4* cv4 = reinterpret_cast<const float4*>(col + kBN + cb);
         const float4* sv4 = reinterpret_cast<const float4*>(col + 2 * kBN + cb);
@@ -993,7 +994,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pq[2 * q4 + hp] = pack_bf16(dq2.x, dq2.y);
               }
               accr2 = __ffma2_rn(q2, __ffma2_rn(x, ik2, m1), accr2);
-              const float2 rel = make_float2(relb - (float)c, relb - (float)(c + 1));
+              const float2 rel = __fadd2_rn(relb2, make_float2(-(float)c, -(float)(c + 1)));
               accw2 = __ffma2_rn(__fmul2_rn(dp2, asq), __fmul2_rn(rel, sinrel), accw2);
             }
           }
