@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define SCREEN_ABI_VERSION 3
+#define SCREEN_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define SCREEN_API __attribute__((visibility("default")))
@@ -94,7 +94,25 @@ typedef struct screen_fwd_args {
                                  /*   the window, += blocks with live scores  */
   void* workspace;               /* screen_fwd_workspace_size() bytes         */
   size_t workspace_bytes;
+  /* attention dropout on alpha (attention.py:68,190): each (b, h, query i,  */
+  /* key j) is dropped iff screen_dropout_bits(seed, b*H+h, i, j) <          */
+  /* dropout_threshold, kept ones scaled by 2^32 / (2^32 - threshold).  0 =  */
+  /* no dropout.  screen_bwd must get the same seed and threshold.           */
+  uint32_t dropout_threshold;
+  uint32_t _pad1;
+  uint64_t dropout_seed;
 } screen_fwd_args;
+
+/* The dropout bits of score (bh, i, j) for a seed (host-side mirror of the
+ * kernels' counter-based hash, for tests and for callers that need the mask):
+ *   k  = mix(seed_lo ^ mix(seed_hi ^ bh * 0x9E3779B1))
+ *   ri = mix(k ^ i * 0x85EBCA77),  bits = mix(ri ^ j * 0xC2B2AE3D)
+ * with 32-bit wrap-around and mix(x) = the lowbias32 finalizer
+ * (x ^= x>>16; x *= 0x7feb352d; x ^= x>>15; x *= 0x846ca68b; x ^= x>>16).
+ * i is the query index (0..Tq-1) and j the key index (0..Tk-1) of the call.
+ * No counterpart in the reference, whose dropout draws from torch's
+ * generator (attention.py:190); bit parity with it is not possible. */
+SCREEN_API uint32_t screen_dropout_bits(uint64_t seed, uint32_t bh, uint32_t i, uint32_t j);
 
 /* Bytes of device workspace screen_fwd needs (bf16 D=64 tensor-core path: the
  * unit-V operand, 1/|k| per key and per-tile bounds; 0 otherwise). */
@@ -144,6 +162,9 @@ typedef struct screen_bwd_args {
   void* dv; int64_t dv_sb, dv_st;
   float* dr; float* dw;          /* (H,) dL/dr, dL/dw                         */
   void* workspace; size_t workspace_bytes;
+  uint32_t dropout_threshold;    /* as screen_fwd_args: the forward's values  */
+  uint32_t _pad1;
+  uint64_t dropout_seed;
 } screen_bwd_args;
 
 /* Bytes of device workspace screen_bwd needs for these shapes. */

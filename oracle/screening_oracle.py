@@ -80,14 +80,64 @@ def screening_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, r: torch.T
     return tanh_norm(out, eps).transpose(1, 2)
 
 
+# ---------------------------------------------------------------------------
+# Attention dropout (multiscreen/attention.py:68,190 applies nn.Dropout to
+# alpha).  torch's dropout mask cannot be reproduced bit for bit, so the CUDA
+# path draws its mask from a counter-based hash instead; this restates that
+# hash (the library's screen_dropout_bits) so that parity tests can apply the
+# very same mask here.
+# ---------------------------------------------------------------------------
+_M32 = 0xFFFFFFFF
+
+
+def _mul32(x: torch.Tensor, c: int) -> torch.Tensor:
+    """(x * c) mod 2^32 for int64 tensors holding uint32 values (split so no
+    product leaves int64)."""
+    lo = x * (c & 0xFFFF)
+    hi = ((x * (c >> 16)) & 0xFFFF) << 16
+    return (lo + hi) & _M32
+
+
+def _mix32(x: torch.Tensor) -> torch.Tensor:
+    """lowbias32 finalizer: x ^= x>>16; x *= 0x7feb352d; x ^= x>>15;
+    x *= 0x846ca68b; x ^= x>>16 (all mod 2^32)."""
+    x = x ^ (x >> 16)
+    x = _mul32(x, 0x7FEB352D)
+    x = x ^ (x >> 15)
+    x = _mul32(x, 0x846CA68B)
+    return x ^ (x >> 16)
+
+
+def dropout_bits(seed: int, bh: torch.Tensor, i: torch.Tensor, j: torch.Tensor) -> torch.Tensor:
+    """Counter bits of scores (bh, query i, key j), broadcast over the three
+    int64 index tensors: k = mix(seed_lo ^ mix(seed_hi ^ bh * 0x9E3779B1)),
+    row = mix(k ^ i * 0x85EBCA77), bits = mix(row ^ j * 0xC2B2AE3D)."""
+    lo, hi = seed & _M32, (seed >> 32) & _M32
+    k = _mix32(lo ^ _mix32(hi ^ _mul32(bh.long(), 0x9E3779B1)))
+    row = _mix32(k ^ _mul32(i.long(), 0x85EBCA77))
+    return _mix32(row ^ _mul32(j.long(), 0xC2B2AE3D))
+
+
+def dropout_keep(seed: int, threshold: int, B: int, H: int, i: torch.Tensor,
+                 j: torch.Tensor) -> torch.Tensor:
+    """(B, H, len(i), len(j)) float mask: 2^32 / (2^32 - threshold) where the
+    score is kept (bits >= threshold), 0 where dropped."""
+    bh = torch.arange(B * H).view(B, H, 1, 1)
+    bits = dropout_bits(seed, bh, i.view(1, 1, -1, 1), j.view(1, 1, 1, -1))
+    scale = 4294967296.0 / (4294967296.0 - threshold)
+    return (bits >= threshold).double() * scale
+
+
 def screening_core_windowed(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, r: torch.Tensor,
                             w: torch.Tensor, causal: bool = True,
                             key_padding_mask: torch.Tensor | None = None, eps: float = 1e-8,
-                            q_offset: int = 0, chunk: int = 256) -> torch.Tensor:
+                            q_offset: int = 0, chunk: int = 256,
+                            dropout: tuple[int, int] | None = None) -> torch.Tensor:
     """Same result as screening_core, evaluated per block of `chunk` queries
     against only the keys inside the largest window (the softmask of
     multiscreen/attention.py:118 is exactly zero for |i - j| >= w), so large T
-    never builds a T x T matrix."""
+    never builds a T x T matrix.  dropout = (threshold, seed) applies the
+    CUDA path's dropout mask to alpha (attention.py:190)."""
     B, Tq, H, D = q.shape
     Tk = k.shape[1]
     dmax = int(math.ceil(float(w.detach().max()))) - 1 if H > 0 else -1
@@ -109,6 +159,10 @@ def screening_core_windowed(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, r
         alpha = alpha * m.unsqueeze(0)
         if key_padding_mask is not None:
             alpha = alpha.masked_fill(key_padding_mask[:, lo:hi + 1].unsqueeze(1).unsqueeze(2), 0.0)
+        if dropout is not None and dropout[0] > 0:
+            keep = dropout_keep(dropout[1], dropout[0], B, H, torch.arange(i0, i1),
+                                torch.arange(lo, hi + 1))
+            alpha = alpha * keep.to(alpha.dtype)
         outs.append(torch.matmul(alpha, vh[:, :, lo:hi + 1]))
     out = torch.cat(outs, dim=2) if outs else torch.zeros(B, H, 0, D, dtype=q.dtype)
     return tanh_norm(out, eps).transpose(1, 2)

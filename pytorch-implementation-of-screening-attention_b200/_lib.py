@@ -35,6 +35,8 @@ class FwdArgs(ctypes.Structure):
         ("nq", c_void_p), ("nk", c_void_p), ("nv", c_void_p),
         ("y", c_void_p), ("no", c_void_p), ("tile_stats", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("dropout_threshold", ctypes.c_uint32), ("_pad1", ctypes.c_uint32),
+        ("dropout_seed", ctypes.c_uint64),
     ]
 
 
@@ -55,6 +57,8 @@ class BwdArgs(ctypes.Structure):
         ("dv", c_void_p), ("dv_sb", c_int64), ("dv_st", c_int64),
         ("dr", c_void_p), ("dw", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("dropout_threshold", ctypes.c_uint32), ("_pad1", ctypes.c_uint32),
+        ("dropout_seed", ctypes.c_uint64),
     ]
 
 
@@ -92,9 +96,9 @@ EXPORTED = (
     "screen_decode", "screen_decode_workspace_size", "screen_tanhnorm_fwd",
     "screen_tanhnorm_bwd", "screen_strerror", "screen_version", "screen_sizeof_args",
     "screen_last_cuda_error", "screen_decode_noalloc", "screen_fwd_workspace_size",
-    "screen_device_status",
+    "screen_device_status", "screen_dropout_bits",
 )
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _lib = None
 
@@ -125,6 +129,9 @@ def load() -> ctypes.CDLL:
                                         c_void_p]
     lib.screen_tanhnorm_bwd.argtypes = [c_int32, c_int64, c_int32, c_float, c_void_p, c_void_p,
                                         c_void_p, c_void_p]
+    lib.screen_dropout_bits.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
+                                        ctypes.c_uint32]
+    lib.screen_dropout_bits.restype = ctypes.c_uint32
     lib.screen_strerror.argtypes = [ctypes.c_int]
     lib.screen_strerror.restype = ctypes.c_char_p
     lib.screen_last_cuda_error.restype = ctypes.c_char_p
@@ -184,13 +191,27 @@ def _kpm(mask):
     return mask.to(torch.bool).contiguous().view(torch.uint8)
 
 
+def dropout_threshold(p: float) -> int:
+    """The kernels' 32-bit drop threshold for probability p (0 <= p < 1): a
+    score is dropped iff its counter bits are below it."""
+    if not 0.0 <= p < 1.0:
+        raise ValueError(f"dropout probability {p} outside [0, 1)")
+    return min(int(p * 4294967296.0), 4294967295)
+
+
+def dropout_bits(seed: int, bh: int, i: int, j: int) -> int:
+    """Counter bits of score (bh, query i, key j) for `seed` (the library's
+    screen_dropout_bits)."""
+    return int(load().screen_dropout_bits(seed & (2**64 - 1), bh, i, j))
+
+
 def screen_fwd(q, k, v, r, w, causal=True, key_padding_mask=None, eps=1e-8, q_offset=0,
-               tile_stats=None, norms=None, stages=0):
+               tile_stats=None, norms=None, stages=0, dropout=None):
     """Fused forward on raw projections q (B,Tq,H,D), k/v (B,Tk,H,D) (any
     batch/time strides); r, w (H,).  Returns (y, no, nq, nk, nv, q, k, v)
     where q, k, v are the (possibly re-laid-out) inputs the kernel read --
     the tensors to keep for the backward.  `norms` = (nq, nk, nv) skips the
-    norm pass."""
+    norm pass.  `dropout` = (threshold, seed) drops alpha (attention.py:190)."""
     _require_cuda(q, k, v, r, w, key_padding_mask)
     lib = load()
     q, k, v = _bthd(q), _bthd(k), _bthd(v)
@@ -223,6 +244,8 @@ def screen_fwd(q, k, v, r, w, causal=True, key_padding_mask=None, eps=1e-8, q_of
                 kpm_sb=0 if kpm is None else kpm.stride(0),
                 nq=_ptr(nq), nk=_ptr(nk), nv=_ptr(nv), y=_ptr(y), no=_ptr(no),
                 tile_stats=_ptr(tile_stats))
+    if dropout is not None:
+        a.dropout_threshold, a.dropout_seed = int(dropout[0]), int(dropout[1]) & (2**64 - 1)
     nbytes = int(lib.screen_fwd_workspace_size(ctypes.byref(a)))
     ws = None
     if nbytes:
@@ -259,9 +282,10 @@ SCREEN_BWD_DETERMINISTIC = 16
 
 
 def screen_bwd(q, k, v, nq, nk, nv, y, no, dy, r, w, causal=True, key_padding_mask=None,
-               eps=1e-8, q_offset=0, out=None, stages=0):
+               eps=1e-8, q_offset=0, out=None, stages=0, dropout=None):
     """Backward of screen_fwd.  Returns dq, dk, dv ((B,T,H,D); written into
-    `out` = (dq, dk, dv) views when given) and dr, dw (H,) float32."""
+    `out` = (dq, dk, dv) views when given) and dr, dw (H,) float32.
+    `dropout` must be the (threshold, seed) the forward used."""
     _require_cuda(dy)
     lib = load()
     dy = _bthd(dy.to(y.dtype))
@@ -294,6 +318,8 @@ def screen_bwd(q, k, v, nq, nk, nv, y, no, dy, r, w, causal=True, key_padding_ma
                 dk=_ptr(dk), dk_sb=dk.stride(0), dk_st=dk.stride(1),
                 dv=_ptr(dv), dv_sb=dv.stride(0), dv_st=dv.stride(1),
                 dr=_ptr(dr), dw=_ptr(dw))
+    if dropout is not None:
+        a.dropout_threshold, a.dropout_seed = int(dropout[0]), int(dropout[1]) & (2**64 - 1)
     nbytes = lib.screen_bwd_workspace_size(ctypes.byref(a))
     ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
     a.workspace = ws.data_ptr()

@@ -25,9 +25,10 @@ from .sequence_parallel import current_shard, screening_attention_sharded
 class ScreeningAttention(nn.Module):
     """Multi-head Screening Attention.
 
-    Args match the reference: d_model, num_heads, dropout (on alpha; the fused
-    kernels implement p = 0 only and raise in training mode for p > 0),
-    causal, eps.
+    Args match the reference: d_model, num_heads, dropout (on alpha, applied
+    in training mode as nn.Dropout does, attention.py:190; the fused kernels
+    draw the mask from a counter-based hash seeded from torch's default
+    generator, so it is not bit-identical to torch's dropout), causal, eps.
     """
 
     def __init__(self, d_model: int, num_heads: int, dropout: float = 0.0, causal: bool = True,
@@ -72,19 +73,21 @@ class ScreeningAttention(nn.Module):
         v = self.v_proj(value).view(B, Tk, H, D)
         return q, k, v
 
-    def _check_dropout(self):
-        if self.training and self.attn_dropout.p > 0 and torch.is_grad_enabled():
-            raise NotImplementedError(
-                "attention dropout > 0 in training is not implemented by the fused kernels")
+    def _dropout_p(self) -> float:
+        """Attention dropout probability of this call (0 outside training)."""
+        return float(self.attn_dropout.p) if self.training else 0.0
 
     def forward(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                 key_padding_mask: torch.Tensor | None = None) -> torch.Tensor:
         """query (B,T_q,d_model), key/value (B,T_k,d_model),
         key_padding_mask (B,T_k) bool, True = ignore.  Returns (B,T_q,d_model)."""
-        self._check_dropout()
+        p = self._dropout_p()
         B, Tq, _ = query.shape
         shard = current_shard() if self.causal else None
         if shard is not None and query is key and key is value:
+            if p > 0:
+                raise NotImplementedError(
+                    "attention dropout with a sequence-sharded input is not implemented")
             # causal self-attention of one block of a sequence-sharded input:
             # the K/V halo before the block comes from the previous ranks
             q, k, v = self._qkv(query, key, value)
@@ -99,11 +102,13 @@ class ScreeningAttention(nn.Module):
             qkv = F.linear(query, wqkv).view(B, Tq, 3, H, D)
             y = screening_attention_packed(qkv, self.sharpness(), self.window(),
                                            causal=self.causal,
-                                           key_padding_mask=key_padding_mask, eps=self.eps)
+                                           key_padding_mask=key_padding_mask, eps=self.eps,
+                                           dropout_p=p)
         else:
             q, k, v = self._qkv(query, key, value)
             y = screening_attention(q, k, v, self.sharpness(), self.window(), causal=self.causal,
-                                    key_padding_mask=key_padding_mask, eps=self.eps)
+                                    key_padding_mask=key_padding_mask, eps=self.eps,
+                                    dropout_p=p)
         return self.out_proj(y.reshape(B, Tq, self.d_model))
 
     # ------------------------------------------------------------------

@@ -50,6 +50,8 @@ Family family_choice() {
 }
 bool use_tc_fwd(int dtype, int D) { return family_choice() == FAM_TC && tc_supported(dtype, D); }
 bool use_mma(int dtype, int D) { return family_choice() != FAM_SIMT && mma_supported(dtype, D); }
+// the warp-level mma.sync kernels have no dropout; with dropout the SIMT family serves
+bool use_mma_drop(int dtype, int D, uint32_t drop_thr) { return drop_thr == 0 && use_mma(dtype, D); }
 
 int common_checks(int dtype, int B, int H, int Tq, int Tk, int D) {
   if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;
@@ -59,10 +61,15 @@ int common_checks(int dtype, int B, int H, int Tq, int Tk, int D) {
 }
 
 AttnShape make_shape(int B, int H, int Tq, int Tk, int causal, long long q_offset, float eps,
-                     const float* r, const float* w, const uint8_t* kpm, long long kpm_sb) {
+                     const float* r, const float* w, const uint8_t* kpm, long long kpm_sb,
+                     uint32_t drop_thr = 0, uint64_t seed = 0) {
   AttnShape s;
   s.B = B; s.H = H; s.Tq = Tq; s.Tk = Tk; s.causal = causal; s.q_offset = q_offset;
   s.eps = eps; s.r = r; s.w = w; s.kpm = kpm; s.kpm_sb = kpm_sb;
+  s.drop_thr = drop_thr;
+  s.drop_scale = drop_thr ? (float)(4294967296.0 / (4294967296.0 - (double)drop_thr)) : 1.0f;
+  s.seed_lo = (uint32_t)seed;
+  s.seed_hi = (uint32_t)(seed >> 32);
   return s;
 }
 
@@ -73,10 +80,11 @@ struct BwdLayout {
 BwdLayout bwd_layout(const screen_bwd_args* a) {
   BwdLayout L;
   AttnShape s = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
-                           a->key_padding_mask, a->kpm_sb);
+                           a->key_padding_mask, a->kpm_sb, a->dropout_threshold,
+                           a->dropout_seed);
   const bool tc = use_tc_fwd(a->dtype, a->D);
   L.P = tc ? tc_bwd_partials(s)
-           : (use_mma(a->dtype, a->D) ? mma_bwd_partials(a->D, s) : simt_bwd_partials(s));
+           : (use_mma_drop(a->dtype, a->D, a->dropout_threshold) ? mma_bwd_partials(a->D, s) : simt_bwd_partials(s));
   L.g_off = 0;
   // G: fp32, or two bf16 planes (hi, lo) on the tensor-core path -- 4 bytes/elem either way
   L.pr_off = round_up((size_t)a->B * a->Tq * a->H * a->D * 4);
@@ -151,7 +159,8 @@ int screen_fwd(const screen_fwd_args* a, screen_stream_t stream) {
   }
   if (!nq || !(stages & 2)) return SCREEN_OK;
   AttnShape sh = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
-                            a->key_padding_mask, a->kpm_sb);
+                            a->key_padding_mask, a->kpm_sb, a->dropout_threshold,
+                           a->dropout_seed);
   FwdPtrs p{Rows{a->q, a->q_sb, a->q_st}, Rows{a->k, a->k_sb, a->k_st},
             Rows{a->v, a->v_sb, a->v_st}, a->nq, a->nk, a->nv, a->y, a->no, a->tile_stats};
   if (tc) {
@@ -159,18 +168,26 @@ int screen_fwd(const screen_fwd_args* a, screen_stream_t stream) {
     if (need > 0 && (!a->workspace || a->workspace_bytes < need || !al16(a->workspace)))
       return SCREEN_ERR_WORKSPACE;
     if ((st = tc_fwd(sh, p, a->workspace, a->norms_given || !(stages & 1), s))) return st;
-  } else if (use_mma(a->dtype, a->D))
+  } else if (use_mma_drop(a->dtype, a->D, a->dropout_threshold))
     mma_fwd(a->D, sh, p, s);
   else
     simt_fwd(a->dtype, a->D, sh, p, s);
   return check_launch();
 }
 
+uint32_t screen_dropout_bits(uint64_t seed, uint32_t bh, uint32_t i, uint32_t j) {
+  AttnShape sh{};
+  sh.seed_lo = (uint32_t)seed;
+  sh.seed_hi = (uint32_t)(seed >> 32);
+  return drop_mix(drop_row(drop_bh_key(sh, bh), i) ^ (j * kDropColMul));
+}
+
 size_t screen_fwd_workspace_size(const screen_fwd_args* a) {
   if (!a || common_checks(a->dtype, a->B, a->H, a->Tq, a->Tk, a->D)) return 0;
   if (!use_tc_fwd(a->dtype, a->D)) return 0;
   AttnShape sh = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
-                            a->key_padding_mask, a->kpm_sb);
+                            a->key_padding_mask, a->kpm_sb, a->dropout_threshold,
+                           a->dropout_seed);
   return round_up(tc_fwd_workspace(sh));
 }
 
@@ -210,17 +227,18 @@ int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
   float* pw = reinterpret_cast<float*>(ws + L.pw_off);
   if (nq && (stages & 1))
     tanhnorm_grad_from_y(a->dtype, a->D, a->y, a->no, a->dy, a->dy_sb, a->dy_st, G,
-                         use_mma(a->dtype, a->D), a->B, a->Tq, a->H, a->eps, s);
+                         use_mma_drop(a->dtype, a->D, a->dropout_threshold), a->B, a->Tq, a->H, a->eps, s);
   if ((st = check_launch())) return st;
   AttnShape sh = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
-                            a->key_padding_mask, a->kpm_sb);
+                            a->key_padding_mask, a->kpm_sb, a->dropout_threshold,
+                           a->dropout_seed);
   BwdPtrs p{Rows{a->q, a->q_sb, a->q_st}, Rows{a->k, a->k_sb, a->k_st},
             Rows{a->v, a->v_sb, a->v_st}, a->nq, a->nk, a->nv, G,
             OutRows{a->dq, a->dq_sb, a->dq_st}, OutRows{a->dk, a->dk_sb, a->dk_st},
             OutRows{a->dv, a->dv_sb, a->dv_st}, pr, pw};
   if (use_tc_fwd(a->dtype, a->D)) {
     if ((st = tc_bwd(sh, p, ws + L.aux_off, stages, s))) return st;
-  } else if (use_mma(a->dtype, a->D))
+  } else if (use_mma_drop(a->dtype, a->D, a->dropout_threshold))
     mma_bwd(a->D, sh, p, stages, s);
   else
     simt_bwd(a->dtype, a->D, sh, p, stages, s);

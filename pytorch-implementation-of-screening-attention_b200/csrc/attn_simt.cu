@@ -69,6 +69,8 @@ __global__ void __launch_bounds__(256) simt_fwd_kernel(AttnShape s, FwdPtrs p) {
   load_unit<T, D>(p.q, p.nq, b, i, s.Tq, s.H, h, q, lane);
 #pragma unroll
   for (int e = 0; e < NE; ++e) o[e] = 0.f;
+  // attention dropout (attention.py:190): this query row's counter key
+  const uint32_t drow = drop_row(drop_bh_key(s, (uint32_t)bh), (uint32_t)i);
 
   for (long long j = lo; j <= hi && dmax >= 0; ++j) {
     if (key_masked(s, b, j)) continue;
@@ -78,7 +80,7 @@ __global__ void __launch_bounds__(256) simt_fwd_kernel(AttnShape s, FwdPtrs p) {
     for (int e = 0; e < NE; ++e) dot += q[e] * kv[e];
     const float sim = warp_sum(dot);
     const float t = 1.0f - r * (1.0f - sim);
-    if (t > 0.f) {
+    if (t > 0.f && drop_keep(drow, (uint32_t)j, s.drop_thr)) {
       const float rel = (float)(j - pos);
       const float m = 0.5f * (cosf(kPi * rel / w) + 1.0f);
       const float alpha = t * t * m;
@@ -87,6 +89,9 @@ __global__ void __launch_bounds__(256) simt_fwd_kernel(AttnShape s, FwdPtrs p) {
       for (int e = 0; e < NE; ++e) o[e] += alpha * kv[e];
     }
   }
+  // kept scores carry the dropout scale 1 / (1 - p)
+#pragma unroll
+  for (int e = 0; e < NE; ++e) o[e] *= s.drop_scale;
   float ss = 0.f;
 #pragma unroll
   for (int e = 0; e < NE; ++e) ss += o[e] * o[e];
@@ -123,8 +128,9 @@ __global__ void __launch_bounds__(256) simt_bwd_dq_kernel(AttnShape s, BwdPtrs p
   load_row<float, D>(reinterpret_cast<const float*>(p.G) + qrow * D, g, lane);
 #pragma unroll
   for (int e = 0; e < NE; ++e) dq[e] = 0.f;
+  const uint32_t drow = drop_row(drop_bh_key(s, (uint32_t)bh), (uint32_t)i);
   for (long long j = lo; j <= hi && dmax >= 0; ++j) {
-    if (key_masked(s, b, j)) continue;
+    if (key_masked(s, b, j) || !drop_keep(drow, (uint32_t)j, s.drop_thr)) continue;
     load_unit<T, D>(p.k, p.nk, b, j, s.Tk, s.H, h, kk, lane);
     load_unit<T, D>(p.v, p.nv, b, j, s.Tk, s.H, h, vv, lane);
     float d1 = 0.f, d2 = 0.f;
@@ -144,6 +150,8 @@ __global__ void __launch_bounds__(256) simt_bwd_dq_kernel(AttnShape s, BwdPtrs p
       for (int e = 0; e < NE; ++e) dq[e] += dS * kk[e];
     }
   }
+#pragma unroll
+  for (int e = 0; e < NE; ++e) dq[e] *= s.drop_scale;
   float dot = 0.f;
 #pragma unroll
   for (int e = 0; e < NE; ++e) dot += q[e] * dq[e];
@@ -184,7 +192,9 @@ __global__ void __launch_bounds__(256) simt_bwd_dkdv_kernel(AttnShape s, BwdPtrs
       long long ilo = plo - s.q_offset, ihi = phi - s.q_offset;
       if (ilo < 0) ilo = 0;
       if (ihi > s.Tq - 1) ihi = s.Tq - 1;
+      const uint32_t bhk = drop_bh_key(s, (uint32_t)bh);
       for (long long i = ilo; i <= ihi; ++i) {
+        if (s.drop_thr && !drop_keep(drop_row(bhk, (uint32_t)i), (uint32_t)j, s.drop_thr)) continue;
         const long long qrow = ((long long)b * s.Tq + i) * s.H + h;
         load_unit<T, D>(p.q, p.nq, b, i, s.Tq, s.H, h, qq, lane);
         load_row<float, D>(Gp + qrow * D, gg, lane);
@@ -214,6 +224,14 @@ __global__ void __launch_bounds__(256) simt_bwd_dkdv_kernel(AttnShape s, BwdPtrs
         }
       }
     }
+    // kept scores carry the dropout scale
+#pragma unroll
+    for (int e = 0; e < NE; ++e) {
+      dk[e] *= s.drop_scale;
+      dv[e] *= s.drop_scale;
+    }
+    acc_r *= s.drop_scale;
+    acc_w *= s.drop_scale;
     // normalisation Jacobians
     float d1 = 0.f, d2 = 0.f;
 #pragma unroll

@@ -87,6 +87,8 @@ __device__ unsigned long long g_fwd_prof[16];
 #define PROF_ADD(slot) do {} while (0)
 #endif
 
+// kDrop: attention dropout on alpha (counter-based bits, AttnShape::drop_thr)
+template <bool kDrop>
 __global__ void __launch_bounds__(kThreads, 2)
     tc_fwd_kernel(AttnShape s, FwdPtrs p, const float* __restrict__ ikT,
                   const float4* __restrict__ ikmeta, int Tkp, const int* __restrict__ order,
@@ -290,6 +292,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const float2 rq2 = make_float2(rq, rq), omr2 = make_float2(omr, omr);
     const float2 cr2 = make_float2(crow, crow), sr2 = make_float2(srow, srow);
     const float2 half2 = make_float2(0.5f, 0.5f);
+    // attention dropout: this query row's counter key
+    const uint32_t drow = kDrop ? drop_row(drop_bh_key(s, (uint32_t)bh), (uint32_t)i) : 0u;
     // alpha of columns (c, c+1) from the pair's S, 1/|k|, cos, sin
     auto pair_alpha = [&](float s0, float s1, float ik0, float ik1, float c0, float c1, float n0,
                           float n1, bool k0, bool k1) -> uint32_t {
@@ -376,15 +380,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float4* ik4 = reinterpret_cast<const float4*>(col);
         const float4* cc4 = reinterpret_cast<const float4*>(col + kBN);
         const float4* sc4 = reinterpret_cast<const float4*>(col + 2 * kBN);
+        // dropout: key j of column c is kept iff its counter bits clear the threshold
+        const uint32_t jgk = (uint32_t)(j0i + kNC * g);
+        auto kp = [&](int c) -> bool {
+          return !kDrop || drop_keep(drow, jgk + (uint32_t)c, s.drop_thr);
+        };
         if (inside) {
 #pragma unroll
           for (int q4 = 0; q4 < kNC / 4; ++q4) {
             const float4 ikv = ik4[q4], ccv = cc4[q4], scv = sc4[q4];
             const int c = 4 * q4;
             pk[2 * q4] = pair_alpha(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), ikv.x,
-                                    ikv.y, ccv.x, ccv.y, scv.x, scv.y, true, true);
+                                    ikv.y, ccv.x, ccv.y, scv.x, scv.y, kp(c), kp(c + 1));
             pk[2 * q4 + 1] = pair_alpha(__uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]),
-                                        ikv.z, ikv.w, ccv.z, ccv.w, scv.z, scv.w, true, true);
+                                        ikv.z, ikv.w, ccv.z, ccv.w, scv.z, scv.w, kp(c + 2),
+                                        kp(c + 3));
           }
         } else {
           // window edge: this row's valid columns are the interval [clo, chi]
@@ -398,11 +408,12 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int c = 4 * q4;
             pk[2 * q4] = pair_alpha(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), ikv.x,
                                     ikv.y, ccv.x, ccv.y, scv.x, scv.y,
-                                    c >= iclo && c <= ichi, c + 1 >= iclo && c + 1 <= ichi);
+                                    c >= iclo && c <= ichi && kp(c),
+                                    c + 1 >= iclo && c + 1 <= ichi && kp(c + 1));
             pk[2 * q4 + 1] = pair_alpha(__uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]),
                                         ikv.z, ikv.w, ccv.z, ccv.w, scv.z, scv.w,
-                                        c + 2 >= iclo && c + 2 <= ichi,
-                                        c + 3 >= iclo && c + 3 <= ichi);
+                                        c + 2 >= iclo && c + 2 <= ichi && kp(c + 2),
+                                        c + 3 >= iclo && c + 3 <= ichi && kp(c + 3));
           }
         }
       } else {
@@ -454,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                   *reinterpret_cast<uint32_t(*)[32]>(&ov[32 * h32]));
       tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < kOC; ++c) o[c] = __uint_as_float(ov[c]);
+      for (int c = 0; c < kOC; ++c) o[c] = __uint_as_float(ov[c]) * (kDrop ? s.drop_scale : 1.0f);
     } else {
 #pragma unroll
       for (int c = 0; c < kOC; ++c) o[c] = 0.f;
@@ -623,7 +634,9 @@ int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_giv
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !g_tc_attr[dev]) {
-    cudaFuncSetAttribute(tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(tc_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kSmemBytes);
+    cudaFuncSetAttribute(tc_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kSmemBytes);
     g_tc_attr[dev] = true;
   }
@@ -657,8 +670,12 @@ int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_giv
     return SCREEN_ERR_CUDA;
   const int nqt = (s.Tq + kBM - 1) / kBM;
   tile_order(s, 0, nqt, order, st);
-  tc_fwd_kernel<<<(unsigned)(BH * nqt), kThreads, kSmemBytes, st>>>(s, p, ikT, meta, (int)Tkp,
-                                                                    order, tq, tk, tv);
+  if (s.drop_thr)
+    tc_fwd_kernel<true><<<(unsigned)(BH * nqt), kThreads, kSmemBytes, st>>>(
+        s, p, ikT, meta, (int)Tkp, order, tq, tk, tv);
+  else
+    tc_fwd_kernel<false><<<(unsigned)(BH * nqt), kThreads, kSmemBytes, st>>>(
+        s, p, ikT, meta, (int)Tkp, order, tq, tk, tv);
   return SCREEN_OK;
 }
 

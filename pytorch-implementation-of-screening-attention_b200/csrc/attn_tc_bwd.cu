@@ -192,6 +192,8 @@ constexpr uint32_t SMEM = OFF_MISC + 64 + 1024;
 static_assert(2 * (SMEM + 1024) <= 228 * 1024, "two CTAs per SM");
 }  // namespace dq
 
+// kDrop: attention dropout on alpha (counter-based bits, AttnShape::drop_thr)
+template <bool kDrop>
 __global__ void __launch_bounds__(kThreads, 2)
     tc_bwd_dq_kernel(AttnShape s, BwdPtrs p, Aux ax, const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmK,
@@ -373,6 +375,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const long long i = i0 + t;
     const float iq = (i < s.Tq) ? ax.iqT[(long long)bh * ax.Tqp + i] : 0.f;
     const float rq = r * iq;
+    // attention dropout: this query row's counter key
+    const uint32_t drow = kDrop ? drop_row(drop_bh_key(s, (uint32_t)bh), (uint32_t)i) : 0u;
     float crow, srow;
     {
       float sn, cs;
@@ -445,6 +449,11 @@ __global__ void __launch_bounds__(kThreads, 2)
                 a0 = (c >= iclo && c <= ichi) ? a0 : 0.f;
                 a1 = (c + 1 >= iclo && c + 1 <= ichi) ? a1 : 0.f;
               }
+              if (kDrop) {
+                const uint32_t jk = (uint32_t)(j0i + cb + c);
+                a0 = drop_keep(drow, jk, s.drop_thr) ? a0 : 0.f;
+                a1 = drop_keep(drow, jk + 1u, s.drop_thr) ? a1 : 0.f;
+              }
               const float2 a2 = make_float2(a0, a1);
               const float2 m2 = __ffma2_rn(cr2, cc2, __ffma2_rn(sr2, sc2, half2));
               // dS / (2 r) = (G v) (1/|v| 1/|k|) m a; the 2 r goes to the epilogue
@@ -484,7 +493,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       bf16* orow = reinterpret_cast<bf16*>(p.dq.p) + (long long)b * p.dq.sb + ii * p.dq.st +
                    (long long)h * kD;
       // dS was stored without its 2 r
-      store_unit_jacobian_tmem(tmem + TMq_ACC + lane_off, ok && misc[3], 2.0f * r, qrow, iq,
+      store_unit_jacobian_tmem(tmem + TMq_ACC + lane_off, ok && misc[3],
+                               2.0f * r * (kDrop ? s.drop_scale : 1.0f), qrow, iq,
                                orow, st_row);
     }
   }
@@ -507,8 +517,9 @@ constexpr uint32_t STAGE = 3 * TILE_B;
 // [128 keys][64 queries] bf16 (SW128), 16 KB apart (the operand's LBO)
 constexpr uint32_t OFF_STG = OFF_Q + kNS * STAGE;
 constexpr uint32_t STG_PAIR = 2 * TILE_A;
-constexpr uint32_t OFF_COL = OFF_STG + 2 * STG_PAIR;    // per stage iq | cos | sin [64] + meta
-constexpr uint32_t COLB = 3 * kBN * 4 + 16;
+// per stage: iq | cos | sin [64] + meta (16 B) + dropout row keys of the 64 queries
+constexpr uint32_t OFF_COL = OFF_STG + 2 * STG_PAIR;
+constexpr uint32_t COLB = 3 * kBN * 4 + 16 + kBN * 4;
 constexpr uint32_t OFF_TAB = OFF_COL + kNS * COLB;
 constexpr uint32_t OFF_RED = OFF_TAB + 2 * kBN * 4;     // [2][8] dr / dw warp sums
 constexpr uint32_t OFF_BAR = OFF_RED + 64 * 4;
@@ -528,7 +539,8 @@ constexpr uint32_t TK_S = 0, TK_DP = 128, TK_ACCV = 256, TK_ACCK = 320, TK_ACCQ 
 // kFuse: dQ is computed here too (dQ += dS K on the tensor cores per pair of
 // query tiles, added into an fp32 accumulator with vector reductions);
 // otherwise tc_bwd_dq_kernel computes it (deterministic order)
-template <bool kFuse>
+// kDrop: attention dropout on alpha (counter-based bits, AttnShape::drop_thr)
+template <bool kFuse, bool kDrop>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_bwd_kv_kernel(AttnShape s, BwdPtrs p, Aux ax, const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmK,
@@ -626,6 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     const float cphi0 = tab[lane], sphi0 = tab[kBN + lane];
     const float cphi1 = tab[lane + 32], sphi1 = tab[kBN + lane + 32];
+    const uint32_t dbhk = kDrop ? drop_bh_key(s, (uint32_t)bh) : 0u;
     const float* iqh = ax.iqT + (long long)bh * ax.Tqp;
     const float4* mh = ax.mq + (long long)bh * (ax.Tqp / kBN);
     int issued = 0;
@@ -669,6 +682,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       col[2 * kBN + lane] = sb * cphi0 + cbv * sphi0;
       col[kBN + lane + 32] = cbv * cphi1 - sb * sphi1;
       col[2 * kBN + lane + 32] = sb * cphi1 + cbv * sphi1;
+      if constexpr (kDrop) {
+        // dropout row keys of this tile's query indices
+        uint32_t* dk = reinterpret_cast<uint32_t*>(col + 3 * kBN + 4);
+        dk[lane] = drop_row(dbhk, (uint32_t)(iq0 + lane));
+        dk[lane + 32] = drop_row(dbhk, (uint32_t)(iq0 + lane + 32));
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_FULL + st));
 #ifdef SCREEN_BWD_PROFILE
@@ -843,7 +862,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float2 iv2 = make_float2(iv, iv), ik2 = make_float2(ik, ik);
     const float2 m1 = make_float2(-1.f, -1.f);
     // dS for the dQ MMA: dq^ = sum_j dS k^ = sum_j dS (1/|k|) K, dS = (G v)(1/|v|) m 2 a r
-    const float rq_f = 2.0f * r * iv * ik;
+    const float rq_f = 2.0f * r * iv * ik * (kDrop ? s.drop_scale : 1.0f);
     const float2 rqf2 = make_float2(rq_f, rq_f);
     float2 accr2 = make_float2(0.f, 0.f), accw2 = make_float2(0.f, 0.f);
     bool ok = true;
@@ -956,6 +975,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float4* iq4 = reinterpret_cast<const float4*>(col + cb);
         const float4* cv4 = reinterpret_cast<const float4*>(col + kBN + cb);
         const float4* sv4 = reinterpret_cast<const float4*>(col + 2 * kBN + cb);
+        const uint32_t* dkey = reinterpret_cast<const uint32_t*>(col + 3 * kBN + 4) + cb;
         uint32_t pa[16], pd[16];
         // interior tiles run without the window-edge selects
         auto run = [&](auto edge) {
@@ -976,6 +996,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (EDGE) {
                 a0 = (c >= iclo && c <= ichi) ? a0 : 0.f;
                 a1 = (c + 1 >= iclo && c + 1 <= ichi) ? a1 : 0.f;
+              }
+              if (kDrop) {
+                a0 = drop_keep(dkey[c], (uint32_t)jr, s.drop_thr) ? a0 : 0.f;
+                a1 = drop_keep(dkey[c + 1], (uint32_t)jr, s.drop_thr) ? a1 : 0.f;
               }
               const float2 a2 = make_float2(a0, a1);
               const float2 m2 = __ffma2_rn(cr2, cv2, __ffma2_rn(sr2, sn2, half2));
@@ -1072,8 +1096,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (kFuse && ok && todo >= 0) ok = drain(todo, todo_qt);
     // every reduce this warp issued completes before the CTA's shared memory goes away
     if (kFuse && lane == 0) bulk_wait<0>();
-    acc_r = 2.f * iv * (accr2.x + accr2.y);   // dr = sum dP m 2a (S - 1)
-    acc_w = iv * (accw2.x + accw2.y);
+    // dr = sum dP m 2a (S - 1); kept scores carry the dropout scale
+    const float dsc = kDrop ? s.drop_scale : 1.0f;
+    acc_r = 2.f * iv * dsc * (accr2.x + accr2.y);
+    acc_w = iv * dsc * (accw2.x + accw2.y);
     // epilogue: warpgroup 0 -> dk, warpgroup 1 -> dv (normalisation Jacobians)
     ok = ok && mbar_wait(bar(BAR_DONE), 0, abort_flag, kWaitLimitNs);
     // tcgen05.ld is warp-collective: every lane takes the same branch
@@ -1090,11 +1116,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (g == 0) {
         // dS was stored without this key's 2 r / |v|
 #pragma unroll
-        for (int c = 0; c < 64; ++c) acc[c] *= 2.0f * r * iv;
+        for (int c = 0; c < 64; ++c) acc[c] *= 2.0f * r * iv * dsc;
         store_unit_jacobian(acc, kh + jrow * p.k.st, ik,
                             reinterpret_cast<bf16*>(p.dk.p) + (long long)b * p.dk.sb +
                                 jrow * p.dk.st + (long long)h * kD);
       } else {
+        if (kDrop) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) acc[c] *= dsc;
+        }
         store_unit_jacobian(acc, vh + jrow * p.v.st, iv,
                             reinterpret_cast<bf16*>(p.dv.p) + (long long)b * p.dv.sb +
                                 jrow * p.dv.st + (long long)h * kD);
@@ -1222,12 +1252,18 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !g_bwd_attr[dev]) {
-    cudaFuncSetAttribute(tc_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(tc_bwd_dq_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)dq::SMEM);
-    cudaFuncSetAttribute(tc_bwd_kv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kv::SMEM);
-    cudaFuncSetAttribute(tc_bwd_kv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kv::SMEM);
+    cudaFuncSetAttribute(tc_bwd_dq_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)dq::SMEM);
+    cudaFuncSetAttribute(tc_bwd_kv_kernel<true, false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
+    cudaFuncSetAttribute(tc_bwd_kv_kernel<false, false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
+    cudaFuncSetAttribute(tc_bwd_kv_kernel<true, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
+    cudaFuncSetAttribute(tc_bwd_kv_kernel<false, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
     g_bwd_attr[dev] = true;
   }
   const long long BH = (long long)s.B * s.H, Tqp = padT(s.Tq), Tkp = padT(s.Tk);
@@ -1271,13 +1307,20 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
     // dq by its own query-major kernel: every sum in a fixed order
     if (s.Tq > 0 && (stages & 2)) {
       dim3 g1((s.Tq + kBM - 1) / kBM, s.B * s.H);
-      tc_bwd_dq_kernel<<<g1, kThreads, dq::SMEM, st>>>(s, p, ax, tq128, tg128, tk64, tv64);
+      if (s.drop_thr)
+        tc_bwd_dq_kernel<true><<<g1, kThreads, dq::SMEM, st>>>(s, p, ax, tq128, tg128, tk64, tv64);
+      else
+        tc_bwd_dq_kernel<false><<<g1, kThreads, dq::SMEM, st>>>(s, p, ax, tq128, tg128, tk64, tv64);
     }
     if (s.Tk > 0 && (stages & 4)) {
       const int nkt = (s.Tk + kBM - 1) / kBM;
       tile_order(s, 1, nkt, order, st);
-      tc_bwd_kv_kernel<false><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(s, p, ax, tq64, tg64, tk128, tv128,
-                                                              tq64);
+      if (s.drop_thr)
+        tc_bwd_kv_kernel<false, true><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(
+            s, p, ax, tq64, tg64, tk128, tv128, tq64);
+      else
+        tc_bwd_kv_kernel<false, false><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(
+            s, p, ax, tq64, tg64, tk128, tv128, tq64);
     }
     return SCREEN_OK;
   }
@@ -1294,8 +1337,12 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
       tile_order(s, 1, nkt, order, st);
       CUtensorMap tdq;
       if (!make_tmap_dq(&tdq, dq_acc, s.B, s.Tq, s.H)) return SCREEN_ERR_CUDA;
-      tc_bwd_kv_kernel<true><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(s, pf, ax, tq64, tg64, tk128, tv128,
-                                                             tdq);
+      if (s.drop_thr)
+        tc_bwd_kv_kernel<true, true><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(
+            s, pf, ax, tq64, tg64, tk128, tv128, tdq);
+      else
+        tc_bwd_kv_kernel<true, false><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(
+            s, pf, ax, tq64, tg64, tk128, tv128, tdq);
     }
     const long long rows = BH * s.Tq;
     if (rows > 0)

@@ -40,7 +40,35 @@ struct AttnShape {
   const float* w;
   const uint8_t* kpm;   // (B,Tk) or null
   long long kpm_sb;
+  // attention dropout: score (bh, i, j) dropped iff drop_bits(...) < drop_thr;
+  // drop_thr = 0: none.  drop_scale = 2^32 / (2^32 - drop_thr) multiplies
+  // every output that is linear in alpha (o before TanhNorm, dq, dk, dv, dr, dw)
+  uint32_t drop_thr;
+  float drop_scale;
+  uint32_t seed_lo, seed_hi;
 };
+
+// Counter-based dropout bits (lowbias32 finalizer as the mixing function):
+// key of (seed, bh), row key of query i, bits of score (i, j).  The same
+// values on the host (screen_dropout_bits) and in every kernel family.
+__host__ __device__ __forceinline__ uint32_t drop_mix(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+__host__ __device__ __forceinline__ uint32_t drop_bh_key(const AttnShape& s, uint32_t bh) {
+  return drop_mix(s.seed_lo ^ drop_mix(s.seed_hi ^ (bh * 0x9E3779B1u)));
+}
+__host__ __device__ __forceinline__ uint32_t drop_row(uint32_t bhk, uint32_t i) {
+  return drop_mix(bhk ^ (i * 0x85EBCA77u));
+}
+constexpr uint32_t kDropColMul = 0xC2B2AE3Du;   // bits = drop_mix(row ^ j * kDropColMul)
+__host__ __device__ __forceinline__ bool drop_keep(uint32_t row, uint32_t j, uint32_t thr) {
+  return drop_mix(row ^ (j * kDropColMul)) >= thr;
+}
 
 struct FwdPtrs {
   Rows q, k, v;

@@ -18,13 +18,24 @@ import torch
 from . import _lib
 
 
+def _dropout_args(p: float, seed: int | None):
+    """(threshold, seed) for the kernels, None without dropout.  Without an
+    explicit seed one is drawn from torch's default CPU generator, so
+    torch.manual_seed makes the masks reproducible."""
+    if p <= 0.0:
+        return None
+    if seed is None:
+        seed = int(torch.randint(0, 2**62, (1,)).item())
+    return (_lib.dropout_threshold(p), int(seed))
+
+
 class ScreenFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, r, w, causal, key_padding_mask, eps, q_offset):
+    def forward(ctx, q, k, v, r, w, causal, key_padding_mask, eps, q_offset, dropout=None):
         y, no, nq, nk, nv, qq, kk, vv = _lib.screen_fwd(q, k, v, r, w, causal, key_padding_mask,
-                                                        eps, q_offset)
+                                                        eps, q_offset, dropout=dropout)
         ctx.save_for_backward(qq, kk, vv, nq, nk, nv, y, no, r, w, key_padding_mask)
-        ctx.causal, ctx.eps, ctx.q_offset = causal, eps, q_offset
+        ctx.causal, ctx.eps, ctx.q_offset, ctx.dropout = causal, eps, q_offset, dropout
         ctx.has_kpm = key_padding_mask is not None
         return y
 
@@ -32,22 +43,33 @@ class ScreenFn(torch.autograd.Function):
     def backward(ctx, dy):
         q, k, v, nq, nk, nv, y, no, r, w, kpm = ctx.saved_tensors
         dq, dk, dv, dr, dw = _lib.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, r, w, ctx.causal,
-                                             kpm if ctx.has_kpm else None, ctx.eps, ctx.q_offset)
+                                             kpm if ctx.has_kpm else None, ctx.eps, ctx.q_offset,
+                                             dropout=ctx.dropout)
         return (dq, dk, dv, dr.to(r.dtype) if ctx.needs_input_grad[3] else None,
-                dw.to(w.dtype) if ctx.needs_input_grad[4] else None, None, None, None, None)
+                dw.to(w.dtype) if ctx.needs_input_grad[4] else None, None, None, None, None,
+                None)
 
 
 def screening_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, r: torch.Tensor,
                         w: torch.Tensor, causal: bool = True,
                         key_padding_mask: torch.Tensor | None = None, eps: float = 1e-8,
-                        q_offset: int = 0) -> torch.Tensor:
+                        q_offset: int = 0, dropout_p: float = 0.0,
+                        dropout_seed: int | None = None) -> torch.Tensor:
     """y = TanhNorm(screen(q^, k^, v^; r, w)) on raw (B,T,H,D) projections.
 
     float32 and bfloat16 run natively; float16 inputs are computed in float32
     and cast back.  r, w are (H,) tensors (any float dtype; math in float32).
+    dropout_p > 0 drops alpha as nn.Dropout does (attention.py:190): each score
+    is zeroed with probability p, kept ones scaled by 1 / (1 - p); the mask is
+    a counter-based hash of (dropout_seed, b*H+h, i, j), regenerated in the
+    backward (see _lib.dropout_bits).
     """
     if not (q.is_cuda and k.is_cuda and v.is_cuda):
         raise RuntimeError("screening_attention runs on CUDA tensors only (no CPU path)")
+    if dropout_p >= 1.0:
+        # every alpha dropped: y = TanhNorm(0) = 0 (nn.Dropout(1.0) zeroes all)
+        B, Tq, H, D = q.shape
+        return (q * 0).reshape(B, Tq, H, D)
     out_dtype = q.dtype
     if q.dtype == torch.float16:
         q, k, v = q.float(), k.float(), v.float()
@@ -56,7 +78,8 @@ def screening_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, r: to
     if v.dtype != q.dtype:
         v = v.to(q.dtype)
     rf, wf = r.float(), w.float()
-    y = ScreenFn.apply(q, k, v, rf, wf, bool(causal), key_padding_mask, float(eps), int(q_offset))
+    y = ScreenFn.apply(q, k, v, rf, wf, bool(causal), key_padding_mask, float(eps), int(q_offset),
+                       _dropout_args(float(dropout_p), dropout_seed))
     return y if y.dtype == out_dtype else y.to(out_dtype)
 
 
@@ -66,12 +89,12 @@ class ScreenPackedFn(torch.autograd.Function):
     into one packed gradient, so no per-view gradient assembly follows."""
 
     @staticmethod
-    def forward(ctx, qkv, r, w, causal, key_padding_mask, eps):
+    def forward(ctx, qkv, r, w, causal, key_padding_mask, eps, dropout=None):
         q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
         y, no, nq, nk, nv, qq, kk, vv = _lib.screen_fwd(q, k, v, r, w, causal, key_padding_mask,
-                                                        eps, 0)
+                                                        eps, 0, dropout=dropout)
         ctx.save_for_backward(qkv, nq, nk, nv, y, no, r, w, key_padding_mask)
-        ctx.causal, ctx.eps = causal, eps
+        ctx.causal, ctx.eps, ctx.dropout = causal, eps, dropout
         ctx.has_kpm = key_padding_mask is not None
         ctx.views_ok = qq.data_ptr() == q.data_ptr() and kk.data_ptr() == k.data_ptr()
         return y
@@ -83,24 +106,27 @@ class ScreenPackedFn(torch.autograd.Function):
         dqkv = torch.empty_like(qkv)
         out = (dqkv[:, :, 0], dqkv[:, :, 1], dqkv[:, :, 2])
         _, _, _, dr, dw = _lib.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, r, w, ctx.causal,
-                                          kpm if ctx.has_kpm else None, ctx.eps, 0, out=out)
+                                          kpm if ctx.has_kpm else None, ctx.eps, 0, out=out,
+                                          dropout=ctx.dropout)
         return (dqkv, dr.to(r.dtype) if ctx.needs_input_grad[1] else None,
-                dw.to(w.dtype) if ctx.needs_input_grad[2] else None, None, None, None)
+                dw.to(w.dtype) if ctx.needs_input_grad[2] else None, None, None, None, None)
 
 
 def screening_attention_packed(qkv: torch.Tensor, r: torch.Tensor, w: torch.Tensor,
                                causal: bool = True,
                                key_padding_mask: torch.Tensor | None = None,
-                               eps: float = 1e-8) -> torch.Tensor:
+                               eps: float = 1e-8, dropout_p: float = 0.0,
+                               dropout_seed: int | None = None) -> torch.Tensor:
     """screening_attention for self-attention with q, k, v packed as one
     contiguous (B, T, 3, H, D) projection output (the fused QKV GEMM)."""
     if not qkv.is_cuda:
         raise RuntimeError("screening_attention runs on CUDA tensors only (no CPU path)")
-    if qkv.dtype == torch.float16 or not qkv.is_contiguous():
+    if qkv.dtype == torch.float16 or not qkv.is_contiguous() or dropout_p >= 1.0:
         q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
-        return screening_attention(q, k, v, r, w, causal, key_padding_mask, eps)
+        return screening_attention(q, k, v, r, w, causal, key_padding_mask, eps,
+                                   dropout_p=dropout_p, dropout_seed=dropout_seed)
     return ScreenPackedFn.apply(qkv, r.float(), w.float(), bool(causal), key_padding_mask,
-                                float(eps))
+                                float(eps), _dropout_args(float(dropout_p), dropout_seed))
 
 
 class TanhNormFn(torch.autograd.Function):

@@ -54,11 +54,53 @@ def test_cpu_tensors_raise_instead_of_falling_back(ms):
         ms.TanhNorm()(torch.randn(2, 8))
 
 
-def test_dropout_training_is_refused(ms):
-    a = ms.ScreeningAttention(64, 4, dropout=0.1).train()
-    x = torch.randn(1, 8, 64)
-    with pytest.raises(NotImplementedError):
-        a(x, x, x)
+def test_dropout_only_in_training(ms):
+    a = ms.ScreeningAttention(64, 4, dropout=0.25)
+    assert a.train()._dropout_p() == 0.25
+    assert a.eval()._dropout_p() == 0.0
+    assert ms.ScreeningAttention(64, 4).train()._dropout_p() == 0.0
+
+
+def test_dropout_bits_oracle_matches_library(ms, oracle):
+    """The oracle's restatement of the counter-based dropout hash equals the
+    library's screen_dropout_bits (host function, no GPU needed)."""
+    from importlib import import_module
+    lib = import_module("pytorch-implementation-of-screening-attention_b200._lib")
+    g = torch.Generator().manual_seed(3)
+    seeds = [0, 1, 2**32 - 1, 2**32, 0x0123456789ABCDEF, 2**64 - 1]
+    idx = torch.randint(0, 2**31 - 1, (40, 3), generator=g)
+    idx[:4] = torch.tensor([[0, 0, 0], [1, 2, 3], [2**31 - 2, 2**31 - 2, 2**31 - 2], [7, 0, 9]])
+    for seed in seeds:
+        bits = oracle.dropout_bits(seed, idx[:, 0], idx[:, 1], idx[:, 2])
+        for (bh, i, j), got in zip(idx.tolist(), bits.tolist()):
+            assert got == lib.dropout_bits(seed, bh, i, j)
+
+
+def test_dropout_mask_statistics(oracle):
+    """Drop rate equals p; masks of neighbouring scores, rows and seeds are
+    uncorrelated (Bernoulli statistics on 2^20 scores, 5-sigma bounds)."""
+    from importlib import import_module
+    lib = import_module("pytorch-implementation-of-screening-attention_b200._lib")
+    n = 1024
+    i = torch.arange(n)
+    j = torch.arange(n)
+    for p in (0.1, 0.5, 0.9):
+        thr = lib.dropout_threshold(p)
+        keep = oracle.dropout_keep(1234, thr, 1, 1, i, j)[0, 0] > 0
+        rate = 1.0 - keep.double().mean().item()
+        sd = math.sqrt(p * (1 - p) / (n * n))
+        assert abs(rate - p) < 5 * sd, (p, rate)
+        k = keep.double() - keep.double().mean()
+        den = (k * k).mean().item()
+        for a, b in ((k[:, 1:], k[:, :-1]), (k[1:, :], k[:-1, :])):
+            corr = (a * b).mean().item() / den
+            assert abs(corr) < 5 / n, corr
+    k1 = oracle.dropout_keep(1, lib.dropout_threshold(0.5), 2, 3, i[:256], j[:256]) > 0
+    k2 = oracle.dropout_keep(2, lib.dropout_threshold(0.5), 2, 3, i[:256], j[:256]) > 0
+    agree = (k1 == k2).double().mean().item()
+    assert abs(agree - 0.5) < 5 * math.sqrt(0.25 / k1.numel())
+    # different (b, h) planes of one seed differ too
+    assert (k1[0, 0] != k1[1, 2]).any()
 
 
 def test_kv_cache_ring_layout(ms):
