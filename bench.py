@@ -423,18 +423,49 @@ def run_lm(args, rank, world):
     net = model
     if dist is not None:
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local])
-    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, fused=True)
+    # one GPU: the whole step (forward, backward, AdamW) is captured once in a
+    # CUDA graph and replayed -- the step is ~150 small kernels, so launch
+    # overhead, not the GPU, bounds the eager loop
+    use_graph = world == 1 and not args.no_graph
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, fused=True, capturable=use_graph)
     g = torch.Generator().manual_seed(100 + rank)
     ids_host = torch.randint(0, V, (B, T), generator=g).pin_memory()
     ids = ids_host.to(dev)
 
-    def step(inp):
+    def eager_step(inp):
         with torch.autocast("cuda", dtype=torch.bfloat16):
             out = net(inp, labels=inp)
         out["loss"].backward()
         opt.step()
         opt.zero_grad(set_to_none=True)
         return out["loss"]
+
+    step = eager_step
+    graph_note = "eager (multi-GPU DDP step)" if world > 1 else "eager (--no-graph)"
+    if use_graph:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(max(args.warmup, 3)):
+                eager_step(ids)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        static_ids = ids.clone()
+        graph = torch.cuda.CUDAGraph()
+        opt.zero_grad(set_to_none=True)
+        with torch.cuda.graph(graph):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                static_out = net(static_ids, labels=static_ids)
+            static_out["loss"].backward()
+            opt.step()
+        static_loss = static_out["loss"]
+
+        def step(inp):
+            if inp.data_ptr() != static_ids.data_ptr():
+                static_ids.copy_(inp, non_blocking=True)
+            graph.replay()
+            return static_loss
+        graph_note = "one CUDA graph per step (forward, backward, fused AdamW)"
 
     for _ in range(args.warmup):
         step(ids)
@@ -453,7 +484,7 @@ def run_lm(args, rank, world):
     torch.cuda.synchronize()
     total = sum(a.elapsed_time(b) for a, b in evs)
     loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
-    ids_dev = torch.empty_like(ids)
+    ids_dev = static_ids if use_graph else torch.empty_like(ids)
     e2e = []
     for _ in range(args.steps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -507,7 +538,7 @@ def run_lm(args, rank, world):
             "data": "synthetic",
             "config": {"workload": f"cfg2: MultiscreenLM(50257, 256, 4, 4, max_seq_len=512), "
                                    f"{n_params} parameters, batch 16/GPU, T=512, bf16 autocast, "
-                                   f"fp32 master weights, fused AdamW",
+                                   f"fp32 master weights, fused AdamW; {graph_note}",
                        "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
                        "l2": "no flush: weights + optimizer state + activations > L2"},
             "roofline": {"bound": "tensor", "kernel": "whole training step", "achieved": tf / world,
@@ -620,6 +651,8 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=100_000)
     ap.add_argument("--decode-splits", type=int, default=0,
                     help="override the cache's split count (0: its own heuristic)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="lm workload: run the training step eagerly instead of as a CUDA graph")
     ap.add_argument("--profile-only", action="store_true",
                     help="warm-up steps + one step, nothing else (for ncu captures)")
     args = ap.parse_args()

@@ -227,7 +227,10 @@ int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
   float* pw = reinterpret_cast<float*>(ws + L.pw_off);
   if (nq && (stages & 1))
     tanhnorm_grad_from_y(a->dtype, a->D, a->y, a->no, a->dy, a->dy_sb, a->dy_st, G,
-                         use_mma_drop(a->dtype, a->D, a->dropout_threshold), a->B, a->Tq, a->H, a->eps, s);
+                         // G as bf16 hi/lo planes for the tensor-core families
+                         use_tc_fwd(a->dtype, a->D) ||
+                             use_mma_drop(a->dtype, a->D, a->dropout_threshold),
+                         a->B, a->Tq, a->H, a->eps, s);
   if ((st = check_launch())) return st;
   AttnShape sh = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
                             a->key_padding_mask, a->kpm_sb, a->dropout_threshold,

@@ -4,6 +4,8 @@ the backward regenerates; the oracle restates the same hash, so the CUDA
 output and all gradients are compared with the oracle under the identical
 mask, within the parity tolerances (max |x - ref| / max |ref| <= 1e-4 for
 float32 I/O, <= 2e-2 for bfloat16 I/O)."""
+import math
+
 import pytest
 import torch
 
@@ -82,7 +84,13 @@ def test_module_dropout_training(ms, cuda):
     torch.manual_seed, different across seeds, finite gradients for every
     parameter; eval mode equals p = 0."""
     torch.manual_seed(0)
-    a = ms.ScreeningAttention(256, 4, dropout=0.3).to(cuda).to(torch.bfloat16)
+    a = ms.ScreeningAttention(256, 4, dropout=0.3)
+    with torch.no_grad():
+        # r = 1.05, w = 256: about a fifth of the scores of random projections
+        # clear the trim threshold (with the default r = 2 almost none do)
+        a.s_r.fill_(math.log(0.05))
+        a.s_v.fill_(math.log(255.0))
+    a = a.to(cuda).to(torch.bfloat16)
     x = torch.randn(2, 384, 256, device=cuda).to(torch.bfloat16)
 
     def run(seed):
@@ -101,6 +109,7 @@ def test_module_dropout_training(ms, cuda):
     assert all(torch.equal(u, v) for u, v in zip(g1, g2))
     assert not torch.equal(y1, y3)
     assert all(torch.isfinite(g).all() for g in g1)
+    assert y1.abs().max() > 0
     a.eval()
     with torch.no_grad():
         ye = a(x, x, x).float()
