@@ -70,17 +70,39 @@ class MultiscreenLM(nn.Module):
         for block in self.blocks:
             x = block(x, key_padding_mask=key_padding_mask)
         x = self.norm(x)
-        logits = self.lm_head(x)
+        logits, lpad = self._lm_logits(x)
         result = {"logits": logits}
         if labels is not None:
+            # model.py:103-107 on the padded logits (pad columns are -inf)
             if shard is None or shard.world == 1:
-                result["loss"] = F.cross_entropy(logits.view(-1, logits.size(-1)),
-                                                 labels.view(-1), ignore_index=-100)
+                result["loss"] = F.cross_entropy(lpad.reshape(-1, lpad.size(-1)),
+                                                 labels.reshape(-1), ignore_index=-100)
             else:
-                result["loss"] = _sharded_mean_ce(logits, labels, shard)
+                result["loss"] = _sharded_mean_ce(lpad, labels, shard)
         return result
 
     # ------------------------------------------------------------------
+    def _lm_logits(self, x: torch.Tensor):
+        """lm_head(x) over all positions.  The vocabulary (50257 for GPT-2) is
+        padded to a multiple of 64 for the GEMM: with an odd leading dimension
+        cuBLAS falls back to unaligned kernels several times slower.  The pad
+        columns get logit -inf (zero weight rows, -inf bias), so softmax and
+        cross-entropy over the padded logits equal those over the real ones.
+        Returns (logits (..., V) -- a view --, padded logits (..., Vp))."""
+        W = self.lm_head.weight
+        V = W.shape[0]
+        pad = (-V) % 64
+        if pad == 0 or not x.is_cuda:
+            lg = self.lm_head(x)
+            return lg, lg
+        if torch.is_autocast_enabled("cuda"):
+            W = W.to(torch.get_autocast_dtype("cuda"))
+        Wp = F.pad(W, (0, 0, 0, pad))
+        bias = torch.zeros(V + pad, dtype=Wp.dtype, device=x.device)
+        bias[V:] = float("-inf")
+        lp = F.linear(x, Wp, bias)
+        return lp[..., :V], lp
+
     def _max_window(self) -> float:
         ws = torch.cat([blk.attn.window().detach() for blk in self.blocks])
         return float(ws.max()) if ws.numel() else 0.0
