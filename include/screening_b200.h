@@ -239,6 +239,31 @@ SCREEN_API int screen_decode(const screen_decode_args* a, screen_stream_t stream
 SCREEN_API int screen_decode_noalloc(const screen_decode_args* a, screen_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Few-row linear layer for the decode step of generate() (B <= 8 tokens):   */
+/* y[m, n] = act(sum_k xin[m, k] W[n, k]) (+ res[m, n]), bf16 in and out,    */
+/* fp32 accumulation.  xin = x, or RMSNorm(x) * norm_w when norm_w is given  */
+/* (torch.nn.RMSNorm: x / sqrt(mean(x^2) + eps), the normalised row rounded  */
+/* to bf16 as the unfused module does).  act: 0 none, 1 exact GELU           */
+/* (nn.GELU()).  Replaces the nn.RMSNorm -> nn.Linear -> nn.GELU -> residual */
+/* chain of the decode step (multiscreen/layers.py:60-76, model.py:97) that  */
+/* the reference runs as separate PyTorch ops on its full-prefix recompute   */
+/* (model.py:133): a bandwidth-bound pass over W instead of a GEMM with M=B. */
+/* ------------------------------------------------------------------------ */
+typedef struct screen_rows_linear_args {
+  int32_t M, N, K;               /* M <= 8 rows, K % 8 == 0                   */
+  int32_t act;                   /* 0 none, 1 GELU (erf)                      */
+  float norm_eps;
+  int32_t _pad0;
+  const void* x; int64_t x_stride;     /* (M, K) bf16, row stride in elements  */
+  const void* norm_w;            /* (K,) bf16 RMSNorm weight, or NULL         */
+  const void* W;                 /* (N, K) bf16, contiguous                   */
+  const void* res; int64_t res_stride; /* (M, N) bf16 added after act, or NULL*/
+  void* y; int64_t y_stride;     /* (M, N) bf16                               */
+} screen_rows_linear_args;
+
+SCREEN_API int screen_rows_linear(const screen_rows_linear_args* a, screen_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Stand-alone TanhNorm (multiscreen/norm.py:8-25) over contiguous rows of   */
 /* length D (any D >= 1).                                                    */
 /* ------------------------------------------------------------------------ */
@@ -254,7 +279,7 @@ SCREEN_API int screen_tanhnorm_bwd(int32_t dtype, int64_t rows, int32_t D, float
 SCREEN_API const char* screen_strerror(int status);
 SCREEN_API int screen_version(void);                  /* SCREEN_ABI_VERSION             */
 /* sizeof of the argument structs, for binding checks: 0 fwd, 1 bwd,
- * 2 kv_cache, 3 kv_append, 4 decode; -1 for an unknown id. */
+ * 2 kv_cache, 3 kv_append, 4 decode, 5 rows_linear; -1 for an unknown id. */
 SCREEN_API int64_t screen_sizeof_args(int which);
 /* Last CUDA error string seen by this thread inside the library. */
 SCREEN_API const char* screen_last_cuda_error(void);

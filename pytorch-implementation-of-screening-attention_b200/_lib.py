@@ -62,6 +62,15 @@ class BwdArgs(ctypes.Structure):
     ]
 
 
+class RowsLinearArgs(ctypes.Structure):
+    _fields_ = [
+        ("M", c_int32), ("N", c_int32), ("K", c_int32), ("act", c_int32),
+        ("norm_eps", c_float), ("_pad0", c_int32),
+        ("x", c_void_p), ("x_stride", c_int64), ("norm_w", c_void_p), ("W", c_void_p),
+        ("res", c_void_p), ("res_stride", c_int64), ("y", c_void_p), ("y_stride", c_int64),
+    ]
+
+
 class KVCacheDesc(ctypes.Structure):
     _fields_ = [
         ("k_pages", c_void_p), ("v_pages", c_void_p), ("block_table", c_void_p),
@@ -96,7 +105,7 @@ EXPORTED = (
     "screen_decode", "screen_decode_workspace_size", "screen_tanhnorm_fwd",
     "screen_tanhnorm_bwd", "screen_strerror", "screen_version", "screen_sizeof_args",
     "screen_last_cuda_error", "screen_decode_noalloc", "screen_fwd_workspace_size",
-    "screen_device_status", "screen_dropout_bits",
+    "screen_device_status", "screen_dropout_bits", "screen_rows_linear",
 )
 ABI_VERSION = 4
 
@@ -129,6 +138,7 @@ def load() -> ctypes.CDLL:
                                         c_void_p]
     lib.screen_tanhnorm_bwd.argtypes = [c_int32, c_int64, c_int32, c_float, c_void_p, c_void_p,
                                         c_void_p, c_void_p]
+    lib.screen_rows_linear.argtypes = [P(RowsLinearArgs), c_void_p]
     lib.screen_dropout_bits.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.c_uint32]
     lib.screen_dropout_bits.restype = ctypes.c_uint32
@@ -139,7 +149,8 @@ def load() -> ctypes.CDLL:
     lib.screen_sizeof_args.restype = c_int64
     if lib.screen_version() != ABI_VERSION:
         raise RuntimeError("libscreening_b200.so ABI version mismatch; rebuild it")
-    for i, st in enumerate((FwdArgs, BwdArgs, KVCacheDesc, KVAppendArgs, DecodeArgs)):
+    for i, st in enumerate((FwdArgs, BwdArgs, KVCacheDesc, KVAppendArgs, DecodeArgs,
+                            RowsLinearArgs)):
         if lib.screen_sizeof_args(i) != ctypes.sizeof(st):
             raise RuntimeError(f"struct {st.__name__} size differs from the C header; rebuild")
     _lib = lib
@@ -189,6 +200,27 @@ def _kpm(mask):
     if mask is None:
         return None
     return mask.to(torch.bool).contiguous().view(torch.uint8)
+
+
+def rows_linear(x, W, norm_w=None, eps=1e-6, act=0, res=None):
+    """act(RMSNorm(x) W^T) + res for few rows (decode step): x (M, K) bf16 with
+    M <= 8, W (N, K) bf16 contiguous, norm_w (K,) bf16 or None, res (M, N)
+    bf16 or None; act 0 none, 1 GELU (erf).  Returns (M, N) bf16."""
+    _require_cuda(x, W, norm_w, res)
+    lib = load()
+    M, K = x.shape
+    N = W.shape[0]
+    if x.stride(1) != 1 or not W.is_contiguous() or W.shape[1] != K:
+        raise ValueError("rows_linear: x rows and W must be contiguous over K")
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    a = RowsLinearArgs(M=M, N=N, K=K, act=int(act), norm_eps=float(eps),
+                       x=_ptr(x), x_stride=x.stride(0), norm_w=_ptr(norm_w), W=_ptr(W),
+                       res=_ptr(res), res_stride=0 if res is None else res.stride(0),
+                       y=_ptr(y), y_stride=y.stride(0))
+    if res is not None and res.stride(1) != 1:
+        raise ValueError("rows_linear: res must be contiguous over N")
+    _check(lib.screen_rows_linear(ctypes.byref(a), _stream(x.device)))
+    return y
 
 
 def dropout_threshold(p: float) -> int:

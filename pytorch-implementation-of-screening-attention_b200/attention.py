@@ -145,12 +145,22 @@ class ScreeningAttention(nn.Module):
         """One new token per sequence: x (B,1,d) at `positions` (B,) int32.
         Appends its unit k/v to the cache and attends over the cached window."""
         B = x.shape[0]
-        H, D = self.num_heads, self.head_dim
         if wqkv is None:
             wqkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
-        qkv = F.linear(x, wqkv).view(B, 1, 3, H, D)
+        y = self.decode_attend(F.linear(x, wqkv), cache, layer, positions, seq_lens, r, w)
+        return self.out_proj(y.reshape(B, 1, self.d_model))
+
+    def decode_attend(self, qkv: torch.Tensor, cache, layer: int, positions: torch.Tensor,
+                      seq_lens: torch.Tensor, r: torch.Tensor | None = None,
+                      w: torch.Tensor | None = None) -> torch.Tensor:
+        """The attention of decode_step between the QKV projection (qkv: B
+        rows of 3*d_model) and out_proj: appends the unit k/v rows to the
+        cache, attends over the cached window; returns (B, d_model)."""
+        B = qkv.shape[0]
+        H, D = self.num_heads, self.head_dim
+        qkv = qkv.reshape(B, 1, 3, H, D)
         cache.append(layer, qkv[:, :, 1], qkv[:, :, 2], positions, eps=self.eps)
         y, _ = cache.decode(layer, qkv[:, 0, 0], seq_lens,
                             self.sharpness() if r is None else r,
                             self.window() if w is None else w, eps=self.eps)
-        return self.out_proj(y.reshape(B, 1, self.d_model))
+        return y.reshape(B, self.d_model)

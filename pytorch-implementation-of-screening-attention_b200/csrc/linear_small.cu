@@ -1,0 +1,179 @@
+// Few-row linear layer for the decode step: y = act(xin W^T) (+ res) with
+// M <= 8 rows, bf16 weights streamed once from HBM (the step reads every
+// weight of the model for a handful of tokens, so it is bandwidth-bound; a
+// GEMM tile with M = B wastes most of its work and picks small-N kernels).
+//
+// CTA = 8 warps, one output feature n per warp: the CTA first stages the M
+// input rows in shared memory as bf16 (optionally RMSNorm'ed: the CTA sums
+// each row's squares itself -- M x K values from L2, tiny next to W), then
+// each lane streams 16-byte chunks of its warp's weight row (K / 256 chunks
+// per lane, all loads issued before the FMAs) against the staged rows, the
+// warp sums the M dot products with shuffles, and lane m writes y[m, n]
+// after GELU / residual.  Replaces nn.RMSNorm -> nn.Linear -> nn.GELU ->
+// residual add of multiscreen/layers.py:60-76 for the decode step.
+#include <cuda_bf16.h>
+#include "rowops.cuh"
+
+namespace screen {
+namespace {
+
+constexpr int kWarps = 8;
+
+__device__ __forceinline__ float gelu_erf(float v) {
+  return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+}
+
+template <int M>
+__global__ void __launch_bounds__(kWarps * 32) rows_linear_kernel(screen_rows_linear_args a) {
+  extern __shared__ __align__(16) __nv_bfloat16 xs[];   // [M][K]
+  __shared__ float red[M][kWarps];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = a.K;
+  const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(a.x);
+  const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
+  // ---- stage the input rows (RMSNorm'ed when norm_w is given)
+  float inv[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) inv[m] = 1.0f;
+  if (nw) {
+    float ss[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) ss[m] = 0.f;
+    for (int k8 = tid; k8 < K / 8; k8 += blockDim.x) {
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const uint4 u = *reinterpret_cast<const uint4*>(x + m * a.x_stride + 8 * k8);
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16(w4[e]);
+          ss[m] = fmaf(f.x, f.x, fmaf(f.y, f.y, ss[m]));
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const float v = warp_sum(ss[m]);
+      if (lane == 0) red[m][warp] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float t = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kWarps; ++w2) t += red[m][w2];
+      inv[m] = rsqrtf(t / (float)K + a.norm_eps);
+    }
+  }
+  for (int k8 = tid; k8 < K / 8; k8 += blockDim.x) {
+    uint4 g = make_uint4(0, 0, 0, 0);
+    if (nw) g = *reinterpret_cast<const uint4*>(nw + 8 * k8);
+    const uint32_t g4[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      uint4 u = *reinterpret_cast<const uint4*>(x + m * a.x_stride + 8 * k8);
+      if (nw) {
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+        uint32_t o4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // torch's fused RMSNorm: x * rsqrt(mean(x^2) + eps) * weight in
+          // fp32, rounded once
+          const float2 f = unpack_bf16(w4[e]), gf = unpack_bf16(g4[e]);
+          o4[e] = pack_bf16(f.x * inv[m] * gf.x, f.y * inv[m] * gf.y);
+        }
+        u = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+      }
+      *reinterpret_cast<uint4*>(xs + m * K + 8 * k8) = u;
+    }
+  }
+  __syncthreads();
+  // ---- one weight row per warp
+  const long long n = (long long)blockIdx.x * kWarps + warp;
+  if (n >= a.N) return;
+  const __nv_bfloat16* wr = reinterpret_cast<const __nv_bfloat16*>(a.W) + n * (long long)K;
+  float acc[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) acc[m] = 0.f;
+  constexpr int kUnroll = 4;
+  for (int k0 = 8 * lane; k0 < K; k0 += 256 * kUnroll) {
+    uint4 wv[kUnroll];
+#pragma unroll
+    for (int uu = 0; uu < kUnroll; ++uu) {
+      const int k = k0 + 256 * uu;
+      wv[uu] = k < K ? __ldg(reinterpret_cast<const uint4*>(wr + k)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int uu = 0; uu < kUnroll; ++uu) {
+      const int k = k0 + 256 * uu;
+      if (k >= K) break;
+      const uint32_t w4[4] = {wv[uu].x, wv[uu].y, wv[uu].z, wv[uu].w};
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(xs + m * K + k);
+        const uint32_t x4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 wf = unpack_bf16(w4[e]), xf = unpack_bf16(x4[e]);
+          acc[m] = fmaf(wf.x, xf.x, fmaf(wf.y, xf.y, acc[m]));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m) acc[m] = warp_sum(acc[m]);
+  if (lane < M) {
+    float v = acc[0];
+#pragma unroll
+    for (int m = 1; m < M; ++m)
+      if (lane == m) v = acc[m];
+    if (a.act == 1) v = __bfloat162float(__float2bfloat16_rn(v)), v = gelu_erf(v);
+    __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(a.y) + lane * a.y_stride + n;
+    if (a.res) {
+      // torch: bf16(linear) + bf16(res), rounded once more
+      v = __bfloat162float(__float2bfloat16_rn(v)) +
+          __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.res)[lane * a.res_stride + n]);
+    }
+    *yp = __float2bfloat16_rn(v);
+  }
+}
+
+template <int M>
+void launch_rows_linear(const screen_rows_linear_args& a, cudaStream_t st) {
+  const size_t smem = (size_t)M * a.K * 2;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(rows_linear_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  const unsigned grid = (unsigned)((a.N + kWarps - 1) / kWarps);
+  rows_linear_kernel<M><<<grid, kWarps * 32, smem, st>>>(a);
+}
+
+}  // namespace
+}  // namespace screen
+
+extern "C" int screen_rows_linear(const screen_rows_linear_args* a, screen_stream_t stream) {
+  using namespace screen;
+  if (!a) return SCREEN_ERR_INVALID_ARG;
+  if (a->M < 0 || a->M > 8 || a->N < 0 || a->K <= 0 || (a->K % 8) != 0 ||
+      (a->act != 0 && a->act != 1))
+    return SCREEN_ERR_INVALID_ARG;
+  if (a->M == 0 || a->N == 0) return SCREEN_OK;
+  if (!a->x || !a->W || !a->y) return SCREEN_ERR_INVALID_ARG;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(a->x) || !al16(a->W) || (a->norm_w && !al16(a->norm_w)) || (a->x_stride % 8) != 0)
+    return SCREEN_ERR_ALIGNMENT;
+  if ((size_t)a->M * a->K * 2 > 200 * 1024) return SCREEN_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (a->M) {
+    case 1: launch_rows_linear<1>(*a, st); break;
+    case 2: launch_rows_linear<2>(*a, st); break;
+    case 3: launch_rows_linear<3>(*a, st); break;
+    case 4: launch_rows_linear<4>(*a, st); break;
+    case 5: launch_rows_linear<5>(*a, st); break;
+    case 6: launch_rows_linear<6>(*a, st); break;
+    case 7: launch_rows_linear<7>(*a, st); break;
+    default: launch_rows_linear<8>(*a, st); break;
+  }
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SCREEN_OK : SCREEN_ERR_CUDA;
+}

@@ -12,6 +12,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import _lib
 from .kv_cache import PagedKVCache
 from .layers import MultiscreenBlock
 from .sequence_parallel import current_shard
@@ -30,6 +31,15 @@ def _sharded_mean_ce(logits, labels, shard):
     tot = torch.stack([s.detach(), (labels != -100).sum().to(s.dtype)])
     dist.all_reduce(tot, group=shard.group)
     return (s + (tot[0] - s.detach())) / tot[1]
+
+
+def _rms_eps(norm: nn.RMSNorm, x: torch.Tensor) -> float:
+    """nn.RMSNorm's eps.  None means the machine epsilon of the type torch
+    computes in, float32 for bf16 / fp16 / fp32 inputs (not the input
+    dtype's: bf16's would be 2^-7)."""
+    if norm.eps is not None:
+        return float(norm.eps)
+    return float(torch.finfo(torch.float64 if x.dtype == torch.float64 else torch.float32).eps)
 
 
 class MultiscreenLM(nn.Module):
@@ -148,11 +158,44 @@ class MultiscreenLM(nn.Module):
         else:
             pos_t = torch.full((B,), position, dtype=torch.int32, device=dev)
         x = self.token_emb(tokens) + self.pos_emb(pos_t.long()).unsqueeze(1)
+        seq_lens = pos_t + 1
+        if self._rows_fast(x):
+            # few tokens: every linear layer is one bandwidth-bound pass over
+            # its weights with RMSNorm, GELU and the residual add fused in
+            d = self.d_model
+            h = x.reshape(B, d)
+            for li, blk in enumerate(self.blocks):
+                wqkv, r, w = state["layers"][li]
+                qkv = _lib.rows_linear(h, wqkv, norm_w=blk.norm1.weight, eps=_rms_eps(blk.norm1, h))
+                y = blk.attn.decode_attend(qkv, cache, li, pos_t, seq_lens, r, w)
+                h = _lib.rows_linear(y, blk.attn.out_proj.weight, res=h)
+                u = _lib.rows_linear(h, blk.ffn[0].weight, norm_w=blk.norm2.weight,
+                                     eps=_rms_eps(blk.norm2, h), act=1)
+                h = _lib.rows_linear(u, blk.ffn[3].weight, res=h)
+            return _lib.rows_linear(h, self.lm_head.weight, norm_w=self.norm.weight,
+                                    eps=_rms_eps(self.norm, h))
         for li, blk in enumerate(self.blocks):
             wqkv, r, w = state["layers"][li]
-            x = x + blk.attn.decode_step(blk.norm1(x), cache, li, pos_t, pos_t + 1, wqkv, r, w)
+            x = x + blk.attn.decode_step(blk.norm1(x), cache, li, pos_t, seq_lens, wqkv, r, w)
             x = x + blk.ffn(blk.norm2(x))
         return self.lm_head(self.norm(x))[:, -1]
+
+    def _rows_fast(self, x: torch.Tensor) -> bool:
+        """The fused few-row decode path applies: bf16 CUDA weights and
+        activations, at most 8 tokens, feature sizes multiples of 8, exact
+        GELU FFN without bias, RMSNorm with an affine weight."""
+        if not (x.is_cuda and x.dtype == torch.bfloat16 and x.shape[0] <= 8):
+            return False
+        if self.lm_head.weight.dtype != torch.bfloat16 or self.d_model % 8:
+            return False
+        for blk in self.blocks:
+            f = blk.ffn
+            if not (isinstance(f[0], nn.Linear) and isinstance(f[1], nn.GELU) and
+                    f[1].approximate == "none" and f[0].bias is None and f[3].bias is None and
+                    f[0].out_features % 8 == 0 and blk.norm1.weight is not None and
+                    blk.norm2.weight is not None and blk.attn.out_proj.bias is None):
+                return False
+        return self.norm.weight is not None
 
     @torch.no_grad()
     def _capture_decode(self, batch: int, first_position: int, cache: PagedKVCache,
