@@ -264,6 +264,31 @@ typedef struct screen_rows_linear_args {
 SCREEN_API int screen_rows_linear(const screen_rows_linear_args* a, screen_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Cross-entropy over bf16 logits rows (the LM loss, multiscreen/model.py:   */
+/* 103-107: F.cross_entropy(logits, labels, ignore_index=-100), mean).       */
+/* fwd: per row lse = log sum exp(x) and loss = lse - x[label] (0 for an     */
+/* ignored label), one pass (online max / sum), fp32 math.  bwd: dlogits =   */
+/* (softmax(x) - onehot(label)) * (*dscale), 0 for ignored rows, one pass.   */
+/* The caller forms the mean (sum(loss) / count) and dscale = dmean / count  */
+/* on the device.  V % 8 == 0 (pad the vocabulary with -inf logits);         */
+/* logits rows 16-byte aligned.                                              */
+/* ------------------------------------------------------------------------ */
+typedef struct screen_xent_args {
+  int64_t rows;
+  int32_t V;                     /* row length (the padded vocabulary)        */
+  int32_t ignore_index;
+  const void* logits; int64_t ld;      /* (rows, V) bf16, row stride          */
+  const int64_t* labels;         /* (rows,)                                   */
+  float* lse;                    /* (rows,) fwd output, bwd input             */
+  float* loss;                   /* (rows,) fwd output                        */
+  void* dlogits; int64_t dld;    /* (rows, V) bf16, bwd output                */
+  const float* dscale;           /* device scalar: dL/d(mean) / count          */
+} screen_xent_args;
+
+SCREEN_API int screen_cross_entropy_fwd(const screen_xent_args* a, screen_stream_t stream);
+SCREEN_API int screen_cross_entropy_bwd(const screen_xent_args* a, screen_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Stand-alone TanhNorm (multiscreen/norm.py:8-25) over contiguous rows of   */
 /* length D (any D >= 1).                                                    */
 /* ------------------------------------------------------------------------ */
@@ -279,7 +304,7 @@ SCREEN_API int screen_tanhnorm_bwd(int32_t dtype, int64_t rows, int32_t D, float
 SCREEN_API const char* screen_strerror(int status);
 SCREEN_API int screen_version(void);                  /* SCREEN_ABI_VERSION             */
 /* sizeof of the argument structs, for binding checks: 0 fwd, 1 bwd,
- * 2 kv_cache, 3 kv_append, 4 decode, 5 rows_linear; -1 for an unknown id. */
+ * 2 kv_cache, 3 kv_append, 4 decode, 5 rows_linear, 6 xent; -1 for an unknown id. */
 SCREEN_API int64_t screen_sizeof_args(int which);
 /* Last CUDA error string seen by this thread inside the library. */
 SCREEN_API const char* screen_last_cuda_error(void);

@@ -71,6 +71,15 @@ class RowsLinearArgs(ctypes.Structure):
     ]
 
 
+class XentArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", c_int64), ("V", c_int32), ("ignore_index", c_int32),
+        ("logits", c_void_p), ("ld", c_int64), ("labels", c_void_p),
+        ("lse", c_void_p), ("loss", c_void_p), ("dlogits", c_void_p), ("dld", c_int64),
+        ("dscale", c_void_p),
+    ]
+
+
 class KVCacheDesc(ctypes.Structure):
     _fields_ = [
         ("k_pages", c_void_p), ("v_pages", c_void_p), ("block_table", c_void_p),
@@ -106,6 +115,7 @@ EXPORTED = (
     "screen_tanhnorm_bwd", "screen_strerror", "screen_version", "screen_sizeof_args",
     "screen_last_cuda_error", "screen_decode_noalloc", "screen_fwd_workspace_size",
     "screen_device_status", "screen_dropout_bits", "screen_rows_linear",
+    "screen_cross_entropy_fwd", "screen_cross_entropy_bwd",
 )
 ABI_VERSION = 4
 
@@ -139,6 +149,8 @@ def load() -> ctypes.CDLL:
     lib.screen_tanhnorm_bwd.argtypes = [c_int32, c_int64, c_int32, c_float, c_void_p, c_void_p,
                                         c_void_p, c_void_p]
     lib.screen_rows_linear.argtypes = [P(RowsLinearArgs), c_void_p]
+    lib.screen_cross_entropy_fwd.argtypes = [P(XentArgs), c_void_p]
+    lib.screen_cross_entropy_bwd.argtypes = [P(XentArgs), c_void_p]
     lib.screen_dropout_bits.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.c_uint32]
     lib.screen_dropout_bits.restype = ctypes.c_uint32
@@ -150,7 +162,7 @@ def load() -> ctypes.CDLL:
     if lib.screen_version() != ABI_VERSION:
         raise RuntimeError("libscreening_b200.so ABI version mismatch; rebuild it")
     for i, st in enumerate((FwdArgs, BwdArgs, KVCacheDesc, KVAppendArgs, DecodeArgs,
-                            RowsLinearArgs)):
+                            RowsLinearArgs, XentArgs)):
         if lib.screen_sizeof_args(i) != ctypes.sizeof(st):
             raise RuntimeError(f"struct {st.__name__} size differs from the C header; rebuild")
     _lib = lib
@@ -221,6 +233,30 @@ def rows_linear(x, W, norm_w=None, eps=1e-6, act=0, res=None):
         raise ValueError("rows_linear: res must be contiguous over N")
     _check(lib.screen_rows_linear(ctypes.byref(a), _stream(x.device)))
     return y
+
+
+def cross_entropy_fwd(logits, labels, ignore_index=-100):
+    """Per-row (lse, loss) of bf16 logits (N, V) (V % 8 == 0) against int64
+    labels (N,); loss is 0 for ignored labels."""
+    _require_cuda(logits, labels)
+    N, V = logits.shape
+    lse = torch.empty(N, dtype=torch.float32, device=logits.device)
+    loss = torch.empty(N, dtype=torch.float32, device=logits.device)
+    a = XentArgs(rows=N, V=V, ignore_index=int(ignore_index), logits=_ptr(logits),
+                 ld=logits.stride(0), labels=_ptr(labels), lse=_ptr(lse), loss=_ptr(loss))
+    _check(load().screen_cross_entropy_fwd(ctypes.byref(a), _stream(logits.device)))
+    return lse, loss
+
+
+def cross_entropy_bwd(logits, labels, lse, dscale, ignore_index=-100):
+    """dlogits (N, V) bf16 = (softmax - onehot) * dscale (a device scalar)."""
+    N, V = logits.shape
+    dl = torch.empty_like(logits)
+    a = XentArgs(rows=N, V=V, ignore_index=int(ignore_index), logits=_ptr(logits),
+                 ld=logits.stride(0), labels=_ptr(labels), lse=_ptr(lse),
+                 dlogits=_ptr(dl), dld=dl.stride(0), dscale=_ptr(dscale))
+    _check(load().screen_cross_entropy_bwd(ctypes.byref(a), _stream(logits.device)))
+    return dl
 
 
 def dropout_threshold(p: float) -> int:

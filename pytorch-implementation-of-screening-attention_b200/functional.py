@@ -129,6 +129,39 @@ def screening_attention_packed(qkv: torch.Tensor, r: torch.Tensor, w: torch.Tens
                                 float(eps), _dropout_args(float(dropout_p), dropout_seed))
 
 
+class CrossEntropyFn(torch.autograd.Function):
+    """Mean cross-entropy of bf16 logits rows with ignore_index (the LM loss,
+    multiscreen/model.py:103-107) in one pass forward and one backward, with
+    no fp32 copy of the logits; the mean and its scale stay on the device."""
+
+    @staticmethod
+    def forward(ctx, logits, labels, ignore_index):
+        lse, loss = _lib.cross_entropy_fwd(logits, labels, ignore_index)
+        count = (labels != ignore_index).sum().to(torch.float32)
+        ctx.save_for_backward(logits, labels, lse, count)
+        ctx.ignore_index = ignore_index
+        return loss.sum() / count
+
+    @staticmethod
+    def backward(ctx, dmean):
+        logits, labels, lse, count = ctx.saved_tensors
+        dscale = (dmean.float() / count).reshape(1).contiguous()
+        dl = _lib.cross_entropy_bwd(logits, labels, lse, dscale, ctx.ignore_index)
+        return dl, None, None
+
+
+def cross_entropy(logits: torch.Tensor, labels: torch.Tensor,
+                  ignore_index: int = -100) -> torch.Tensor:
+    """F.cross_entropy(logits, labels, ignore_index) (mean) for (N, V) logits;
+    bf16 CUDA logits with V % 8 == 0 run the fused kernels."""
+    if (logits.is_cuda and logits.dtype == torch.bfloat16 and logits.dim() == 2 and
+            logits.shape[1] % 8 == 0 and logits.stride(1) == 1 and logits.stride(0) % 8 == 0 and
+            logits.data_ptr() % 16 == 0):
+        return CrossEntropyFn.apply(logits, labels.reshape(-1).long().contiguous(),
+                                    int(ignore_index))
+    return torch.nn.functional.cross_entropy(logits, labels, ignore_index=ignore_index)
+
+
 class TanhNormFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, eps):

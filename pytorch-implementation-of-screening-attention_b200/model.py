@@ -13,6 +13,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib
+from .functional import cross_entropy
 from .kv_cache import PagedKVCache
 from .layers import MultiscreenBlock
 from .sequence_parallel import current_shard
@@ -85,8 +86,8 @@ class MultiscreenLM(nn.Module):
         if labels is not None:
             # model.py:103-107 on the padded logits (pad columns are -inf)
             if shard is None or shard.world == 1:
-                result["loss"] = F.cross_entropy(lpad.reshape(-1, lpad.size(-1)),
-                                                 labels.reshape(-1), ignore_index=-100)
+                result["loss"] = cross_entropy(lpad.reshape(-1, lpad.size(-1)),
+                                               labels.reshape(-1), ignore_index=-100)
             else:
                 result["loss"] = _sharded_mean_ce(lpad, labels, shard)
         return result
