@@ -12,12 +12,8 @@ from pathlib import Path
 
 import torch
 
-import os as _os
-
-# SCREEN_LIB_PATH points the binding at another build of the library (used to
-# compare kernel variants); by default the in-tree build is loaded.
-LIB_PATH = Path(_os.environ.get("SCREEN_LIB_PATH") or
-                Path(__file__).resolve().parent / "_lib" / "libscreening_b200.so")
+# the in-tree build (built by _build.py / __graft_entry__.build())
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libscreening_b200.so"
 
 F32, BF16 = 0, 1
 _DTYPES = {torch.float32: F32, torch.bfloat16: BF16}

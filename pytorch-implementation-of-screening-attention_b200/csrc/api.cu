@@ -10,9 +10,10 @@
 using namespace screen;
 
 namespace {
-
 thread_local char g_last_err[256] = "";
+}  // namespace
 
+namespace screen {
 int check_launch() {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -21,6 +22,14 @@ int check_launch() {
   }
   return SCREEN_OK;
 }
+int record_cuda_error(cudaError_t e) {
+  if (e == cudaSuccess) return SCREEN_OK;
+  snprintf(g_last_err, sizeof(g_last_err), "%s", cudaGetErrorString(e));
+  return SCREEN_ERR_CUDA;
+}
+}  // namespace screen
+
+namespace {
 
 bool dim_ok(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
 bool dtype_ok(int t) { return t == SCREEN_F32 || t == SCREEN_BF16; }
@@ -195,8 +204,8 @@ size_t screen_fwd_workspace_size(const screen_fwd_args* a) {
 
 int screen_device_status(int clear) {
   const int a = tc_device_status(clear != 0), b = tc_bwd_device_status(clear != 0);
-  const int c = decode_device_status(clear != 0);
-  return a != 0 ? a : (b != 0 ? b : c);
+  const int c = decode_device_status(clear != 0), d = xent_device_status(clear != 0);
+  return a != 0 ? a : (b != 0 ? b : (c != 0 ? c : d));
 }
 
 size_t screen_bwd_workspace_size(const screen_bwd_args* a) {

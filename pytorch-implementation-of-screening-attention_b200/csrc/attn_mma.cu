@@ -697,8 +697,6 @@ __global__ void __launch_bounds__(kKvThreads, 1) mma_bwd_dkdv_kernel(AttnShape s
   }
 }
 
-bool g_attr_set[64];
-
 }  // namespace
 
 bool mma_supported(int dtype, int D) { return dtype == SCREEN_BF16 && D == kD; }
@@ -707,18 +705,11 @@ long long mma_bwd_partials(int, const AttnShape& s) {
   return (long long)s.B * ((s.Tk + kKvBN - 1) / kKvBN);
 }
 
+// a failed opt-in stays in cudaGetLastError, which the entry point checks
 static void ensure_attrs() {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !g_attr_set[dev]) {
-    cudaFuncSetAttribute(mma_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kFwdSmem);
-    cudaFuncSetAttribute(mma_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kDqSmem);
-    cudaFuncSetAttribute(mma_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kKvSmem);
-    g_attr_set[dev] = true;
-  }
+  if (ensure_smem_optin((const void*)mma_fwd_kernel, (int)kFwdSmem) == cudaSuccess &&
+      ensure_smem_optin((const void*)mma_bwd_dq_kernel, (int)kDqSmem) == cudaSuccess)
+    ensure_smem_optin((const void*)mma_bwd_dkdv_kernel, (int)kKvSmem);
 }
 
 void mma_fwd(int, const AttnShape& s, const FwdPtrs& p, cudaStream_t st) {

@@ -38,10 +38,7 @@ using namespace sm100;
 typedef __nv_bfloat16 bf16;
 
 // kCG compute warpgroups split each key tile's 64 columns (32 / kCG each)
-#ifndef SCREEN_FWD_CG
-#define SCREEN_FWD_CG 2
-#endif
-constexpr int kCG = SCREEN_FWD_CG;
+constexpr int kCG = 2;
 constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 5;
 // S / P ring in TMEM: P (bf16) is written over the S (fp32) columns it came
 // from, so three 64-column buffers + O fit the 256 columns of a CTA
@@ -76,16 +73,6 @@ static_assert(TM_O + kD <= TM_COLS, "TMEM budget");
 
 __device__ int g_device_status = 0;
 
-// Wait-time instrumentation of the forward (variant builds with
-// -DSCREEN_FWD_PROFILE only): clock cycles each role spends in its waits.
-#ifdef SCREEN_FWD_PROFILE
-__device__ unsigned long long g_fwd_prof[16];
-#define PROF_T0() const long long _pt0 = clock64()
-#define PROF_ADD(slot) atomicAdd(&g_fwd_prof[slot], (unsigned long long)(clock64() - _pt0))
-#else
-#define PROF_T0() do {} while (0)
-#define PROF_ADD(slot) do {} while (0)
-#endif
 
 // kDrop: attention dropout on alpha (counter-based bits, AttnShape::drop_thr)
 template <bool kDrop>
@@ -176,9 +163,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // lane 0 waits, the whole warp follows its verdict (no divergent exit)
         int okw = 1;
         if (lane == 0) {
-          PROF_T0();
           okw = mbar_wait(bar(BAR_KV_EMPTY + st), ((j / kNS) - 1) & 1, abort_flag, kWaitLimitNs);
-          PROF_ADD(0);
         }
         if (!__shfl_sync(0xffffffffu, okw, 0)) break;
       }
@@ -228,9 +213,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       auto issue_s = [&](int jj) -> bool {
         const int st = jj % kNS, bb = jj % kSB;
         {
-          PROF_T0();
           const bool okk = mbar_wait(bar(BAR_KV_FULL + st), (jj / kNS) & 1, abort_flag, kWaitLimitNs);
-          PROF_ADD(1);
           if (!okk) return false;
         }
         tc_fence_after();
@@ -246,9 +229,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int j = 0; j < n && ok; ++j) {
         const int st = j % kNS, bb = j % kSB;
         {
-          PROF_T0();
           ok = mbar_wait(bar(BAR_P_FULL + bb), (j / kSB) & 1, abort_flag, kWaitLimitNs);
-          PROF_ADD(3);
         }
         if (!ok) break;
         tc_fence_after();
@@ -297,28 +278,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     // alpha of columns (c, c+1) from the pair's S, 1/|k|, cos, sin
     auto pair_alpha = [&](float s0, float s1, float ik0, float ik1, float c0, float c1, float n0,
                           float n1, bool k0, bool k1) -> uint32_t {
-#ifdef SCREEN_SCALAR_EW
-      // relu(t) = saturate(t): t = 1 - r (1 - S) <= 1, so the clamp is free
-      float a0 = __saturatef(fmaf(rq, s0 * ik0, omr)), a1 = __saturatef(fmaf(rq, s1 * ik1, omr));
-      a0 = k0 ? a0 : 0.f;
-      a1 = k1 ? a1 : 0.f;
-      const float m0 = fmaf(crow, c0, fmaf(srow, n0, 0.5f));
-      const float m1 = fmaf(crow, c1, fmaf(srow, n1, 0.5f));
-      return pack_bf16(a0 * m0 * a0, a1 * m1 * a1);
-#else
       const float2 x = __fmul2_rn(make_float2(s0, s1), make_float2(ik0, ik1));
       // relu(t) = saturate(t): t = 1 - r (1 - S) <= 1, so the clamp is free
       const float a0 = __saturatef(fmaf(rq, x.x, omr)), a1 = __saturatef(fmaf(rq, x.y, omr));
       const float2 a2 = make_float2(k0 ? a0 : 0.f, k1 ? a1 : 0.f);
-#ifdef SCREEN_EXP_NOMASK
-      const float2 m2 = half2;
-#else
       const float2 m2 =
           __ffma2_rn(cr2, make_float2(c0, c1), __ffma2_rn(sr2, make_float2(n0, n1), half2));
-#endif
       const float2 al = __fmul2_rn(__fmul2_rn(a2, m2), a2);
       return pack_bf16(al.x, al.y);
-#endif
     };
     bool ok = true;
     unsigned long long live_tiles = 0;
@@ -331,14 +298,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     // [p0 + kBM - 1 - dmax, p0] (causal) / [.. , p0 + dmax] (non-causal)
     const int in_lo = p0i + kBM - 1 - dmax;
     for (int j = 0; j < n; ++j, j0i += kBN) {
-#ifdef SCREEN_FWD_PROFILE
-      const long long _tc0 = clock64();
-#endif
       {
-        PROF_T0();
         ok = mbar_wait(bar(BAR_KV_FULL + st), st_ph, abort_flag, kWaitLimitNs) &&
              mbar_wait(bar(BAR_S_FULL + bb), bb_ph, abort_flag, kWaitLimitNs);
-        if (tid == 0) PROF_ADD(4);
       }
       // warp-uniform verdict (the TMEM accesses below are warp-collective);
       // a warp that gives up leaves the loop alone -- every other wait on its
@@ -366,11 +328,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       imax = max(imax, (int)sv[kNC - 1]);
       const float smax = __int_as_float(imax);
       const float ikmax = colt[3 * kBN + 1];
-#ifdef SCREEN_EXP_NOPRETEST
-      const bool mine = true;
-#else
       const bool mine = r < 1.0f || (imax > 0 && fmaf(rq, smax * ikmax, omr) > 0.f);
-#endif
       // liveness per warp block (32 rows x kNC columns): a dead block stores
       // P = 0, so the warps never wait on one another within a tile
       const bool live = __any_sync(0xffffffffu, mine);
@@ -432,10 +390,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(bar(BAR_P_FULL + bb));
       if (++st == kNS) { st = 0; st_ph ^= 1; }
       if (++bb == kSB) { bb = 0; bb_ph ^= 1; }
-#ifdef SCREEN_FWD_PROFILE
-      if (tid == 0) atomicAdd(&g_fwd_prof[5], (unsigned long long)(clock64() - _tc0));
-      if (tid == 0) atomicAdd(&g_fwd_prof[7], 1ull);
-#endif
     }
     if (p.tile_stats && lane == 0) {
       // in 16x64 score blocks (the unit of the warp-level kernels): a tile is
@@ -446,9 +400,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // epilogue: O -> TanhNorm -> y
     {
-      PROF_T0();
       ok = ok && mbar_wait(bar(BAR_O_FULL), 0, abort_flag, kWaitLimitNs);
-      if (tid == 0) PROF_ADD(6);
     }
     // tcgen05.ld below is warp-collective: every lane takes the same branch
     ok = __all_sync(0xffffffffu, ok);
@@ -613,8 +565,6 @@ __global__ void tc_ik_meta_kernel(float* __restrict__ ikT, float4* __restrict__ 
   meta[idx] = make_float4(mn, mx, 0.f, 0.f);
 }
 
-bool g_tc_attr[64];
-
 long long tk_pad(int Tk) { return ((long long)Tk + kBN - 1) / kBN * kBN; }
 size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -631,14 +581,10 @@ size_t tc_fwd_workspace(const AttnShape& s) {
 int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
            cudaStream_t st) {
   if (s.B == 0 || s.H == 0) return SCREEN_OK;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !g_tc_attr[dev]) {
-    cudaFuncSetAttribute(tc_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kSmemBytes);
-    cudaFuncSetAttribute(tc_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kSmemBytes);
-    g_tc_attr[dev] = true;
+  {
+    cudaError_t e = ensure_smem_optin((const void*)tc_fwd_kernel<false>, (int)kSmemBytes);
+    if (e == cudaSuccess) e = ensure_smem_optin((const void*)tc_fwd_kernel<true>, (int)kSmemBytes);
+    if (e != cudaSuccess) return record_cuda_error(e);
   }
   const long long BH = (long long)s.B * s.H, Tkp = tk_pad(s.Tk);
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
@@ -679,17 +625,6 @@ int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_giv
   return SCREEN_OK;
 }
 
-#ifdef SCREEN_FWD_PROFILE
-extern "C" SCREEN_API int screen_debug_fwd_profile(unsigned long long* out, int clear) {
-  if (cudaMemcpyFromSymbol(out, g_fwd_prof, sizeof(unsigned long long) * 16) != cudaSuccess)
-    return -1;
-  if (clear) {
-    unsigned long long z[16] = {};
-    cudaMemcpyToSymbol(g_fwd_prof, z, sizeof(z));
-  }
-  return 0;
-}
-#endif
 
 int tc_device_status(bool clear) {
   int v = 0;

@@ -27,10 +27,7 @@ namespace {
 using namespace sm100;
 typedef __nv_bfloat16 bf16;
 
-#ifndef SCREEN_KV_STAGES
-#define SCREEN_KV_STAGES 4
-#endif
-constexpr int kD = 64, kBM = 128, kBN = 64, kNS = SCREEN_KV_STAGES, kThreads = 320;
+constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 4, kThreads = 320;
 constexpr int kCompute = 256;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t TILE_A = kBM * kD * 2;  // 128-row operand tile, 16 KB
@@ -49,17 +46,6 @@ struct Aux {
 
 __device__ int g_bwd_status = 0;
 
-// Cycle instrumentation of the key-major kernel (variant builds with
-// -DSCREEN_BWD_PROFILE only): clock cycles per role and phase, summed over CTAs.
-#ifdef SCREEN_BWD_PROFILE
-__device__ unsigned long long g_bwd_prof[16];
-__device__ unsigned long long g_prof_lat[4];
-#define BPROF_T(name) const long long name = clock64()
-#define BPROF_ADD(slot, t0) atomicAdd(&g_bwd_prof[slot], (unsigned long long)(clock64() - (t0)))
-#else
-#define BPROF_T(name) do {} while (0)
-#define BPROF_ADD(slot, t0) do {} while (0)
-#endif
 __device__ __forceinline__ int* status_word() { return &g_bwd_status; }
 
 __device__ __forceinline__ void store_unit_jacobian(const float (&acc)[64], const bf16* xrow,
@@ -608,15 +594,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bf16* vh = reinterpret_cast<const bf16*>(p.v.p) + (long long)b * p.v.sb + (long long)h * kD;
   float acc_r = 0.f, acc_w = 0.f;
 
-#ifdef SCREEN_VAR_PREFETCH
-  if (warp == 8 && lane == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmG)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
-    if (kFuse) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmDQ)) : "memory");
-  }
-#endif
   if (warp == 8) {
     // ---------------------------------------------------------- producer
     // lane 0 issues the TMA copies: K, V once (128 rows), then per query
@@ -646,13 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int st = j % kNS;
       if (j >= kNS) {
         int okw = 1;
-#ifdef SCREEN_BWD_PROFILE
-        BPROF_T(_p0);
-#endif
         if (lane == 0) okw = mbar_wait(bar(BAR_EMPTY + st), ((j / kNS) - 1) & 1, abort_flag, kWaitLimitNs);
-#ifdef SCREEN_BWD_PROFILE
-        if (lane == 0) BPROF_ADD(10, _p0);
-#endif
         if (!__shfl_sync(0xffffffffu, okw, 0)) break;
       }
       const int qt = qt0 + j;
@@ -668,9 +639,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(sb_ + 2 * TILE_B, &tmG, 0, h, (int)iq0, b + s.B, fb);
         bulk_g2s(colb, iqh + iq0, kBN * 4, fb);
         bulk_g2s(colb + 3 * kBN * 4, mh + qt, 16, fb);
-#ifdef SCREEN_BWD_PROFILE
-        reinterpret_cast<volatile long long*>(red + 16)[st] = clock64();
-#endif
       }
       issued = j + 1;
       // column angle pi (iq0 + c + q_offset - j0) / w by rotation
@@ -690,12 +658,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_FULL + st));
-#ifdef SCREEN_BWD_PROFILE
-      if (lane == 0) {
-        atomicAdd(&g_prof_lat[2], (unsigned long long)(clock64() - reinterpret_cast<volatile long long*>(red + 16)[st]));
-        atomicAdd(&g_prof_lat[3], 1ull);
-      }
-#endif
     }
     if (lane == 0 && *abort_flag) {
       // let the copies already issued land before the CTA's smem goes away
@@ -715,9 +677,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idMN = idesc_bf16(kBM, kD, 0, 1);
       constexpr uint32_t idQ = idesc_bf16(kBM, kD, 1, 1);   // A = dS^T staging, MN-major
       bool started = false, ok = mbar_wait(bar(BAR_A), 0, abort_flag, kWaitLimitNs);
-#ifdef SCREEN_BWD_PROFILE
-      BPROF_T(_m3);
-#endif
       // shared-memory descriptors built once: an operand at byte offset x
       // from a base is base_desc + x / 16 (the start-address field holds
       // address / 16 in 14 bits; every address here is below 256 KB)
@@ -730,14 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pair_i = 0;   // pairs of query tiles whose dQ has been issued
       auto issue_kv = [&](int jj) -> bool {
         const int bb = jj & 1, st = jj % kNS;
-#ifdef SCREEN_BWD_PROFILE
-        BPROF_T(_m0);
-#endif
         if (!mbar_wait(bar(BAR_P + bb), (jj >> 1) & 1, abort_flag, kWaitLimitNs)) return false;
-        BPROF_ADD(7, _m0);
-#ifdef SCREEN_BWD_PROFILE
-        BPROF_T(_m4);
-#endif
         tc_fence_after();
         // alpha_j / dS_j sit in the first 16 columns of each compute group's
         // 32-column half of the S / dP buffer
@@ -752,23 +704,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                  kk > 0 ? 1u : s0);
         }
         started = true;
-        BPROF_ADD(11, _m4);
         if constexpr (kFuse) {
           const int qt = qt0 + jj;
           if ((qt & 1) || jj == n - 1) {
             // the pair of query tiles (qt & ~1, qt | 1) is complete:
             // dQ[128 q][64 d] = dS (A: [key][q] staging, MN-major, M = 128) x K
             const int buf = pair_i & 1;
-#ifdef SCREEN_BWD_PROFILE
-            BPROF_T(_m1);
-#endif
             if (pair_i >= 2 &&
                 !mbar_wait(bar(BAR_DQE + buf), ((pair_i >> 1) - 1) & 1, abort_flag, kWaitLimitNs))
               return false;
-            BPROF_ADD(8, _m1);
-#ifdef SCREEN_BWD_PROFILE
-            BPROF_T(_m6);
-#endif
             tc_fence_after();
             const uint64_t sd = dStg + (uint64_t)(buf * (STG_PAIR >> 4));
 #pragma unroll
@@ -776,7 +720,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               mma_ss(tmem + TK_ACCQ + 64 * buf, sd + kk * (16 * 128 / 16),
                      dK_mn + kk * (16 * 128 / 16), idQ, kk > 0 ? 1u : 0u);
             mma_commit(bar(BAR_DQF + buf));
-            BPROF_ADD(15, _m6);
             ++pair_i;
           }
         }
@@ -787,23 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % kNS, bb = j & 1;
         // buffer bb held alpha / dS of tile j - 2, read by MMAs issued
         // before these (in-order execution)
-#ifdef SCREEN_BWD_PROFILE
-        BPROF_T(_m2);
-#endif
         ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs);
-        BPROF_ADD(6, _m2);
-#ifdef SCREEN_BWD_PROFILE
-        {
-          const long long now = clock64();
-          if (now - _m2 > 64) {
-            atomicAdd(&g_prof_lat[0], (unsigned long long)(now - reinterpret_cast<volatile long long*>(red + 16)[st]));
-            atomicAdd(&g_prof_lat[1], 1ull);
-          }
-        }
-#endif
-#ifdef SCREEN_BWD_PROFILE
-        BPROF_T(_m5);
-#endif
         if (!ok) break;
         tc_fence_after();
         fence_proxy_async_smem();
@@ -819,15 +746,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < kD / 16; ++kk)
           mma_ss(tmem + TK_DP + kBN * bb, dV_k + 2 * kk, gld + 2 * kk, idS, 1u);
         mma_commit(bar(BAR_SD + bb));
-        BPROF_ADD(13, _m5);
         if (j >= 1) ok = issue_kv(j - 1);
       }
       if (ok && n >= 1) ok = issue_kv(n - 1);
-#ifdef SCREEN_BWD_PROFILE
-      BPROF_ADD(9, _m3);
-      atomicAdd(&g_bwd_prof[12], (unsigned long long)n);
-      atomicAdd(&g_bwd_prof[14], 1ull);
-#endif
       misc[3] = started ? 1u : 0u;
       mma_commit(bar(BAR_DONE));
       mbar_arrive(bar(BAR_DONE));
@@ -897,9 +818,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();   // generic-proxy writes -> TMA reads
       __syncwarp();
       if (lane == 0) {
-#ifndef SCREEN_VAR_NORED
         tma_reduce_add_4d(&tmDQ, base + region, cb, h, (pqt & ~1) * kBN + 32 * (warp & 3), b);
-#endif
         bulk_commit();
       }
       sf_pending = buf;
@@ -924,9 +843,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int st = j % kNS, bb = j & 1;
       const int qt = qt0 + j;
       if (kFuse && (j == 0 || (qt & 1) == 0)) ++pair_c;
-#ifdef SCREEN_BWD_PROFILE
-      BPROF_T(_c0);
-#endif
       ok = mbar_wait(bar(BAR_FULL + st), (j / kNS) & 1, abort_flag, kWaitLimitNs) &&
            mbar_wait(bar(BAR_SD + bb), (j >> 1) & 1, abort_flag, kWaitLimitNs);
       // warp-uniform verdict (the TMEM accesses below are warp-collective);
@@ -936,18 +852,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       if constexpr (kFuse) release();
-#ifdef SCREEN_BWD_PROFILE
-      if (tid == 0) BPROF_ADD(0, _c0);
-      BPROF_T(_c1);
-#endif
       uint32_t sv[32], dv[32];
       tmem_ld32(tmem + TK_S + kBN * bb + cb + lane_off, sv);
       tmem_ld32(tmem + TK_DP + kBN * bb + cb + lane_off, dv);
       tmem_wait_ld();
-#ifdef SCREEN_BWD_PROFILE
-      if (tid == 0) BPROF_ADD(1, _c1);
-      BPROF_T(_c2);
-#endif
       const float* col = colp + st * (COLB / 4);
       int imax = (int)sv[0];
 #pragma unroll
@@ -1023,14 +931,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         };
-#ifdef SCREEN_VAR_NOEDGE
-        run(std::true_type{});
-#else
         if (inside)
           run(std::false_type{});
         else
           run(std::true_type{});
-#endif
         // alpha / dS over this group's own S / dP columns (already loaded)
         tmem_st16(tmem + TK_S + kBN * bb + cb + lane_off, pa);
         tmem_st16(tmem + TK_DP + kBN * bb + cb + lane_off, pd);
@@ -1041,10 +945,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 16; ++c) pq[c] = 0u;
       }
-#ifdef SCREEN_BWD_PROFILE
-      if (tid == 0) BPROF_ADD(2, _c2);
-      BPROF_T(_c3);
-#endif
       if constexpr (kFuse) {
         // dS^T row t (this group's 32 queries) into half (qt & 1) of the
         // pair's staging buffer, SW128 (16-byte chunk c of the row at c ^ (t % 8));
@@ -1073,10 +973,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(BAR_P + bb));
-#ifdef SCREEN_BWD_PROFILE
-      if (tid == 0) BPROF_ADD(3, _c3);
-      BPROF_T(_c4);
-#endif
       if constexpr (kFuse) {
         // drain the pair completed one tile ago (its dQ MMA has had a tile's
         // time), then remember this one if it completes a pair
@@ -1089,9 +985,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           todo_qt = qt;
         }
       }
-#ifdef SCREEN_BWD_PROFILE
-      if (tid == 0) { BPROF_ADD(4, _c4); BPROF_ADD(5, _c0); }
-#endif
     }
     if (kFuse && ok && todo >= 0) ok = drain(todo, todo_qt);
     // every reduce this warp issued completes before the CTA's shared memory goes away
@@ -1201,7 +1094,6 @@ __global__ void tc_bwd_aux_kernel(const float* __restrict__ nq, const float* __r
   if (c == 0) (isk ? mk : mq)[blk] = make_float4(fmaxf(sm[0], sm[1]), 0.f, 0.f, 0.f);
 }
 
-bool g_bwd_attr[64];
 long long padT(int T) { return ((long long)T + kBN - 1) / kBN * kBN; }
 size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -1249,22 +1141,16 @@ long long tc_bwd_partials(const AttnShape& s) {
 
 int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st) {
   if (s.B == 0 || s.H == 0) return SCREEN_OK;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !g_bwd_attr[dev]) {
-    cudaFuncSetAttribute(tc_bwd_dq_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)dq::SMEM);
-    cudaFuncSetAttribute(tc_bwd_dq_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)dq::SMEM);
-    cudaFuncSetAttribute(tc_bwd_kv_kernel<true, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
-    cudaFuncSetAttribute(tc_bwd_kv_kernel<false, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
-    cudaFuncSetAttribute(tc_bwd_kv_kernel<true, true>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
-    cudaFuncSetAttribute(tc_bwd_kv_kernel<false, true>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
-    g_bwd_attr[dev] = true;
+  {
+    const void* fns[6] = {(const void*)tc_bwd_dq_kernel<false>, (const void*)tc_bwd_dq_kernel<true>,
+                          (const void*)tc_bwd_kv_kernel<true, false>,
+                          (const void*)tc_bwd_kv_kernel<false, false>,
+                          (const void*)tc_bwd_kv_kernel<true, true>,
+                          (const void*)tc_bwd_kv_kernel<false, true>};
+    for (int i = 0; i < 6; ++i) {
+      const cudaError_t e = ensure_smem_optin(fns[i], i < 2 ? (int)dq::SMEM : (int)kv::SMEM);
+      if (e != cudaSuccess) return record_cuda_error(e);
+    }
   }
   const long long BH = (long long)s.B * s.H, Tqp = padT(s.Tq), Tkp = padT(s.Tk);
   uint8_t* w8 = reinterpret_cast<uint8_t*>(aux_ws);
@@ -1352,23 +1238,6 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
   return SCREEN_OK;
 }
 
-#ifdef SCREEN_BWD_PROFILE
-extern "C" SCREEN_API int screen_debug_bwd_profile(unsigned long long* out, int clear) {
-  if (cudaMemcpyFromSymbol(out, g_bwd_prof, sizeof(unsigned long long) * 16) != cudaSuccess)
-    return -1;
-  unsigned long long lat[4];
-  cudaMemcpyFromSymbol(lat, g_prof_lat, sizeof(lat));
-  out[18] = lat[3] ? lat[2] / lat[3] : 0;   // producer: TMA issue -> its plain arrival
-  out[16] = lat[1] ? lat[0] / lat[1] : 0;   // mean load latency when the MMA warp waited
-  out[17] = lat[1];
-  if (clear) {
-    unsigned long long z[16] = {};
-    cudaMemcpyToSymbol(g_bwd_prof, z, sizeof(z));
-    cudaMemcpyToSymbol(g_prof_lat, z, 4 * sizeof(unsigned long long));
-  }
-  return 0;
-}
-#endif
 
 int tc_bwd_device_status(bool clear) {
   int v = 0;

@@ -5,6 +5,9 @@
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <mutex>
+#include <set>
+#include <tuple>
 #include "../../include/screening_b200.h"
 
 namespace screen {
@@ -130,6 +133,36 @@ __device__ __forceinline__ float tanhnorm_bwd_coef(float n) {
 
 }  // namespace screen
 
+
+// ---------------------------------------------------------------------------
+// Host helpers shared by every translation unit of the library.
+// ---------------------------------------------------------------------------
+namespace screen {
+// cudaGetLastError after a launch: on failure record the CUDA message for
+// screen_last_cuda_error() and return SCREEN_ERR_LAUNCH (defined in api.cu).
+int check_launch();
+// Record `e` (if it is an error) for screen_last_cuda_error(); returns
+// SCREEN_ERR_CUDA on error, SCREEN_OK otherwise (defined in api.cu).
+int record_cuda_error(cudaError_t e);
+
+// Raise kernel `fn`'s dynamic shared-memory limit to `bytes` on the current
+// device.  The attribute is per device, so the call is made once per
+// (device, kernel, size) under a lock; later calls return the cached result.
+inline cudaError_t ensure_smem_optin(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<int, const void*, int>> done;
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(dev, fn, bytes);
+  if (done.count(key)) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert(key);
+  return e;
+}
+}  // namespace screen
+
 // ---------------------------------------------------------------------------
 // sm_100a primitives: mbarriers, tcgen05 (TMEM alloc / MMA / ld / st), the
 // global timer used to bound every wait.
@@ -154,21 +187,11 @@ __device__ __forceinline__ void mbar_arrive_cp_async(uint32_t bar) {
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
-#ifdef SCREEN_WAIT_HINT
-  // suspend in hardware (up to ~20 us) until the phase completes
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; "
-      "selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(20000)
-      : "memory");
-#else
   asm volatile(
       "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");
-#endif
   return ok != 0;
 }
 // Wait for phase `parity` of `bar`, giving up after `limit_ns` or when another

@@ -12,6 +12,13 @@ namespace {
 
 constexpr int kT = 256;
 
+// Raised (SCREEN_ERR_INVALID_ARG) by the forward when a label is neither
+// ignore_index nor in [0, V).  F.cross_entropy stops with a device assert
+// there; this kernel gives such a row loss 0 and gradient 0 (the Python
+// caller leaves it out of the mean's denominator) and reports it through
+// screen_device_status().
+__device__ int g_xent_status = 0;
+
 __device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
   const float mm = fmaxf(m, m2);
   if (mm == -INFINITY) return;   // both empty
@@ -61,9 +68,9 @@ __global__ void __launch_bounds__(kT) xent_fwd_kernel(screen_xent_args a) {
     const float lse = M + logf(S);
     a.lse[row] = lse;
     const long long lab = a.labels[row];
-    a.loss[row] = (lab == a.ignore_index || lab < 0 || lab >= a.V)
-                      ? 0.f
-                      : lse - __bfloat162float(x[lab]);
+    const bool out_of_range = lab < 0 || lab >= a.V;
+    if (out_of_range && lab != a.ignore_index) atomicExch(&g_xent_status, (int)SCREEN_ERR_INVALID_ARG);
+    a.loss[row] = (lab == a.ignore_index || out_of_range) ? 0.f : lse - __bfloat162float(x[lab]);
   }
 }
 
@@ -104,6 +111,17 @@ int xent_check(const screen_xent_args* a, bool bwd) {
 }
 
 }  // namespace
+
+int xent_device_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_xent_status, sizeof(int)) != cudaSuccess) return SCREEN_ERR_CUDA;
+  if (clear && v != 0) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_xent_status, &z, sizeof(int));
+  }
+  return v;
+}
+
 }  // namespace screen
 
 extern "C" int screen_cross_entropy_fwd(const screen_xent_args* a, screen_stream_t stream) {
@@ -111,7 +129,7 @@ extern "C" int screen_cross_entropy_fwd(const screen_xent_args* a, screen_stream
   const int st = xent_check(a, false);
   if (st != 1) return st;
   xent_fwd_kernel<<<(unsigned)a->rows, kT, 0, (cudaStream_t)stream>>>(*a);
-  return cudaGetLastError() == cudaSuccess ? SCREEN_OK : SCREEN_ERR_CUDA;
+  return check_launch();
 }
 
 extern "C" int screen_cross_entropy_bwd(const screen_xent_args* a, screen_stream_t stream) {
@@ -119,5 +137,5 @@ extern "C" int screen_cross_entropy_bwd(const screen_xent_args* a, screen_stream
   const int st = xent_check(a, true);
   if (st != 1) return st;
   xent_bwd_kernel<<<(unsigned)a->rows, kT, 0, (cudaStream_t)stream>>>(*a);
-  return cudaGetLastError() == cudaSuccess ? SCREEN_OK : SCREEN_ERR_CUDA;
+  return check_launch();
 }

@@ -557,12 +557,9 @@ void launch_decode(const screen_decode_args& a, float* part, cudaStream_t s) {
   if (nstages < kDecConsumers) nstages = kDecConsumers;
   const size_t smem = (size_t)nstages * stage_bytes;
   if (smem <= (200u << 10) && stage_bytes % 16 == 0) {
-    static bool attr_set = false;  // per template instance
-    if (!attr_set) {
-      cudaFuncSetAttribute(decode_bulk_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           200 << 10);
-      attr_set = true;
-    }
+    // the opt-in is per device; on failure the error stays in
+    // cudaGetLastError for the entry point's launch check
+    if (ensure_smem_optin((const void*)decode_bulk_kernel<T, D>, 200 << 10) != cudaSuccess) return;
     decode_bulk_kernel<T, D><<<grid, 32 * (kDecConsumers + 1), smem, s>>>(a, part, nstages, sk);
   } else {
     decode_split_kernel<T, D><<<grid, 128, 0, s>>>(a, part);

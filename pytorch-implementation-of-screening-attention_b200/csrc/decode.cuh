@@ -6,4 +6,5 @@ namespace screen {
 void kv_append(const screen_kv_append_args& a, cudaStream_t s);
 void decode(const screen_decode_args& a, float* part, cudaStream_t s);
 int decode_device_status(bool clear);
+int xent_device_status(bool clear);
 }  // namespace screen

@@ -38,7 +38,10 @@ void* scratch_on_current_device() {
   if (!g_scratch_ptr[dev]) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess || !p) return nullptr;
+    if (e != cudaSuccess || !p) {
+      screen::record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+      return nullptr;
+    }
     g_scratch_ptr[dev] = p;
   }
   return g_scratch_ptr[dev];
@@ -69,7 +72,7 @@ int screen_decode_noalloc(const screen_decode_args* a, screen_stream_t stream) {
   void* scratch = scratch_on_current_device();
   if (!scratch) return SCREEN_ERR_CUDA;
   screen::decode(*a, reinterpret_cast<float*>(scratch), (cudaStream_t)stream);
-  return cudaGetLastError() == cudaSuccess ? SCREEN_OK : SCREEN_ERR_LAUNCH;
+  return screen::check_launch();
 }
 
 }  // extern "C"

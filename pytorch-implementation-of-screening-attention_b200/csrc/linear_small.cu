@@ -139,13 +139,16 @@ __global__ void __launch_bounds__(kWarps * 32) rows_linear_kernel(screen_rows_li
 }
 
 template <int M>
-void launch_rows_linear(const screen_rows_linear_args& a, cudaStream_t st) {
+int launch_rows_linear(const screen_rows_linear_args& a, cudaStream_t st) {
   const size_t smem = (size_t)M * a.K * 2;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(rows_linear_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+  // one opt-in per device at the 200 KB maximum covers every K
+  if (smem > 48 * 1024) {
+    const cudaError_t e = ensure_smem_optin((const void*)rows_linear_kernel<M>, 200 * 1024);
+    if (e != cudaSuccess) return record_cuda_error(e);
+  }
   const unsigned grid = (unsigned)((a.N + kWarps - 1) / kWarps);
   rows_linear_kernel<M><<<grid, kWarps * 32, smem, st>>>(a);
+  return check_launch();
 }
 
 }  // namespace
@@ -165,15 +168,13 @@ extern "C" int screen_rows_linear(const screen_rows_linear_args* a, screen_strea
   if ((size_t)a->M * a->K * 2 > 200 * 1024) return SCREEN_ERR_UNSUPPORTED;
   cudaStream_t st = (cudaStream_t)stream;
   switch (a->M) {
-    case 1: launch_rows_linear<1>(*a, st); break;
-    case 2: launch_rows_linear<2>(*a, st); break;
-    case 3: launch_rows_linear<3>(*a, st); break;
-    case 4: launch_rows_linear<4>(*a, st); break;
-    case 5: launch_rows_linear<5>(*a, st); break;
-    case 6: launch_rows_linear<6>(*a, st); break;
-    case 7: launch_rows_linear<7>(*a, st); break;
-    default: launch_rows_linear<8>(*a, st); break;
+    case 1: return launch_rows_linear<1>(*a, st);
+    case 2: return launch_rows_linear<2>(*a, st);
+    case 3: return launch_rows_linear<3>(*a, st);
+    case 4: return launch_rows_linear<4>(*a, st);
+    case 5: return launch_rows_linear<5>(*a, st);
+    case 6: return launch_rows_linear<6>(*a, st);
+    case 7: return launch_rows_linear<7>(*a, st);
+    default: return launch_rows_linear<8>(*a, st);
   }
-  const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SCREEN_OK : SCREEN_ERR_CUDA;
 }

@@ -137,7 +137,10 @@ class CrossEntropyFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, logits, labels, ignore_index):
         lse, loss = _lib.cross_entropy_fwd(logits, labels, ignore_index)
-        count = (labels != ignore_index).sum().to(torch.float32)
+        # rows whose label is outside [0, V) get loss 0 in the kernel (which
+        # flags them in screen_device_status); they stay out of the mean too
+        V = logits.shape[1]
+        count = ((labels != ignore_index) & (labels >= 0) & (labels < V)).sum().to(torch.float32)
         ctx.save_for_backward(logits, labels, lse, count)
         ctx.ignore_index = ignore_index
         return loss.sum() / count

@@ -27,8 +27,11 @@ def test_struct_sizes_and_version(ms):
     lib = ms._lib.load()
     assert lib.screen_version() == ms._lib.ABI_VERSION
     L = ms._lib
-    for i, st in enumerate((L.FwdArgs, L.BwdArgs, L.KVCacheDesc, L.KVAppendArgs, L.DecodeArgs)):
-        assert lib.screen_sizeof_args(i) == ctypes.sizeof(st)
+    mirrors = (L.FwdArgs, L.BwdArgs, L.KVCacheDesc, L.KVAppendArgs, L.DecodeArgs,
+               L.RowsLinearArgs, L.XentArgs)
+    for i, st in enumerate(mirrors):
+        assert lib.screen_sizeof_args(i) == ctypes.sizeof(st), st.__name__
+    assert lib.screen_sizeof_args(len(mirrors)) == -1
     assert lib.screen_sizeof_args(99) == -1
 
 

@@ -39,3 +39,21 @@ def test_cross_entropy_all_ignored_is_nan_like_torch(cuda):
     labels = torch.full((4,), -100, device=cuda)
     assert torch.isnan(FN.cross_entropy(logits, labels))
     assert torch.isnan(F.cross_entropy(logits.float(), labels, ignore_index=-100))
+
+
+def test_cross_entropy_flags_out_of_range_labels(cuda, ms):
+    """A label outside [0, V) that is not ignore_index: F.cross_entropy stops
+    with a device assert; the fused kernel gives the row loss 0, leaves it out
+    of the mean and raises the device status word instead."""
+    ms._lib.device_status(clear=True)
+    g = torch.Generator(device=cuda).manual_seed(5)
+    logits = torch.randn(6, 32, device=cuda, generator=g).to(torch.bfloat16)
+    labels = torch.tensor([3, 40, 7, -5, -100, 0], device=cuda)
+    loss = FN.cross_entropy(logits, labels)
+    keep = torch.tensor([0, 2, 5], device=cuda)
+    ref = F.cross_entropy(logits.float()[keep], labels[keep])
+    assert rel_err(loss.float().view(1), ref.view(1)) <= 1e-4
+    assert ms._lib.device_status(clear=True) == -1
+    # in-range labels leave the status clear
+    FN.cross_entropy(logits, labels.clamp(0, 31))
+    assert ms._lib.device_status(clear=True) == 0

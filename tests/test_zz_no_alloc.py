@@ -19,13 +19,13 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda:0")
 
 
-def _cache_with_tokens(ms, dtype, B, H, D, T, w_max):
-    g = torch.Generator(device=DEV).manual_seed(11)
-    cache = ms.PagedKVCache(1, B, H, D, max_len=T, max_window=w_max, dtype=dtype, device=DEV,
+def _cache_with_tokens(ms, dtype, B, H, D, T, w_max, dev=DEV):
+    g = torch.Generator(device=dev).manual_seed(11)
+    cache = ms.PagedKVCache(1, B, H, D, max_len=T, max_window=w_max, dtype=dtype, device=dev,
                             page_size=16)
-    k = torch.randn(B, T, H, D, device=DEV, generator=g).to(dtype)
-    v = torch.randn(B, T, H, D, device=DEV, generator=g).to(dtype)
-    cache.append(0, k, v, torch.zeros(B, dtype=torch.int32, device=DEV))
+    k = torch.randn(B, T, H, D, device=dev, generator=g).to(dtype)
+    v = torch.randn(B, T, H, D, device=dev, generator=g).to(dtype)
+    cache.append(0, k, v, torch.zeros(B, dtype=torch.int32, device=dev))
     return cache, k
 
 
@@ -41,36 +41,55 @@ def _args(L, q, seq_lens, r, w, cache, y, no, num_splits, workspace=None):
     return a
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_noalloc_decode_matches_workspace_decode_twice(ms, dtype):
+def _compare_twice(ms, dtype, dev):
+    """Two noalloc calls in a row on `dev`, each against screen_decode with a
+    caller workspace on the same inputs."""
     L = ms._lib
     lib = L.load()
     B, H, D, T = 4, 3, 64, 200
-    cache, k = _cache_with_tokens(ms, dtype, B, H, D, T, w_max=120.0)
-    r = torch.tensor([1.05, 1.2, 1.6], device=DEV)
-    w = torch.tensor([7.5, 60.0, 120.0], device=DEV)
-    stream = torch.cuda.current_stream().cuda_stream
+    cache, k = _cache_with_tokens(ms, dtype, B, H, D, T, w_max=120.0, dev=dev)
+    r = torch.tensor([1.05, 1.2, 1.6], device=dev)
+    w = torch.tensor([7.5, 60.0, 120.0], device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
     tol = 1e-4 if dtype == torch.float32 else 2e-2
     for call, (t, splits) in enumerate([(150, 4), (199, 3)]):
         # the query of each call leans on a different cached key, so a stale
         # partial left by the first call would show in the second
-        q = (k[:, t - 5] + 0.3 * torch.randn(B, H, D, device=DEV, dtype=torch.float32)
+        q = (k[:, t - 5] + 0.3 * torch.randn(B, H, D, device=dev, dtype=torch.float32)
              .to(dtype)).contiguous()
-        seq_lens = torch.full((B,), t + 1, dtype=torch.int32, device=DEV)
-        y_ref = torch.empty(B, H, D, dtype=dtype, device=DEV)
-        no_ref = torch.empty(B, H, dtype=torch.float32, device=DEV)
-        ws = torch.empty(B * H * splits * D * 4 + 256, dtype=torch.uint8, device=DEV)
+        seq_lens = torch.full((B,), t + 1, dtype=torch.int32, device=dev)
+        y_ref = torch.empty(B, H, D, dtype=dtype, device=dev)
+        no_ref = torch.empty(B, H, dtype=torch.float32, device=dev)
+        ws = torch.empty(B * H * splits * D * 4 + 256, dtype=torch.uint8, device=dev)
         a_ref = _args(L, q, seq_lens, r, w, cache, y_ref, no_ref, splits, ws)
         assert lib.screen_decode(ctypes.byref(a_ref), ctypes.c_void_p(stream)) == 0
-        y = torch.full((B, H, D), float("nan"), dtype=dtype, device=DEV)
-        no = torch.full((B, H), float("nan"), dtype=torch.float32, device=DEV)
+        y = torch.full((B, H, D), float("nan"), dtype=dtype, device=dev)
+        no = torch.full((B, H), float("nan"), dtype=torch.float32, device=dev)
         a = _args(L, q, seq_lens, r, w, cache, y, no, splits)
         assert lib.screen_decode_noalloc(ctypes.byref(a), ctypes.c_void_p(stream)) == 0, call
-        torch.cuda.synchronize()
+        torch.cuda.synchronize(dev)
         assert torch.isfinite(y.float()).all()
         assert rel_err(y, y_ref) <= tol, call
         assert rel_err(no, no_ref) <= tol, call
         assert torch.count_nonzero(y_ref) > 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_noalloc_decode_matches_workspace_decode_twice(ms, dtype):
+    with torch.cuda.device(DEV):
+        _compare_twice(ms, dtype, DEV)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs a second visible GPU")
+def test_noalloc_decode_on_a_second_device(ms):
+    """The scratch address and the decode kernel's shared-memory opt-in are
+    per device: a process that decoded on cuda:0 must also decode on cuda:1."""
+    with torch.cuda.device(DEV):
+        _compare_twice(ms, torch.bfloat16, DEV)
+    dev1 = torch.device("cuda:1")
+    with torch.cuda.device(dev1):
+        _compare_twice(ms, torch.bfloat16, dev1)
 
 
 def test_noalloc_decode_rejects_requests_beyond_the_scratch(ms):
