@@ -1,19 +1,26 @@
-"""Benchmark: Screening Attention fwd+bwd on B200 (BASELINE.json metric).
+"""Benchmark: Screening Attention fwd+bwd on B200.
 
-Workload (cfg3 of BASELINE.json): isolated ScreeningAttention, d_model=1024,
-16 heads x 64, causal, batch 8 per GPU, T=4096, bf16, x ~ N(0,1), r_h ~ U[1,2],
+Headline workload (cfg3): isolated ScreeningAttention, d_model=1024, 16
+heads x 64, causal, global batch 8, T=4096, bf16, x ~ N(0,1), r_h ~ U[1,2],
 w_h ~ U[256,4096] (seeded).  One step = module forward + backward (q/k/v/out
-projections on cuBLAS, the screening core on this repo's kernels); with N>1
-GPUs every rank runs its own batch of 8 (weak scaling, batch sharding) and the
-projection-weight gradients are all-reduced over NCCL, as data-parallel
-training does.
+projections on cuBLAS, the screening core on this repo's kernels).  With N
+GPUs the global batch of 8 is split over the ranks (8/N sequences each:
+strong scaling, batch sharding) and the projection-weight gradients are
+all-reduced over NCCL in buckets that overlap the backward (DDP), as
+data-parallel training does.  A weak-scaling run (8 sequences per rank) is
+reported beside it.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload cfg3|decode|prefill|lm|generate]
 
-Prints one JSON line (rank 0).  `--impl reference` times the reference
-algorithm's CPU implementation (the oracle restatement of
-multiscreen/attention.py, fp32, all host threads) on a bounded sample of the
-same workload (one sequence of T=4096 with all 16 heads per step).
+Prints one JSON line (rank 0).  At one GPU the cfg3 line also carries
+sub-records measured in the same run: the decode kernel's HBM fraction at a
+100K-key window, attention-only fwd+bwd at T=32K and 128K, the cfg2 training
+step, the cfg5 decode step and the reference's own Triton kernels at cfg3
+shapes.  `--impl reference` times the reference algorithm's CPU
+implementation (the windowed restatement of multiscreen/attention.py in the
+oracle, fp32, all host threads) on a bounded sample of the same workload
+(one of the 8 sequences, all 16 heads, per step).
 """
 from __future__ import annotations
 
@@ -36,8 +43,12 @@ PKG = "pytorch-implementation-of-screening-attention_b200"
 
 D_MODEL, HEADS, HEAD_DIM, BATCH, SEQ = 1024, 16, 64, 8, 4096
 METRIC = "screening-attn fwd+bwd tokens/s (ScreeningAttention d=1024 H=16 D=64 causal T=4096, bf16)"
-WORKLOAD = ("cfg3: isolated ScreeningAttention d_model=1024, 16 heads x 64, causal, batch 8/GPU, "
-            "T=4096, bf16, r~U[1,2], w~U[256,4096], fwd+bwd")
+WORKLOAD = ("cfg3: isolated ScreeningAttention d_model=1024, 16 heads x 64, causal, global batch 8 "
+            "split over the GPUs, T=4096, bf16, r~U[1,2], w~U[256,4096], fwd+bwd")
+# this repo's kernels launched per cfg3 step: forward (prep, k meta, CTA
+# order, attention), backward (TanhNorm-grad prologue, aux norms, CTA order,
+# fused attention, dq finalize, dr/dw reduction)
+LAUNCHES_PER_STEP = 10
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -119,6 +130,19 @@ class ClockSampler:
                 "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
 
 
+class NullClock:
+    """Stand-in for ClockSampler inside sub-records (the outer line samples)."""
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        pass
+
+    def summary(self):
+        return None
+
+
 def cpu_reference_sample(threads: int | None = None):
     """Oracle fwd+bwd of one sequence (B=1, T=4096, 16 heads) in fp32 on the
     host; returns (seconds, tokens, threads)."""
@@ -150,13 +174,14 @@ def run_reference(args, rank):
             times.append(dt)
     per = sum(times) / len(times)
     val = SEQ / per
-    sample = f"1 sequence x T={SEQ} x {HEADS} heads (1/{BATCH} of one GPU's batch) per step, fp32"
+    sample = (f"windowed CPU restatement of multiscreen/attention.py (oracle), fp32: 1 sequence x "
+              f"T={SEQ} x {HEADS} heads per step = 1/{BATCH} of the cfg3 batch")
     line = {
         "impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "seq_len": SEQ, "global_batch": BATCH * args.gpus},
+        "config": {"workload": WORKLOAD, "seq_len": SEQ, "global_batch": BATCH},
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": nt, "kind": "port",
                          "sample": sample},
         "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -165,30 +190,27 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
-def run_decode(args, rank, world):
+def measure_decode(dev, window: int, steps: int, warmup: int, splits: int = 0, seed: int = 7,
+                   clk=None) -> dict:
     """Decode-kernel roofline: one new token per sequence, B=4 sequences per
     GPU (cfg5: batch 32 over 8 GPUs), 16 heads x 64, bf16 paged cache with
-    `--decode-window` cached keys in every head's window (the cfg5 prompt is
-    100K tokens; at random init w <= 256, so the window is widened here to
-    make the kernel's HBM stream measurable).  Algorithmic bytes per launch =
+    `window` cached keys in every head's window (the cfg5 prompt is 100K
+    tokens; at random init w <= 256, so the window is widened here to make
+    the kernel's HBM stream measurable).  Algorithmic bytes per launch =
     keys in window x (K + V rows) + query + output."""
     import importlib
     ms = importlib.import_module(PKG)
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    B, H, D, Wn = 4, HEADS, HEAD_DIM, args.decode_window
-    T = Wn + 1
+    B, H, D = 4, HEADS, HEAD_DIM
+    T = window + 1
     cache = ms.PagedKVCache(1, B, H, D, max_len=T, max_window=float(T), dtype=torch.bfloat16,
                             device=dev, page_size=64)
-    if args.decode_splits > 0:
-        cache.num_splits = args.decode_splits
-    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    if splits > 0:
+        cache.num_splits = splits
+    g = torch.Generator(device=dev).manual_seed(seed)
     for pg in (cache.k_pages[0], cache.v_pages[0]):
         pg.copy_(torch.nn.functional.normalize(
             torch.randn(pg.shape, device=dev, generator=g), dim=-1).to(torch.bfloat16))
     q = torch.randn(B, H, D, device=dev, generator=g).to(torch.bfloat16)
-    # queries lean on random cached keys so alpha (and the V reads) are non-zero
     seq = torch.full((B,), T, dtype=torch.int32, device=dev)
     r = torch.full((H,), 1.02, device=dev)
     w = torch.full((H,), float(T + 1), device=dev)
@@ -198,13 +220,13 @@ def run_decode(args, rank, world):
     need_flush = window_bytes < 4 * 126 * 1024 * 1024
     flush = torch.empty(256 * 1024 * 1024 // 4 if need_flush else 1, dtype=torch.float32,
                         device=dev)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         cache.decode(0, q, seq, r, w)
     torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    clk = ClockSampler(local)
-    clk.__enter__()
+           for _ in range(steps)]
+    if clk is not None:
+        clk.__enter__()
     for a, b in evs:
         if need_flush:
             flush.zero_()
@@ -212,28 +234,41 @@ def run_decode(args, rank, world):
         cache.decode(0, q, seq, r, w)
         b.record()
     torch.cuda.synchronize()
-    clk.__exit__(None, None, None)
+    if clk is not None:
+        clk.__exit__(None, None, None)
     ms_per = statistics.median(a.elapsed_time(b) for a, b in evs)
     keys = B * H * T
     alg_bytes = keys * D * 2 * 2 + 2 * B * H * D * 2
     gbs = alg_bytes / (ms_per / 1e3) / 1e9
     pk, kind = peaks()
     peak = float(pk["hbm_gbs"])
+    return {"workload": f"cfg5 decode kernel: B=4/GPU, H=16, D=64, {T} keys per (b,h) window, "
+                        f"num_splits={cache.num_splits}",
+            "l2": ("flushed (256 MiB write) between launches" if need_flush else
+                   f"inputs larger than L2 ({window_bytes / 2**30:.2f} GiB of K/V read per "
+                   "launch), no flush"),
+            "ms": ms_per, "gbs": gbs, "peak_gbs": peak, "frac": gbs / peak, "peak_kind": kind,
+            "bytes_per_launch": alg_bytes, "tokens_per_s_attention_only": B / (ms_per / 1e3)}
+
+
+def run_decode(args, rank, world):
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    clk = ClockSampler(local)
+    d = measure_decode(dev, args.decode_window, args.steps, args.warmup, args.decode_splits,
+                       seed=7 + rank, clk=clk)
     if rank == 0:
         print(json.dumps({
             "metric": "screening decode attention, paged bf16 KV, HBM bandwidth",
-            "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per, "higher_is_better": True,
+            "value": d["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": d["ms"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"cfg5 decode kernel: B=4/GPU, H=16, D=64, {T} keys per "
-                                   f"(b,h) window, num_splits={cache.num_splits}",
-                       "l2": ("flushed (256 MiB write) between launches" if need_flush else
-                              f"inputs larger than L2 ({window_bytes / 2**30:.2f} GiB of K/V "
-                              "read per launch), no flush")},
-            "roofline": {"bound": "hbm", "kernel": "decode_split+finish", "achieved": gbs,
-                         "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind,
-                         "traffic": None},
-            "tokens_per_s_attention_only": B / (ms_per / 1e3),
+            "config": {"workload": d["workload"], "l2": d["l2"]},
+            "roofline": {"bound": "hbm", "kernel": "decode_bulk+finish", "achieved": d["gbs"],
+                         "peak": d["peak_gbs"], "unit": "GB/s", "frac": d["frac"],
+                         "peak_kind": d["peak_kind"], "traffic": None},
+            "tokens_per_s_attention_only": d["tokens_per_s_attention_only"],
             "clocks": clk.summary(), "gpu_launches": 2 * args.steps,
         }), flush=True)
 
@@ -402,7 +437,7 @@ def run_prefill(args, rank, world):
         dist.destroy_process_group()
 
 
-def run_lm(args, rank, world):
+def run_lm(args, rank, world, sub=False):
     """cfg2: one training step of MultiscreenLM(50257, d_model=256, 4 heads,
     4 layers, max_seq_len=512) on batch 16 x T=512 synthetic token ids per
     GPU: bf16 autocast forward + backward, fp32 master weights, fused AdamW;
@@ -470,7 +505,7 @@ def run_lm(args, rank, world):
     for _ in range(args.warmup):
         step(ids)
     torch.cuda.synchronize()
-    clk = ClockSampler(local)
+    clk = NullClock() if sub else ClockSampler(local)
     clk.__enter__()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
@@ -512,6 +547,12 @@ def run_lm(args, rank, world):
     peak = float(pk.get("bf16_tflops_sustained", pk["bf16_tflops"]))
     tf = (dense + attn) / (ms_per / 1e3) / 1e12
     cpu = None
+    if sub:
+        return {"workload": "cfg2: MultiscreenLM(50257, 256, 4, 4), batch 16 x 512, bf16 "
+                            "autocast, fp32 master weights, fused AdamW, one CUDA graph per step",
+                "ms_per_step": ms_per, "tokens_per_s": toks / (ms_per / 1e3),
+                "e2e_tokens_per_s": toks / (e2e_ms / args.steps / 1e3),
+                "tflops_per_gpu": tf / world, "frac_of_sustained_peak": tf / world / peak}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import screening_oracle as oracle
         nt = os.cpu_count() or 1
@@ -554,7 +595,7 @@ def run_lm(args, rank, world):
         dist.destroy_process_group()
 
 
-def run_generate(args, rank, world):
+def run_generate(args, rank, world, sub=False):
     """cfg5: MultiscreenLM(50257, 1024, 16, 12) at random init (w = 2..256 per
     head), 4 prompts of --prompt-len random tokens per GPU, 256 greedy new
     tokens through the paged KV cache.  Prefill and decode are timed apart
@@ -602,7 +643,7 @@ def run_generate(args, rank, world):
 
     for _ in range(args.warmup):
         one()
-    clk = ClockSampler(local)
+    clk = NullClock() if sub else ClockSampler(local)
     clk.__enter__()
     if dist is not None:
         dist.barrier()
@@ -614,6 +655,12 @@ def run_generate(args, rank, world):
         t = torch.tensor([pre, dec], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         pre, dec = (float(x) for x in t.tolist())
+    if sub:
+        return {"workload": f"cfg5: MultiscreenLM(50257, 1024, 16, 12), 4 sequences x {T0}-token "
+                            f"prompts, {NEW} greedy tokens, paged bf16 cache, one CUDA-graph "
+                            "replay per token",
+                "decode_ms_per_token": dec / NEW, "decode_tokens_per_s": B * NEW / (dec / 1e3),
+                "prefill_ms": pre, "prefill_tokens_per_s": B * T0 / (pre / 1e3)}
     if rank == 0:
         print(json.dumps({
             "metric": "generate() decode tokens/s (cfg5: MultiscreenLM 1024 x 16 x 12, 100K-token "
@@ -640,7 +687,11 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=BATCH, help="per-GPU batch (profiling: smaller)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="per-GPU batch override (profiling); default global batch / GPUs")
+    ap.add_argument("--global-batch", type=int, default=BATCH)
+    ap.add_argument("--no-sub", action="store_true",
+                    help="cfg3: skip the sub-records (weak scaling, other configurations)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-reps", type=int, default=5)
     ap.add_argument("--workload", default="cfg3", choices=["cfg3", "decode", "prefill", "lm", "generate"],
@@ -677,6 +728,105 @@ def main():
         run_generate(args, rank, world)
         return
 
+    run_cfg3(args, rank, world, local)
+
+
+def time_events(fn, reps, flush=None, warmup=1):
+    """Median CUDA-event time (ms) of fn() on the current stream."""
+    for _ in range(warmup):
+        fn()
+    out = []
+    for _ in range(reps):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        out.append(a.elapsed_time(b))
+    return statistics.median(out)
+
+
+def measure_long_context(dev, T: int, reps: int = 3) -> dict:
+    """Attention-only fwd+bwd (the screening core: screen_fwd, screen_bwd) at
+    batch 1, 16 heads x 64, length T, with the cfg3 per-head r / w draws;
+    q, k, v ~ N(0, 1) bf16.  TFLOP/s on the windowed algorithmic pairs
+    (2 GEMMs forward, 5 backward, 2*D flops per pair per GEMM)."""
+    import importlib
+    L = importlib.import_module(PKG)._lib
+    g = torch.Generator(device=dev).manual_seed(T)
+    q, k, v, dy = (torch.randn(1, T, HEADS, HEAD_DIM, device=dev, generator=g)
+                   .to(torch.bfloat16) for _ in range(4))
+    r, w = (t.to(dev) for t in head_params())
+    y, no, nq, nk, nv, q2, k2, v2 = L.screen_fwd(q, k, v, r, w, True)
+    fwd = time_events(lambda: L.screen_fwd(q, k, v, r, w, True), reps)
+    bwd = time_events(lambda: L.screen_bwd(q2, k2, v2, nq, nk, nv, y, no, dy, r, w), reps)
+    pairs = windowed_pairs(w.cpu(), T)
+    gemm = 2.0 * HEAD_DIM
+    pk, kind = peaks()
+    peak = float(pk["bf16_tflops"])
+    tf_f = 2 * gemm * pairs / (fwd / 1e3) / 1e12
+    tf_b = 5 * gemm * pairs / (bwd / 1e3) / 1e12
+    tf = 7 * gemm * pairs / ((fwd + bwd) / 1e3) / 1e12
+    return {"T": T, "batch": 1, "fwd_ms": fwd, "bwd_ms": bwd,
+            "tokens_per_s": T / ((fwd + bwd) / 1e3),
+            "tflops_windowed": {"fwd": tf_f, "bwd": tf_b, "fwd_bwd": tf},
+            "frac_of_peak": {"fwd": tf_f / peak, "bwd": tf_b / peak, "fwd_bwd": tf / peak},
+            "peak_tflops": peak, "peak_kind": kind,
+            "windowed_pairs": pairs, "dense_pairs": HEADS * T * (T + 1) / 2}
+
+
+def measure_prior_art_triton(dev, ours_fwd_ms: float, ours_bwd_ms: float, reps: int = 3) -> dict:
+    """The reference's own GPU path, its Triton kernels screening_attention_fwd
+    (multiscreen/kernels/screening_fwd.py:216-270) and screening_attention_bwd
+    (multiscreen/kernels/screening_bwd.py:229-287), unmodified from the
+    installed copy under baseline/_ref, at the cfg3 attention shapes (B=8,
+    H=16, T=4096, D=64, bf16 unit rows, the cfg3 r / w draws).  Its backward
+    returns dq, dk, dv only (no dr, dw)."""
+    ref = REPO / "baseline" / "_ref"
+    if not (ref / "multiscreen").exists():
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    from multiscreen.kernels.screening_fwd import screening_attention_fwd
+    from multiscreen.kernels.screening_bwd import screening_attention_bwd
+    g = torch.Generator(device=dev).manual_seed(3)
+    q, k, v, do = (torch.nn.functional.normalize(
+        torch.randn(BATCH, HEADS, SEQ, HEAD_DIM, device=dev, generator=g), dim=-1)
+        .to(torch.bfloat16) for _ in range(4))
+    r, w = (t.to(dev) for t in head_params())
+    fwd = time_events(lambda: screening_attention_fwd(q, k, v, r, w, causal=True), reps)
+    bwd = time_events(lambda: screening_attention_bwd(q, k, v, do, r, w, causal=True), reps)
+    return {"source": "multiscreen.kernels (Triton), unmodified, baseline/_ref",
+            "shape": "B=8, H=16, T=4096, D=64, causal, bf16 in, fp32 out",
+            "triton_fwd_ms": fwd, "triton_bwd_ms": bwd, "ours_fwd_ms": ours_fwd_ms,
+            "ours_bwd_ms": ours_bwd_ms, "speedup_fwd": fwd / ours_fwd_ms,
+            "speedup_bwd": bwd / ours_bwd_ms,
+            "note": "the Triton backward computes dq, dk, dv only; ours adds dr, dw"}
+
+
+def _sub(fn):
+    try:
+        return fn()
+    except Exception as e:  # a sub-record must not sink the headline line
+        return {"error": f"{type(e).__name__}: {e}"[:300]}
+
+
+class _SelfAttention(torch.nn.Module):
+    """attn(x, x, x) as a one-argument module, so that DDP's input handling
+    cannot break the query-is-key-is-value identity of self-attention."""
+
+    def __init__(self, attn):
+        super().__init__()
+        self.attn = attn
+
+    def forward(self, x):
+        return self.attn(x, x, x)
+
+
+def run_cfg3(args, rank, world, local):
+    import argparse as _ap
     import importlib
     ms = importlib.import_module(PKG)
     L = ms._lib
@@ -691,29 +841,44 @@ def main():
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.profile_only):
         dt, toks, nt = cpu_reference_sample()
         cpu = {"value": toks / dt, "unit": "tokens/s", "cores": nt, "kind": "port",
-               "sample": f"oracle fwd+bwd, 1 sequence x T={SEQ} x {HEADS} heads, fp32, {dt:.1f} s"}
+               "sample": f"windowed CPU restatement of multiscreen/attention.py (oracle) fwd+bwd, "
+                         f"fp32, 1 sequence x T={SEQ} x {HEADS} heads = 1/{BATCH} of the cfg3 "
+                         f"batch, {dt:.1f} s"}
 
-    B = args.batch
+    # strong scaling: the global batch of 8 is split over the ranks
+    GB = args.global_batch
+    if GB % world:
+        raise SystemExit(f"global batch {GB} is not divisible by {world} ranks")
+    B = args.batch if args.batch else GB // world
     torch.manual_seed(0)
-    attn = ms.ScreeningAttention(D_MODEL, HEADS).to(dev)
+    attn = ms.ScreeningAttention(D_MODEL, HEADS)
     r_h, w_h = head_params()
     with torch.no_grad():
         attn.s_r.copy_(torch.log(r_h - 1.0))
         attn.s_v.copy_(torch.log(w_h - 1.0))
-    attn = attn.to(torch.bfloat16)
-    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
-    x = torch.randn(B, SEQ, D_MODEL, device=dev, generator=gen).to(torch.bfloat16)
-    cot = torch.randn(B, SEQ, D_MODEL, device=dev, generator=gen).to(torch.bfloat16)
+    attn = attn.to(dev).to(torch.bfloat16)
+    net = _SelfAttention(attn)
+    if dist is not None:
+        # gradient all-reduce in buckets, each launched from the autograd
+        # hooks as soon as its gradients are ready, on NCCL's stream: the
+        # out_proj bucket overlaps the screening backward
+        net = torch.nn.parallel.DistributedDataParallel(
+            net, device_ids=[local], bucket_cap_mb=2, gradient_as_bucket_view=True)
     params = [p for p in attn.parameters()]
 
-    def step(inp):
+    def make_inputs(batch, seed_rank):
+        gen = torch.Generator(device=dev).manual_seed(1000 + seed_rank)
+        xx = torch.randn(batch, SEQ, D_MODEL, device=dev, generator=gen).to(torch.bfloat16)
+        cc = torch.randn(batch, SEQ, D_MODEL, device=dev, generator=gen).to(torch.bfloat16)
+        return xx, cc
+
+    x, cot = make_inputs(B, rank)
+
+    def step(inp, cot_=None):
         for p in params:
             p.grad = None
-        y = attn(inp, inp, inp)
-        y.backward(cot)
-        if dist is not None:
-            flat = torch.cat([p.grad.reshape(-1).float() for p in params])
-            dist.all_reduce(flat)
+        y = net(inp)
+        y.backward(cot if cot_ is None else cot_)
         return y
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
@@ -730,29 +895,43 @@ def main():
         torch.cuda.synchronize()
         return
 
-    # ---- timed region: K steps, L2 flushed between steps (outside the events)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    for s0, s1 in evs:
-        flush.zero_()
-        s0.record()
-        step(x)
-        s1.record()
-    torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    step_ms = [a.elapsed_time(b) for a, b in evs]
-    total_ms = sum(step_ms)
-    if dist is not None:
-        t = torch.tensor([total_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    ms_per_step = total_ms / args.steps
+    def timed(inp, cot_):
+        """K steps, L2 flushed between steps (outside the events); the job
+        time is the max over ranks of the summed step times."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for s0, s1 in evs:
+            flush.zero_()
+            s0.record()
+            step(inp, cot_)
+            s1.record()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        tot = sum(a.elapsed_time(b) for a, b in evs)
+        if dist is not None:
+            t = torch.tensor([tot], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            tot = float(t.item())
+        return tot / args.steps
+
+    ms_per_step = timed(x, cot)
     tokens_per_step = B * SEQ * world
     value = tokens_per_step / (ms_per_step / 1e3)
+
+    weak = None
+    if world > 1 and not args.no_sub:
+        # weak scaling beside it: a full batch of 8 on every rank
+        xw, cw = make_inputs(BATCH, rank)
+        for _ in range(args.warmup):
+            step(xw, cw)
+        wms = timed(xw, cw)
+        weak = {"per_gpu_batch": BATCH, "global_batch": BATCH * world, "ms_per_step": wms,
+                "value": BATCH * SEQ * world / (wms / 1e3), "unit": "tokens/s"}
+        del xw, cw
 
     # ---- per-kernel timing of the screening core (CUDA events, same stream)
     H, Dh = HEADS, HEAD_DIM
@@ -763,27 +942,15 @@ def main():
     stats = torch.zeros(2, dtype=torch.int64, device=dev)
     y, no, nq, nk, nv, q2, k2, v2 = L.screen_fwd(q, k, v, rr, ww, True, tile_stats=stats)
     dy = cot.view(B, SEQ, H, Dh)
-
-    def time_call(fn, reps):
-        out = []
-        for _ in range(reps):
-            flush.zero_()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            fn()
-            b.record()
-            torch.cuda.synchronize()
-            out.append(a.elapsed_time(b))
-        return statistics.median(out)
-
+    reps = args.kernel_reps
     kt = {
-        "fwd": time_call(lambda: L.screen_fwd(q, k, v, rr, ww, True, norms=(nq, nk, nv), stages=2),
-                         args.kernel_reps),
-        "bwd_prologue": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww,
-                                                       stages=1), args.kernel_reps),
+        "fwd": time_events(lambda: L.screen_fwd(q, k, v, rr, ww, True, norms=(nq, nk, nv),
+                                                stages=2), reps, flush),
+        "bwd_prologue": time_events(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww,
+                                                         stages=1), reps, flush),
         # stage 4: the fused key-major kernel (dk, dv and dq) + the dq finalize
-        "bwd": time_call(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww, stages=5),
-                         args.kernel_reps),
+        "bwd": time_events(lambda: L.screen_bwd(q, k, v, nq, nk, nv, y, no, dy, rr, ww,
+                                                stages=5), reps, flush),
     }
     # stage 5 includes the prologue; isolate the attention kernel
     kt["bwd"] = max(kt["bwd"] - kt["bwd_prologue"], 1e-6)
@@ -811,7 +978,7 @@ def main():
     }
     traffic = None
     tfile = REPO / "profiles" / f"{dom}_traffic.txt"
-    if tfile.exists():
+    if tfile.exists() and B == BATCH:
         for ln in tfile.read_text().splitlines():
             if ln.startswith("dram_bytes_per_launch_full_workload:"):
                 traffic = float(ln.split(":")[1])
@@ -845,15 +1012,17 @@ def main():
     used = [False, False]
 
     def issue_copy(i):
-        k2 = i % 2
+        k2_ = i % 2
         with torch.cuda.stream(cp):
-            if used[k2]:
-                cp.wait_event(free[k2])
-            bufs[k2].copy_(x_host, non_blocking=True)
-            ready[k2].record(cp)
+            if used[k2_]:
+                cp.wait_event(free[k2_])
+            bufs[k2_].copy_(x_host, non_blocking=True)
+            ready[k2_].record(cp)
 
     n_all = args.warmup + args.steps
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
     issue_copy(0)
     for i in range(n_all):
         if i == args.warmup:
@@ -879,17 +1048,39 @@ def main():
     if dist is not None:
         t = torch.tensor([e2e_ms, e2e_serial_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms, e2e_serial_ms = (float(v) for v in t.tolist())
+        e2e_ms, e2e_serial_ms = (float(v_) for v_ in t.tolist())
+
+    # ---- sub-records (one GPU): the other configurations' key numbers
+    sub = None
+    if world == 1 and not args.no_sub:
+        del qkv, q, k, v, y, q2, k2, v2, bufs
+        torch.cuda.empty_cache()
+        sub = {}
+        sub["prior_art_triton"] = _sub(lambda: measure_prior_art_triton(dev, kt["fwd"],
+                                                                        kt["bwd"] + kt["bwd_prologue"]))
+        sub["decode_kernel_100k"] = _sub(lambda: measure_decode(dev, 100_000, 10, 3))
+        for T_ in (32768, 131072):
+            sub[f"attention_T{T_ // 1024}k"] = _sub(lambda: measure_long_context(dev, T_))
+        torch.cuda.empty_cache()
+        sa = _ap.Namespace(**vars(args))
+        sa.steps, sa.warmup, sa.no_graph = 10, 3, False
+        sub["cfg2_lm_step"] = _sub(lambda: run_lm(sa, 0, 1, sub=True))
+        torch.cuda.empty_cache()
+        sg = _ap.Namespace(**vars(args))
+        sg.steps, sg.warmup, sg.prompt_len = 1, 1, 100_000
+        sub["cfg5_generate"] = _sub(lambda: run_generate(sg, 0, 1, sub=True))
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "model": "ScreeningAttention(1024, 16)",
-                       "global_batch": B * world, "seq_len": SEQ,
-                       "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) between steps"},
+                       "global_batch": B * world, "per_gpu_batch": B, "seq_len": SEQ,
+                       "parallelism": f"dp{world} (batch sharding; DDP bucketed all-reduce "
+                                      f"overlapped with the backward)" if world > 1 else "dp1",
+                       "l2": "flushed (256 MiB write) between steps"},
             "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": pk_kind,
                          "traffic": traffic,
@@ -902,8 +1093,10 @@ def main():
                     "h2d_gbs_measured": h2d_gbs, "pinned": bool(x_host.is_pinned()),
                     "input_pipeline": "next step's H2D copy on a copy stream during this step",
                     "serial_value": tokens_per_step / (e2e_serial_ms / 1e3)},
+            "weak_scaling": weak,
             "clocks": clk.summary(),
-            "gpu_launches": 6 * args.steps,
+            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            "sub": sub,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:

@@ -278,3 +278,45 @@ def param_grads_reference(q, k, v, r, w, causal=True, key_padding_mask=None, eps
     g = torch.ones_like(y) if dy is None else dy.to(dtype)
     y.backward(g)
     return y.detach(), q.grad, k.grad, v.grad, r.grad, w.grad
+
+
+def windowed_core_grads(q, k, v, r, w, dy, causal=True, q_offset=0, eps=1e-8, chunk=256,
+                        dtype=torch.float64):
+    """(y, dq, dk, dv, dr, dw) of screening_core for the cotangent dy, with
+    bounded memory at long T: the loss sum(y * dy) is a sum over query rows,
+    and row i depends on q_i and on the keys inside its window only
+    (multiscreen/attention.py:156-196, mask exactly zero outside the window,
+    attention.py:117-118), so each block of `chunk` query rows runs forward
+    and backward on its own against its key range and the gradients of k, v,
+    r and w are summed over the blocks.  Inputs (B, T, H, D) on the CPU."""
+    B, Tq, H, D = q.shape
+    Tk = k.shape[1]
+    dmax = int(math.ceil(float(w.detach().max()))) - 1 if H > 0 else -1
+    qd, kd, vd, dyd = (t.detach().to(dtype) for t in (q, k, v, dy))
+    rd = r.detach().to(dtype).requires_grad_(True)
+    wd = w.detach().to(dtype).requires_grad_(True)
+    y = torch.zeros(B, Tq, H, D, dtype=dtype)
+    dq = torch.zeros_like(qd)
+    dk = torch.zeros_like(kd)
+    dv = torch.zeros_like(vd)
+    for i0 in range(0, Tq, chunk):
+        i1 = min(Tq, i0 + chunk)
+        p0, p1 = i0 + q_offset, i1 - 1 + q_offset
+        lo = max(0, p0 - dmax)
+        hi = min(Tk - 1, p1 if causal else p1 + dmax)
+        if hi < lo or dmax < 0:
+            continue
+        qc = qd[:, i0:i1].clone().requires_grad_(True)
+        kc = kd[:, lo:hi + 1].clone().requires_grad_(True)
+        vc = vd[:, lo:hi + 1].clone().requires_grad_(True)
+        # the block's query i sits at key-axis position i + q_offset, i.e.
+        # (i - i0) + (p0 - lo) inside the key slice
+        yc = screening_core(qc, kc, vc, rd, wd, causal, None, eps, q_offset=p0 - lo)
+        yc.backward(dyd[:, i0:i1])
+        y[:, i0:i1] = yc.detach()
+        dq[:, i0:i1] = qc.grad
+        dk[:, lo:hi + 1] += kc.grad
+        dv[:, lo:hi + 1] += vc.grad
+    dr = rd.grad if rd.grad is not None else torch.zeros_like(rd)
+    dw = wd.grad if wd.grad is not None else torch.zeros_like(wd)
+    return y, dq, dk, dv, dr.detach(), dw.detach()
