@@ -393,6 +393,18 @@ __device__ __forceinline__ int item_tiles(const AttnShape& s, int kind, int ntil
   const long long n = hi / 64 - lo / 64 + 1;
   return n > kOrderBuckets - 1 ? kOrderBuckets - 1 : (int)n;
 }
+// Sort key of a CTA.  Forward (kind 0): its own tile count.  Backward
+// (kind 1): the count of its head's first key tile, so all key tiles of one
+// head (every batch) sit together in the order, longest heads first.  The
+// heads' windows differ by up to 16x, so the balance is that of
+// longest-first; but the backward's live working set becomes the q, G and dq
+// rows of about one head instead of every head: at cfg3 (B=8) the fused
+// backward's DRAM traffic fell from 2.43 GB to 0.84 GB per launch (ncu) at
+// the same duration.
+__device__ __forceinline__ int order_key(const AttnShape& s, int kind, int ntiles, long long id) {
+  return item_tiles(s, kind, ntiles, kind == 1 ? (id / ntiles) * ntiles : id);
+}
+
 __global__ void __launch_bounds__(1024) tile_order_kernel(AttnShape s, int kind, int ntiles,
                                                           long long N, int* perm) {
   __shared__ int cnt[kOrderBuckets];
@@ -401,7 +413,7 @@ __global__ void __launch_bounds__(1024) tile_order_kernel(AttnShape s, int kind,
   cnt[t] = 0;
   __syncthreads();
   for (long long id = t; id < N; id += blockDim.x)
-    atomicAdd(&cnt[kOrderBuckets - 1 - item_tiles(s, kind, ntiles, id)], 1);
+    atomicAdd(&cnt[kOrderBuckets - 1 - order_key(s, kind, ntiles, id)], 1);
   __syncthreads();
   // exclusive prefix sum over the buckets (bucket 0 = most tiles)
   const int v = cnt[t];
@@ -428,7 +440,7 @@ __global__ void __launch_bounds__(1024) tile_order_kernel(AttnShape s, int kind,
   cnt[t] = base + incl - v;
   __syncthreads();
   for (long long id = t; id < N; id += blockDim.x) {
-    const int pos = atomicAdd(&cnt[kOrderBuckets - 1 - item_tiles(s, kind, ntiles, id)], 1);
+    const int pos = atomicAdd(&cnt[kOrderBuckets - 1 - order_key(s, kind, ntiles, id)], 1);
     perm[pos] = (int)id;
   }
 }
