@@ -703,7 +703,8 @@ def main():
     ap.add_argument("--decode-splits", type=int, default=0,
                     help="override the cache's split count (0: its own heuristic)")
     ap.add_argument("--no-graph", action="store_true",
-                    help="lm workload: run the training step eagerly instead of as a CUDA graph")
+                    help="cfg3 / lm workloads: run the training step eagerly instead of as a "
+                         "CUDA graph")
     ap.add_argument("--profile-only", action="store_true",
                     help="warm-up steps + one step, nothing else (for ncu captures)")
     args = ap.parse_args()
@@ -813,16 +814,73 @@ def _sub(fn):
         return {"error": f"{type(e).__name__}: {e}"[:300]}
 
 
-class _SelfAttention(torch.nn.Module):
-    """attn(x, x, x) as a one-argument module, so that DDP's input handling
-    cannot break the query-is-key-is-value identity of self-attention."""
+class TrainStep:
+    """One cfg3 training step: module forward, backward and (N > 1) the
+    data-parallel gradient all-reduce (mean over the ranks).  The out_proj
+    weight gradient -- ready as soon as the backward starts -- is all-reduced
+    on a side stream from its post-accumulate hook, overlapping the screening
+    backward; the q/k/v/s_r/s_v gradients follow as one flat bucket.  With
+    `graph` the whole step is captured once as a CUDA graph and replayed (at
+    one sequence per GPU the eager step is bound by host-side launch work,
+    ~0.9 ms against ~0.35 ms of GPU work)."""
 
-    def __init__(self, attn):
-        super().__init__()
-        self.attn = attn
+    def __init__(self, attn, params, cot, dist, graph: bool, warmup: int):
+        self.attn, self.params, self.cot, self.dist = attn, params, cot, dist
+        self.rest = [p for p in params if p is not attn.out_proj.weight]
+        self.side = torch.cuda.Stream()
+        self.graph = None
+        if dist is not None:
+            # one hook per module; it reduces on the side stream of the step
+            # being run (or captured)
+            attn._grad_side = self.side
+            if not hasattr(attn, "_grad_hook"):
+                def hook(p):
+                    side = attn._grad_side
+                    side.wait_stream(torch.cuda.current_stream())
+                    with torch.cuda.stream(side):
+                        dist.all_reduce(p.grad, op=dist.ReduceOp.AVG)
+                attn._grad_hook = attn.out_proj.weight.register_post_accumulate_grad_hook(hook)
+        if graph:
+            self.x = torch.empty_like(cot)
+            self.x.copy_(cot)
+            cur = torch.cuda.current_stream()
+            ws = torch.cuda.Stream()
+            ws.wait_stream(cur)
+            with torch.cuda.stream(ws):
+                for _ in range(max(warmup, 3)):
+                    self._body(self.x)
+            cur.wait_stream(ws)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.y = self._body(self.x)
+            self.graph = g
 
-    def forward(self, x):
-        return self.attn(x, x, x)
+    def _body(self, inp):
+        if self.dist is not None:
+            self.attn._grad_side = self.side
+        for p in self.params:
+            p.grad = None
+        y = self.attn(inp, inp, inp)
+        y.backward(self.cot)
+        if self.dist is not None:
+            flat = torch.cat([p.grad.reshape(-1) for p in self.rest])
+            self.dist.all_reduce(flat, op=self.dist.ReduceOp.AVG)
+            off = 0
+            for p in self.rest:
+                n = p.grad.numel()
+                p.grad.copy_(flat[off:off + n].view_as(p.grad))
+                off += n
+            torch.cuda.current_stream().wait_stream(self.side)
+        return y
+
+    def __call__(self, inp):
+        if self.graph is None:
+            return self._body(inp)
+        if inp.data_ptr() != self.x.data_ptr():
+            self.x.copy_(inp, non_blocking=True)
+        self.graph.replay()
+        return self.y
 
 
 def run_cfg3(args, rank, world, local):
@@ -857,13 +915,6 @@ def run_cfg3(args, rank, world, local):
         attn.s_r.copy_(torch.log(r_h - 1.0))
         attn.s_v.copy_(torch.log(w_h - 1.0))
     attn = attn.to(dev).to(torch.bfloat16)
-    net = _SelfAttention(attn)
-    if dist is not None:
-        # gradient all-reduce in buckets, each launched from the autograd
-        # hooks as soon as its gradients are ready, on NCCL's stream: the
-        # out_proj bucket overlaps the screening backward
-        net = torch.nn.parallel.DistributedDataParallel(
-            net, device_ids=[local], bucket_cap_mb=2, gradient_as_bucket_view=True)
     params = [p for p in attn.parameters()]
 
     def make_inputs(batch, seed_rank):
@@ -873,13 +924,11 @@ def run_cfg3(args, rank, world, local):
         return xx, cc
 
     x, cot = make_inputs(B, rank)
+    use_graph = not args.no_graph
+    train = TrainStep(attn, params, cot, dist, use_graph, args.warmup)
 
-    def step(inp, cot_=None):
-        for p in params:
-            p.grad = None
-        y = net(inp)
-        y.backward(cot if cot_ is None else cot_)
-        return y
+    def step(inp, tr=None):
+        return (tr or train)(inp)
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     # clocks are sampled from the warm-up through the e2e loop (all GPU-bound);
@@ -895,7 +944,7 @@ def run_cfg3(args, rank, world, local):
         torch.cuda.synchronize()
         return
 
-    def timed(inp, cot_):
+    def timed(inp, tr=None):
         """K steps, L2 flushed between steps (outside the events); the job
         time is the max over ranks of the summed step times."""
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -906,7 +955,7 @@ def run_cfg3(args, rank, world, local):
         for s0, s1 in evs:
             flush.zero_()
             s0.record()
-            step(inp, cot_)
+            step(inp, tr)
             s1.record()
         torch.cuda.synchronize()
         if dist is not None:
@@ -918,7 +967,7 @@ def run_cfg3(args, rank, world, local):
             tot = float(t.item())
         return tot / args.steps
 
-    ms_per_step = timed(x, cot)
+    ms_per_step = timed(x)
     tokens_per_step = B * SEQ * world
     value = tokens_per_step / (ms_per_step / 1e3)
 
@@ -926,12 +975,13 @@ def run_cfg3(args, rank, world, local):
     if world > 1 and not args.no_sub:
         # weak scaling beside it: a full batch of 8 on every rank
         xw, cw = make_inputs(BATCH, rank)
+        tw = TrainStep(attn, params, cw, dist, use_graph, args.warmup)
         for _ in range(args.warmup):
-            step(xw, cw)
-        wms = timed(xw, cw)
+            step(xw, tw)
+        wms = timed(xw, tw)
         weak = {"per_gpu_batch": BATCH, "global_batch": BATCH * world, "ms_per_step": wms,
                 "value": BATCH * SEQ * world / (wms / 1e3), "unit": "tokens/s"}
-        del xw, cw
+        del xw, cw, tw
 
     # ---- per-kernel timing of the screening core (CUDA events, same stream)
     H, Dh = HEADS, HEAD_DIM
@@ -1078,8 +1128,11 @@ def run_cfg3(args, rank, world, local):
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "model": "ScreeningAttention(1024, 16)",
                        "global_batch": B * world, "per_gpu_batch": B, "seq_len": SEQ,
-                       "parallelism": f"dp{world} (batch sharding; DDP bucketed all-reduce "
-                                      f"overlapped with the backward)" if world > 1 else "dp1",
+                       "parallelism": (f"dp{world} (batch sharding; gradient all-reduce over "
+                                       f"NCCL, out_proj bucket overlapped with the backward)"
+                                       if world > 1 else "dp1"),
+                       "step": ("one CUDA graph per step (forward, backward, all-reduce)"
+                                if use_graph else "eager"),
                        "l2": "flushed (256 MiB write) between steps"},
             "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": pk_kind,
