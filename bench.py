@@ -130,6 +130,18 @@ class ClockSampler:
                 "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
 
 
+def finish_distributed(dist):
+    """End a multi-rank run: wait for the device and the other ranks, then
+    leave without tearing down the NCCL communicators -- a process group
+    destroyed while CUDA graphs that captured its collectives are alive can
+    block at exit."""
+    torch.cuda.synchronize()
+    dist.barrier()
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
+
+
 class NullClock:
     """Stand-in for ClockSampler inside sub-records (the outer line samples)."""
 
@@ -434,7 +446,7 @@ def run_prefill(args, rank, world):
             "gpu_launches": 6 * cfg["layers"] * args.steps,
         }), flush=True)
     if dist is not None:
-        dist.destroy_process_group()
+        finish_distributed(dist)
 
 
 def run_lm(args, rank, world, sub=False):
@@ -592,7 +604,7 @@ def run_lm(args, rank, world, sub=False):
             "clocks": clk.summary(),
         }), flush=True)
     if dist is not None:
-        dist.destroy_process_group()
+        finish_distributed(dist)
 
 
 def run_generate(args, rank, world, sub=False):
@@ -678,7 +690,7 @@ def run_generate(args, rank, world, sub=False):
             "clocks": clk.summary(),
         }), flush=True)
     if dist is not None:
-        dist.destroy_process_group()
+        finish_distributed(dist)
 
 
 def main():
@@ -1153,7 +1165,7 @@ def run_cfg3(args, rank, world, local):
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
-        dist.destroy_process_group()
+        finish_distributed(dist)
 
 
 if __name__ == "__main__":

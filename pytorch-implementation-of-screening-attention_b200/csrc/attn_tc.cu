@@ -546,23 +546,33 @@ __global__ void tc_prep_kernel(Rows q, Rows k, Rows v, int B, int Tq, int Tk, in
 
 // zero 1/|k| for the padding keys Tk..Tkp-1, then per 64-key tile the
 // (min, max) of 1/|k| for the forward's trim pre-test
+// per-64-key-tile (min, max) of 1/|k| (zero past Tk, and the padding zeroed):
+// one warp per tile, two keys per lane
 __global__ void tc_ik_meta_kernel(float* __restrict__ ikT, float4* __restrict__ meta, int BH,
                                   int Tk, int Tkp) {
   const int ntiles = Tkp / kBN;
-  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long idx = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (idx >= (long long)BH * ntiles) return;
   const long long bhh = idx / ntiles;
   const int tile = (int)(idx % ntiles);
   float* x = ikT + bhh * Tkp + (long long)tile * kBN;
   float mn = 3.0e38f, mx = 0.f;
-  for (int c = 0; c < kBN; ++c) {
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int c = lane + 32 * hh;
     const long long t = (long long)tile * kBN + c;
     float vv = 0.f;
     if (t < Tk) vv = x[c]; else x[c] = 0.f;
     mn = fminf(mn, vv);
     mx = fmaxf(mx, vv);
   }
-  meta[idx] = make_float4(mn, mx, 0.f, 0.f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if (lane == 0) meta[idx] = make_float4(mn, mx, 0.f, 0.f);
 }
 
 long long tk_pad(int Tk) { return ((long long)Tk + kBN - 1) / kBN * kBN; }
@@ -605,7 +615,7 @@ int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_giv
   }
   const long long mt = BH * (Tkp / kBN);
   if (mt > 0)
-    tc_ik_meta_kernel<<<(unsigned)((mt + 255) / 256), 256, 0, st>>>(ikT, meta, (int)BH, s.Tk,
+    tc_ik_meta_kernel<<<(unsigned)((mt * 32 + 255) / 256), 256, 0, st>>>(ikT, meta, (int)BH, s.Tk,
                                                                    (int)Tkp);
   if (s.Tq == 0) return SCREEN_OK;
   CUtensorMap tq, tk, tv;
