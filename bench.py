@@ -391,6 +391,22 @@ def run_prefill(args, rank, world):
         b.record()
     torch.cuda.synchronize()
     total_ms = sum(a.elapsed_time(b) for a, b in evs)
+    # one more step with CUDA events around each layer's sharded attention:
+    # interior rows (overlapping the halo exchange), the stream's stall for
+    # the halo (wait + assembly), boundary rows
+    overlap = None
+    if dist is not None:
+        with ms.shard_timeline() as tl:
+            step(ids)
+        torch.cuda.synchronize()
+        ov = ms.shard_timeline_summary(tl)
+        keys = ["interior_ms", "halo_stall_ms", "boundary_ms"]
+        t = torch.tensor([ov.get(k_, 0.0) for k_ in keys], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        overlap = {"per_layer_max_over_ranks": dict(zip(keys, (float(x_) for x_ in t.tolist()))),
+                   "layers": ov.get("calls", 0),
+                   "note": "CUDA events on each rank's stream; halo_stall = time the stream "
+                           "waited for the K/V halo after its interior rows were done"}
     # end to end: ids from pinned host memory, last logits back to the host
     logit_host = torch.empty(1, cfg["vocab"], dtype=torch.bfloat16).pin_memory()
     ids_dev = torch.empty_like(ids)
@@ -438,6 +454,7 @@ def run_prefill(args, rank, world):
                          "traffic": None, "per": "GPU (achieved = job FLOP/s / ranks)",
                          "flops_basis": "windowed attention pairs + dense block GEMMs"},
             "flops_per_step": fl,
+            "halo_overlap": overlap,
             "cpu_baseline": cpu,
             "e2e": {"value": T / (e2e_per / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": ids_local_host.numel() * 8,

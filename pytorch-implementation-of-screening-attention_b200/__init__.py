@@ -20,7 +20,7 @@ from .layers import MultiscreenBlock, MultiscreenDecoderLayer
 from .model import MultiscreenLM
 from .norm import TanhNorm
 from .sequence_parallel import (SequenceShard, current_shard, screening_attention_sharded,
-                                sequence_parallel)
+                                sequence_parallel, shard_timeline, shard_timeline_summary)
 from . import _lib
 
 _sys.modules.setdefault("screening_b200", _sys.modules[__name__])
@@ -36,6 +36,8 @@ __all__ = [
     "tanh_norm",
     "PagedKVCache",
     "sequence_parallel",
+    "shard_timeline",
+    "shard_timeline_summary",
     "screening_attention_sharded",
     "SequenceShard",
 ]

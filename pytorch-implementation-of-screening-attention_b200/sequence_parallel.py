@@ -72,6 +72,45 @@ def current_shard() -> SequenceShard | None:
     return _ACTIVE.get()
 
 
+_TIMELINE: contextvars.ContextVar = contextvars.ContextVar("screening_shard_timeline",
+                                                            default=None)
+
+
+@contextlib.contextmanager
+def shard_timeline():
+    """Record CUDA events around the three phases of every sharded attention
+    call made inside the context: [start, interior done, halo ready,
+    boundary done] per call.  Yields the list; read it after a synchronize
+    with shard_timeline_summary()."""
+    events: list = []
+    tok = _TIMELINE.set(events)
+    try:
+        yield events
+    finally:
+        _TIMELINE.reset(tok)
+
+
+def _mark(events, slot):
+    if events is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        slot.append(e)
+
+
+def shard_timeline_summary(events) -> dict:
+    """Mean per call (ms): interior attention, the stream's stall for the
+    halo once the interior rows are done (0 when the exchange is hidden),
+    boundary attention."""
+    rows = [c for c in events if len(c) == 4]
+    if not rows:
+        return {}
+    n = len(rows)
+    return {"calls": n,
+            "interior_ms": sum(c[0].elapsed_time(c[1]) for c in rows) / n,
+            "halo_stall_ms": sum(c[1].elapsed_time(c[2]) for c in rows) / n,
+            "boundary_ms": sum(c[2].elapsed_time(c[3]) for c in rows) / n}
+
+
 def halo_plan(rank: int, world: int, local_len: int, halo: int):
     """Rows exchanged for a halo of `halo` keys with equal blocks of `local_len`.
 
@@ -225,6 +264,11 @@ def screening_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tenso
     if L != shard.local_len or k.shape[1] != L:
         raise ValueError(f"local block length {L} != shard length {shard.local_len}")
     halo = window_halo(w)
+    tl = _TIMELINE.get()
+    marks: list = []
+    if tl is not None:
+        tl.append(marks)
+    _mark(tl, marks)
     pending = None
     if shard.world > 1 and halo > 0:
         pending = _HaloStart(shard, k.detach(), v.detach(), halo,
@@ -235,6 +279,7 @@ def screening_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tenso
     if nb < L:
         # interior rows, overlapped with the exchange
         parts.append((nb, attn(q[:, nb:], k, v, r, w, True, key_padding_mask, eps, nb)))
+    _mark(tl, marks)
     if nb > 0:
         mh = None
         if pending is not None:
@@ -247,6 +292,7 @@ def screening_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tenso
         else:
             kh = k.new_zeros(B, 0, H, D)
             vh = v.new_zeros(B, 0, H, D)
+        _mark(tl, marks)
         n = kh.shape[1]
         ke = torch.cat([kh.to(k.dtype), k[:, :nb]], dim=1)
         ve = torch.cat([vh.to(v.dtype), v[:, :nb]], dim=1)
@@ -256,6 +302,7 @@ def screening_attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tenso
             if n > 0:
                 kpm = torch.cat([mh if mh is not None else kpm.new_zeros(B, n), kpm], dim=1)
         parts.append((0, attn(q[:, :nb], ke, ve, r, w, True, kpm, eps, n)))
+        _mark(tl, marks)
     parts.sort(key=lambda p: p[0])
     ys = [p[1] for p in parts]
     return ys[0] if len(ys) == 1 else torch.cat(ys, dim=1)
