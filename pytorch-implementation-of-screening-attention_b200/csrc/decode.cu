@@ -89,6 +89,42 @@ __global__ void kv_append_kernel(screen_kv_append_args a) {
 // Decode split: CTA (split, b*H + h), 4 warps; LPK lanes read one 16-byte
 // slice each of a key row, KPW keys per warp step.
 // ---------------------------------------------------------------------------
+// End of a decode CTA: with several splits, store this split's partial sum
+// for decode_finish_kernel; with one split the CTA holds the whole
+// alpha-weighted sum and applies TanhNorm itself (no finishing launch).
+// red[k][d]: the per-warp sums.  Uniform over the CTA (it syncs).
+template <typename T, int D, int NW>
+__device__ __forceinline__ void store_split(const screen_decode_args& a, float* __restrict__ part,
+                                            float (&red)[NW][D], int bh, int split) {
+  const int tid = threadIdx.x;
+  if (a.num_splits > 1) {
+    for (int d = tid; d < D; d += blockDim.x) {
+      float s2 = 0.f;
+#pragma unroll
+      for (int k = 0; k < NW; ++k) s2 += red[k][d];
+      part[((long long)bh * a.num_splits + split) * D + d] = s2;
+    }
+    return;
+  }
+  for (int d = tid; d < D; d += blockDim.x) {
+    float s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) s2 += red[k][d];
+    red[0][d] = s2;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    float ss = 0.f;
+    for (int d = tid; d < D; d += 32) ss = fmaf(red[0][d], red[0][d], ss);
+    ss = warp_sum(ss);
+    const float nraw = sqrtf(ss);
+    const float g = tanhnorm_scale(nraw, a.eps);
+    for (int d = tid; d < D; d += 32)
+      reinterpret_cast<T*>(a.y)[(long long)bh * D + d] = from_f<T>(red[0][d] * g);
+    if (tid == 0 && a.no) a.no[bh] = nraw;
+  }
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_split_kernel(screen_decode_args a,
                                                            float* __restrict__ part) {
@@ -223,12 +259,7 @@ __global__ void __launch_bounds__(128) decode_split_kernel(screen_decode_args a,
     for (int e = 0; e < VEC; ++e) red[warp][sub * VEC + e] = acc[e];
   }
   __syncthreads();
-  for (int d = tid; d < D; d += 128) {
-    float s2 = 0.f;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) s2 += red[k][d];
-    part[((long long)bh * a.num_splits + split) * D + d] = s2;
-  }
+  store_split<T, D, NW>(a, part, red, bh, split);
 }
 
 // ---------------------------------------------------------------------------
@@ -487,12 +518,7 @@ __global__ void __launch_bounds__(32 * (kDecConsumers + 1)) decode_bulk_kernel(
     }
   }
   __syncthreads();
-  for (int d = tid; d < D; d += blockDim.x) {
-    float s2 = 0.f;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) s2 += red[k][d];
-    part[((long long)bh * a.num_splits + split) * D + d] = s2;
-  }
+  store_split<T, D, NW>(a, part, red, bh, split);
 }
 
 // Sum the splits, TanhNorm, store y (B,H,D) and |o|.  256 threads: 256/D
@@ -545,12 +571,9 @@ void launch_decode(const screen_decode_args& a, float* part, cudaStream_t s) {
   int sk = 1;
   while (sk < 32 && a.cache.page_size % (2 * sk) == 0) sk *= 2;
   const size_t stage_bytes = 2 * (size_t)sk * D * sizeof(T);
-  // shared-memory ring budget per CTA (KB); 64 KB leaves 3 CTAs per SM
-  static const int ring_kb = [] {
-    const char* e = getenv("SCREEN_DECODE_RING_KB");
-    const int v = e ? atoi(e) : 64;
-    return v < 16 ? 16 : (v > 200 ? 200 : v);
-  }();
+  // shared-memory ring budget per CTA: 64 KB leaves 3 CTAs per SM (32 and
+  // 48 KB rings measured slower at 32K and 100K keys)
+  constexpr int ring_kb = 64;
   int nstages = (int)(((size_t)ring_kb << 10) / stage_bytes);
   nstages = nstages / kDecConsumers * kDecConsumers;
   if (nstages > kDecMaxStages) nstages = kDecMaxStages;
@@ -564,7 +587,7 @@ void launch_decode(const screen_decode_args& a, float* part, cudaStream_t s) {
   } else {
     decode_split_kernel<T, D><<<grid, 128, 0, s>>>(a, part);
   }
-  decode_finish_kernel<T, D><<<a.B * a.H, 256, 0, s>>>(a, part);
+  if (a.num_splits > 1) decode_finish_kernel<T, D><<<a.B * a.H, 256, 0, s>>>(a, part);
 }
 
 }  // namespace

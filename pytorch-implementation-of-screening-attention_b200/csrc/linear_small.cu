@@ -23,12 +23,31 @@ __device__ __forceinline__ float gelu_erf(float v) {
   return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
 }
 
-template <int M>
+constexpr int kUnroll = 4;   // 16-byte weight chunks per lane in flight per row
+
+// R: output features per warp (rows of W); R > 1 amortises the CTA's input
+// staging over more weight rows for very wide layers (the lm_head)
+template <int M, int R>
 __global__ void __launch_bounds__(kWarps * 32) rows_linear_kernel(screen_rows_linear_args a) {
   extern __shared__ __align__(16) __nv_bfloat16 xs[];   // [M][K]
   __shared__ float red[M][kWarps];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = a.K;
+  const long long nb = ((long long)blockIdx.x * kWarps + warp) * R;
+  // the first weight chunks of this warp's rows are requested before the
+  // input staging, so their HBM latency overlaps it
+  uint4 wpre[R][kUnroll];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const bool rowok = nb + i < a.N;
+    const __nv_bfloat16* wr = reinterpret_cast<const __nv_bfloat16*>(a.W) + (nb + i) * (long long)K;
+#pragma unroll
+    for (int uu = 0; uu < kUnroll; ++uu) {
+      const int k = 8 * lane + 256 * uu;
+      wpre[i][uu] = rowok && k < K ? __ldg(reinterpret_cast<const uint4*>(wr + k))
+                                    : make_uint4(0, 0, 0, 0);
+    }
+  }
   const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(a.x);
   const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
   // ---- stage the input rows (RMSNorm'ed when norm_w is given)
@@ -88,67 +107,95 @@ __global__ void __launch_bounds__(kWarps * 32) rows_linear_kernel(screen_rows_li
     }
   }
   __syncthreads();
-  // ---- one weight row per warp
-  const long long n = (long long)blockIdx.x * kWarps + warp;
-  if (n >= a.N) return;
-  const __nv_bfloat16* wr = reinterpret_cast<const __nv_bfloat16*>(a.W) + n * (long long)K;
-  float acc[M];
+  // ---- R weight rows per warp
+  if (nb >= a.N) return;
+  float acc[R][M];
 #pragma unroll
-  for (int m = 0; m < M; ++m) acc[m] = 0.f;
-  constexpr int kUnroll = 4;
+  for (int i = 0; i < R; ++i)
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[i][m] = 0.f;
   for (int k0 = 8 * lane; k0 < K; k0 += 256 * kUnroll) {
-    uint4 wv[kUnroll];
+    uint4 wv[R][kUnroll];
+    if (k0 == 8 * lane) {
 #pragma unroll
-    for (int uu = 0; uu < kUnroll; ++uu) {
-      const int k = k0 + 256 * uu;
-      wv[uu] = k < K ? __ldg(reinterpret_cast<const uint4*>(wr + k)) : make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < R; ++i)
+#pragma unroll
+        for (int uu = 0; uu < kUnroll; ++uu) wv[i][uu] = wpre[i][uu];
+    } else {
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const bool rowok = nb + i < a.N;
+        const __nv_bfloat16* wr =
+            reinterpret_cast<const __nv_bfloat16*>(a.W) + (nb + i) * (long long)K;
+#pragma unroll
+        for (int uu = 0; uu < kUnroll; ++uu) {
+          const int k = k0 + 256 * uu;
+          wv[i][uu] = rowok && k < K ? __ldg(reinterpret_cast<const uint4*>(wr + k))
+                                     : make_uint4(0, 0, 0, 0);
+        }
+      }
     }
 #pragma unroll
     for (int uu = 0; uu < kUnroll; ++uu) {
       const int k = k0 + 256 * uu;
       if (k >= K) break;
-      const uint32_t w4[4] = {wv[uu].x, wv[uu].y, wv[uu].z, wv[uu].w};
 #pragma unroll
       for (int m = 0; m < M; ++m) {
         const uint4 xv = *reinterpret_cast<const uint4*>(xs + m * K + k);
         const uint32_t x4[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 wf = unpack_bf16(w4[e]), xf = unpack_bf16(x4[e]);
-          acc[m] = fmaf(wf.x, xf.x, fmaf(wf.y, xf.y, acc[m]));
+        for (int i = 0; i < R; ++i) {
+          const uint32_t w4[4] = {wv[i][uu].x, wv[i][uu].y, wv[i][uu].z, wv[i][uu].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 wf = unpack_bf16(w4[e]), xf = unpack_bf16(x4[e]);
+            acc[i][m] = fmaf(wf.x, xf.x, fmaf(wf.y, xf.y, acc[i][m]));
+          }
         }
       }
     }
   }
 #pragma unroll
-  for (int m = 0; m < M; ++m) acc[m] = warp_sum(acc[m]);
-  if (lane < M) {
-    float v = acc[0];
+  for (int i = 0; i < R; ++i) {
+    const long long n = nb + i;
 #pragma unroll
-    for (int m = 1; m < M; ++m)
-      if (lane == m) v = acc[m];
-    if (a.act == 1) v = __bfloat162float(__float2bfloat16_rn(v)), v = gelu_erf(v);
-    __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(a.y) + lane * a.y_stride + n;
-    if (a.res) {
-      // torch: bf16(linear) + bf16(res), rounded once more
-      v = __bfloat162float(__float2bfloat16_rn(v)) +
-          __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.res)[lane * a.res_stride + n]);
+    for (int m = 0; m < M; ++m) acc[i][m] = warp_sum(acc[i][m]);
+    if (n < a.N && lane < M) {
+      float v = acc[i][0];
+#pragma unroll
+      for (int m = 1; m < M; ++m)
+        if (lane == m) v = acc[i][m];
+      if (a.act == 1) v = __bfloat162float(__float2bfloat16_rn(v)), v = gelu_erf(v);
+      __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(a.y) + lane * a.y_stride + n;
+      if (a.res) {
+        // torch: bf16(linear) + bf16(res), rounded once more
+        v = __bfloat162float(__float2bfloat16_rn(v)) +
+            __bfloat162float(
+                reinterpret_cast<const __nv_bfloat16*>(a.res)[lane * a.res_stride + n]);
+      }
+      *yp = __float2bfloat16_rn(v);
     }
-    *yp = __float2bfloat16_rn(v);
   }
 }
 
-template <int M>
-int launch_rows_linear(const screen_rows_linear_args& a, cudaStream_t st) {
+template <int M, int R>
+int launch_rows_linear_r(const screen_rows_linear_args& a, cudaStream_t st) {
   const size_t smem = (size_t)M * a.K * 2;
   // one opt-in per device at the 200 KB maximum covers every K
   if (smem > 48 * 1024) {
-    const cudaError_t e = ensure_smem_optin((const void*)rows_linear_kernel<M>, 200 * 1024);
+    const cudaError_t e = ensure_smem_optin((const void*)rows_linear_kernel<M, R>, 200 * 1024);
     if (e != cudaSuccess) return record_cuda_error(e);
   }
-  const unsigned grid = (unsigned)((a.N + kWarps - 1) / kWarps);
-  rows_linear_kernel<M><<<grid, kWarps * 32, smem, st>>>(a);
+  const long long per_cta = (long long)kWarps * R;
+  const unsigned grid = (unsigned)((a.N + per_cta - 1) / per_cta);
+  rows_linear_kernel<M, R><<<grid, kWarps * 32, smem, st>>>(a);
   return check_launch();
+}
+
+// wide layers (the vocabulary projection) take 4 rows per warp
+template <int M>
+int launch_rows_linear(const screen_rows_linear_args& a, cudaStream_t st) {
+  return a.N >= 16384 ? launch_rows_linear_r<M, 4>(a, st) : launch_rows_linear_r<M, 1>(a, st);
 }
 
 }  // namespace

@@ -44,9 +44,15 @@ class PagedKVCache:
         # sqrt(pages) splits for long windows -- measured on B200 at 32K and
         # 100K keys per window, fewer splits leave a wave tail, more pay the
         # per-CTA pipeline fill; the split partials are summed
+        # short windows (<= 512 keys: the w <= 256 of a model at init) take
+        # one split per (b, h), which applies TanhNorm itself: a finishing
+        # launch costs more than the few pages it would spread
         pages = math.ceil(self.keep / page_size)
         fill = math.ceil(148 * 3 / max(1, batch * num_heads))
-        self.num_splits = max(1, min(256, pages, max(fill, round(1.1 * math.sqrt(pages)))))
+        if self.keep <= 512:
+            self.num_splits = 1
+        else:
+            self.num_splits = max(1, min(256, pages, max(fill, round(1.1 * math.sqrt(pages)))))
 
     def nbytes(self) -> int:
         return sum(p.numel() * p.element_size() for p in self.k_pages + self.v_pages)
