@@ -926,6 +926,7 @@ def run_cfg3(args, rank, world, local):
 
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.profile_only):
+        cpu_reference_sample()                   # warm-up (allocator, thread pool)
         dt, toks, nt = cpu_reference_sample()
         cpu = {"value": toks / dt, "unit": "tokens/s", "cores": nt, "kind": "port",
                "sample": f"windowed CPU restatement of multiscreen/attention.py (oracle) fwd+bwd, "
