@@ -16,8 +16,8 @@ reported beside it.
 Prints one JSON line (rank 0).  At one GPU the cfg3 line also carries
 sub-records measured in the same run: the decode kernel's HBM fraction at a
 100K-key window, attention-only fwd+bwd at T=32K and 128K, the cfg2 training
-step, the cfg5 decode step and the reference's own Triton kernels at cfg3
-shapes.  `--impl reference` times the reference algorithm's CPU
+step, the cfg4 prefill, the cfg5 decode step and the reference's own Triton
+kernels at cfg3 shapes.  `--impl reference` times the reference algorithm's CPU
 implementation (the windowed restatement of multiscreen/attention.py in the
 oracle, fp32, all host threads) on a bounded sample of the same workload
 (one of the 8 sequences, all 16 heads, per step).
@@ -326,7 +326,7 @@ def cpu_prefill_sample(T_sample: int = 4096):
     return dt, nt
 
 
-def run_prefill(args, rank, world):
+def run_prefill(args, rank, world, sub=False):
     """cfg4: long-context prefill of MultiscreenLM(50257, 1024, 16, 12) over
     T = --prefill-len tokens (batch 1, bf16, w = 2048 in every head, random
     init), sequence-sharded over the ranks (T / world tokens each, K/V halo of
@@ -348,7 +348,7 @@ def run_prefill(args, rank, world):
     Lb = T // world
     cfg = PREFILL
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or sub):
         dt, nt = cpu_prefill_sample()
         per_tok = dt / 4096 * cfg["layers"]
         cpu = {"value": 1.0 / per_tok, "unit": "tokens/s", "cores": nt, "kind": "port",
@@ -378,7 +378,7 @@ def run_prefill(args, rank, world):
         step(ids)
         torch.cuda.synchronize()
         return
-    clk = ClockSampler(local)
+    clk = NullClock() if sub else ClockSampler(local)
     clk.__enter__()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
@@ -434,6 +434,13 @@ def run_prefill(args, rank, world):
     pk, kind = peaks()
     peak = float(pk.get("bf16_tflops_sustained", pk["bf16_tflops"]))
     tf = fl["total"] / (ms_per / 1e3) / 1e12
+    if sub:
+        return {"workload": f"cfg4: MultiscreenLM(50257, 1024, 16, 12) prefill, batch 1, T={T}, "
+                            "w=2048, random init, no_grad, last-position logits, one GPU",
+                "ms_per_step": ms_per, "tokens_per_s": T / (ms_per / 1e3),
+                "e2e_tokens_per_s": T / (e2e_per / 1e3), "tflops": tf,
+                "frac_of_sustained_peak": tf / peak,
+                "flops_basis": "windowed attention pairs + dense block GEMMs"}
     if rank == 0:
         print(json.dumps({
             "metric": "long-context prefill tokens/s (MultiscreenLM 1024x16x12, T=131072, w=2048)",
@@ -1145,6 +1152,10 @@ def run_cfg3(args, rank, world, local):
         sa = _ap.Namespace(**vars(args))
         sa.steps, sa.warmup, sa.no_graph = 10, 3, False
         sub["cfg2_lm_step"] = _sub(lambda: run_lm(sa, 0, 1, sub=True))
+        torch.cuda.empty_cache()
+        sp = _ap.Namespace(**vars(args))
+        sp.steps, sp.warmup, sp.prefill_len = 3, 3, 131072
+        sub["cfg4_prefill"] = _sub(lambda: run_prefill(sp, 0, 1, sub=True))
         torch.cuda.empty_cache()
         sg = _ap.Namespace(**vars(args))
         sg.steps, sg.warmup, sg.prompt_len = 1, 1, 100_000
