@@ -219,7 +219,11 @@ SCREEN_API size_t screen_decode_workspace_size(const screen_decode_args* a);
 
 /* One causal query per (b,h) at position seq_lens[b]-1 against the cached
  * keys inside its window.  Equals the last row of screen_fwd over the whole
- * prefix (the logits row generate() keeps at multiscreen/model.py:133). */
+ * prefix (the logits row generate() keeps at multiscreen/model.py:133).
+ * With num_splits > 1 each (b,h) window is cut into that many runs of pages
+ * whose partial sums go through the workspace and a finishing pass; with
+ * num_splits == 1 one CTA per (b,h) applies TanhNorm itself (the workspace is
+ * then not read). */
 SCREEN_API int screen_decode(const screen_decode_args* a, screen_stream_t stream);
 
 /* Bytes of the static device scratch array used by screen_decode_noalloc. */
