@@ -58,6 +58,7 @@ Family family_choice() {
   return f;
 }
 bool use_tc_fwd(int dtype, int D) { return family_choice() == FAM_TC && tc_supported(dtype, D); }
+bool use_tc_bwd(int dtype, int D) { return family_choice() == FAM_TC && tc_bwd_supported(dtype, D); }
 bool use_mma(int dtype, int D) { return family_choice() != FAM_SIMT && mma_supported(dtype, D); }
 // the warp-level mma.sync kernels have no dropout; with dropout the SIMT family serves
 bool use_mma_drop(int dtype, int D, uint32_t drop_thr) { return drop_thr == 0 && use_mma(dtype, D); }
@@ -91,7 +92,7 @@ BwdLayout bwd_layout(const screen_bwd_args* a) {
   AttnShape s = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
                            a->key_padding_mask, a->kpm_sb, a->dropout_threshold,
                            a->dropout_seed);
-  const bool tc = use_tc_fwd(a->dtype, a->D);
+  const bool tc = use_tc_bwd(a->dtype, a->D);
   L.P = tc ? tc_bwd_partials(s)
            : (use_mma_drop(a->dtype, a->D, a->dropout_threshold) ? mma_bwd_partials(a->D, s) : simt_bwd_partials(s));
   L.g_off = 0;
@@ -175,10 +176,10 @@ int screen_fwd(const screen_fwd_args* a, screen_stream_t stream) {
   FwdPtrs p{Rows{a->q, a->q_sb, a->q_st}, Rows{a->k, a->k_sb, a->k_st},
             Rows{a->v, a->v_sb, a->v_st}, a->nq, a->nk, a->nv, a->y, a->no, a->tile_stats};
   if (tc) {
-    const size_t need = tc_fwd_workspace(sh);
+    const size_t need = tc_fwd_workspace(sh, a->D);
     if (need > 0 && (!a->workspace || a->workspace_bytes < need || !al16(a->workspace)))
       return SCREEN_ERR_WORKSPACE;
-    if ((st = tc_fwd(sh, p, a->workspace, a->norms_given || !(stages & 1), s))) return st;
+    if ((st = tc_fwd(sh, p, a->workspace, a->norms_given || !(stages & 1), a->D, s))) return st;
   } else if (use_mma_drop(a->dtype, a->D, a->dropout_threshold))
     mma_fwd(a->D, sh, p, s);
   else
@@ -199,7 +200,7 @@ size_t screen_fwd_workspace_size(const screen_fwd_args* a) {
   AttnShape sh = make_shape(a->B, a->H, a->Tq, a->Tk, a->causal, a->q_offset, a->eps, a->r, a->w,
                             a->key_padding_mask, a->kpm_sb, a->dropout_threshold,
                            a->dropout_seed);
-  return round_up(tc_fwd_workspace(sh));
+  return round_up(tc_fwd_workspace(sh, a->D));
 }
 
 int screen_device_status(int clear) {
@@ -239,7 +240,7 @@ int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
   if (nq && (stages & 1))
     tanhnorm_grad_from_y(a->dtype, a->D, a->y, a->no, a->dy, a->dy_sb, a->dy_st, G,
                          // G as bf16 hi/lo planes for the tensor-core families
-                         use_tc_fwd(a->dtype, a->D) ||
+                         use_tc_bwd(a->dtype, a->D) ||
                              use_mma_drop(a->dtype, a->D, a->dropout_threshold),
                          a->B, a->Tq, a->H, a->eps, s);
   if ((st = check_launch())) return st;
@@ -250,7 +251,7 @@ int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
             Rows{a->v, a->v_sb, a->v_st}, a->nq, a->nk, a->nv, G,
             OutRows{a->dq, a->dq_sb, a->dq_st}, OutRows{a->dk, a->dk_sb, a->dk_st},
             OutRows{a->dv, a->dv_sb, a->dv_st}, pr, pw};
-  if (use_tc_fwd(a->dtype, a->D)) {
+  if (use_tc_bwd(a->dtype, a->D)) {
     if ((st = tc_bwd(sh, p, ws + L.aux_off, stages, s))) return st;
   } else if (use_mma_drop(a->dtype, a->D, a->dropout_threshold))
     mma_bwd(a->D, sh, p, stages, s);

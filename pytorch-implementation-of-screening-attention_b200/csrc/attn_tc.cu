@@ -39,48 +39,68 @@ typedef __nv_bfloat16 bf16;
 
 // kCG compute warpgroups split each key tile's 64 columns (32 / kCG each)
 constexpr int kCG = 2;
-constexpr int kD = 64, kBM = 128, kBN = 64, kNS = 5;
-// S / P ring in TMEM: P (bf16) is written over the S (fp32) columns it came
-// from, so three 64-column buffers + O fit the 256 columns of a CTA
-constexpr int kSB = 3;
+constexpr int kBM = 128, kBN = 64;
 constexpr int kCW = 4 * kCG;                 // compute warps
 constexpr int kNC = kBN / kCG;               // columns per compute thread per tile
 constexpr int kCT = 32 * kCW;                // compute threads
 constexpr int kProdWarp = kCW, kMmaWarp = kCW + 1;
 constexpr int kThreads = 32 * (kCW + 2);
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
+constexpr uint32_t TM_S = 0, TM_COLS = 256;
 
-// shared-memory layout (offsets from a 1024-byte aligned base)
-constexpr uint32_t OFF_Q = 0;
-constexpr uint32_t OFF_K = OFF_Q + kBM * kD * 2;
-constexpr uint32_t OFF_V = OFF_K + kNS * kBN * kD * 2;
-constexpr uint32_t OFF_COL = OFF_V + kNS * kBN * kD * 2;  // per stage ik|cos|sin [64] + meta
-constexpr uint32_t COL_BYTES = 3 * kBN * 4 + 16;           // meta = (ik min, ik max, -, -)
-constexpr uint32_t OFF_TAB = OFF_COL + kNS * COL_BYTES;    // (cos, sin)(pi c / w), c < 64
-constexpr uint32_t OFF_BAR = OFF_TAB + 2 * kBN * 4;
-constexpr int BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = BAR_KV_FULL + kNS,
-              BAR_S_FULL = BAR_KV_EMPTY + kNS, BAR_P_FULL = BAR_S_FULL + kSB,
-              BAR_O_FULL = BAR_P_FULL + kSB, BAR_COUNT = BAR_O_FULL + 1;
-constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 24;
-static_assert(BAR_COUNT <= 24, "barrier space");
-constexpr uint32_t OFF_RED = OFF_MISC + 64;                // [kCG][kBM] epilogue sums
-constexpr uint32_t SMEM_USED = OFF_RED + kCG * kBM * 4;
-// at least 80 KB per CTA: at most two CTAs (2 x 256 TMEM columns) per SM
-constexpr uint32_t kSmemBytes = (SMEM_USED + 1024 > 80 * 1024) ? SMEM_USED + 1024 : 80 * 1024;
-
-constexpr uint32_t TM_S = 0, TM_O = kSB * kBN, TM_COLS = 256;
-static_assert(TM_O + kD <= TM_COLS, "TMEM budget");
+// Per head dim D (64 or 128).  Operand tiles are stored as D / 64 column
+// halves of 64 elements (128-byte rows, SW128), each half a separate TMA box
+// and a separate run of K-steps for the MMA.
+//   kNS: K / V^ ring stages; kSB: S / P buffers in TMEM (P, bf16, is written
+//   over the S columns it came from), then O: kSB * 64 + D <= 256 columns,
+//   so two CTAs share an SM at either D.
+template <int D>
+struct FwdCfg {
+  static constexpr int kD = D, kHalves = D / 64;
+  static constexpr int kNS = D == 64 ? 5 : 2;
+  static constexpr int kSB = D == 64 ? 3 : 2;
+  static constexpr uint32_t TILE_Q = kBM * D * 2, TILE_KV = kBN * D * 2;
+  static constexpr uint32_t HALF_Q = kBM * 128, HALF_KV = kBN * 128;   // one 64-column half
+  // shared-memory layout (offsets from a 1024-byte aligned base)
+  static constexpr uint32_t OFF_Q = 0;
+  static constexpr uint32_t OFF_K = OFF_Q + TILE_Q;
+  static constexpr uint32_t OFF_V = OFF_K + kNS * TILE_KV;
+  static constexpr uint32_t OFF_COL = OFF_V + kNS * TILE_KV;  // per stage ik|cos|sin [64] + meta
+  static constexpr uint32_t COL_BYTES = 3 * kBN * 4 + 16;      // meta = (ik min, ik max, -, -)
+  static constexpr uint32_t OFF_TAB = OFF_COL + kNS * COL_BYTES;  // (cos, sin)(pi c / w), c < 64
+  static constexpr uint32_t OFF_BAR = OFF_TAB + 2 * kBN * 4;
+  static constexpr int BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = BAR_KV_FULL + kNS,
+                       BAR_S_FULL = BAR_KV_EMPTY + kNS, BAR_P_FULL = BAR_S_FULL + kSB,
+                       BAR_O_FULL = BAR_P_FULL + kSB, BAR_COUNT = BAR_O_FULL + 1;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 24;
+  static constexpr uint32_t OFF_RED = OFF_MISC + 64;           // [kCG][kBM] epilogue sums
+  static constexpr uint32_t SMEM_USED = OFF_RED + kCG * kBM * 4;
+  // at least 80 KB per CTA: at most two CTAs (2 x 256 TMEM columns) per SM
+  static constexpr uint32_t kSmemBytes =
+      (SMEM_USED + 1024 > 80 * 1024) ? SMEM_USED + 1024 : 80 * 1024;
+  static constexpr uint32_t TM_O = kSB * kBN;
+  static_assert(BAR_COUNT <= 24, "barrier space");
+  static_assert(TM_O + D <= TM_COLS, "TMEM budget");
+  static_assert(2 * kSmemBytes <= 228 * 1024, "two CTAs per SM");
+};
 
 __device__ int g_device_status = 0;
 
 
 // kDrop: attention dropout on alpha (counter-based bits, AttnShape::drop_thr)
-template <bool kDrop>
+template <bool kDrop, int D>
 __global__ void __launch_bounds__(kThreads, 2)
     tc_fwd_kernel(AttnShape s, FwdPtrs p, const float* __restrict__ ikT,
                   const float4* __restrict__ ikmeta, int Tkp, const int* __restrict__ order,
                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV) {
+  using C = FwdCfg<D>;
+  constexpr int kD = D, kNS = C::kNS, kSB = C::kSB, kHalves = C::kHalves;
+  constexpr uint32_t OFF_Q = C::OFF_Q, OFF_K = C::OFF_K, OFF_V = C::OFF_V, OFF_COL = C::OFF_COL,
+                     COL_BYTES = C::COL_BYTES, OFF_TAB = C::OFF_TAB, OFF_BAR = C::OFF_BAR,
+                     OFF_MISC = C::OFF_MISC, OFF_RED = C::OFF_RED, TM_O = C::TM_O;
+  constexpr int BAR_Q = C::BAR_Q, BAR_KV_FULL = C::BAR_KV_FULL, BAR_KV_EMPTY = C::BAR_KV_EMPTY,
+                BAR_S_FULL = C::BAR_S_FULL, BAR_P_FULL = C::BAR_P_FULL, BAR_O_FULL = C::BAR_O_FULL;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -141,7 +161,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     // of the tile from one sincospif and a rotation of the per-CTA table
     if (lane == 0) {
       mbar_arrive_expect_tx(bar(BAR_Q), kBM * kD * 2);
-      tma_load_4d(sQ, &tmQ, 0, h, (int)i0, b, bar(BAR_Q));
+#pragma unroll
+      for (int hf = 0; hf < kHalves; ++hf)
+        tma_load_4d(sQ + hf * C::HALF_Q, &tmQ, 64 * hf, h, (int)i0, b, bar(BAR_Q));
     }
     // (cos, sin)(pi c / w) for the 64 column offsets of a tile
 #pragma unroll
@@ -175,8 +197,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane == 0) {
         const uint32_t fb = bar(BAR_KV_FULL + st);
         mbar_arrive_expect_tx(fb, 2 * kBN * kD * 2 + kBN * 4 + 16);
-        tma_load_4d(kb, &tmK, 0, h, (int)j0, b, fb);
-        tma_load_4d(vb, &tmV, 0, h, (int)j0, b, fb);
+#pragma unroll
+        for (int hf = 0; hf < kHalves; ++hf) {
+          tma_load_4d(kb + hf * C::HALF_KV, &tmK, 64 * hf, h, (int)j0, b, fb);
+          tma_load_4d(vb + hf * C::HALF_KV, &tmV, 64 * hf, h, (int)j0, b, fb);
+        }
         bulk_g2s(colb, ikh + j0, kBN * 4, fb);
         bulk_g2s(colb + 3 * kBN * 4, mh + kt, 16, fb);
       }
@@ -218,10 +243,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tc_fence_after();
         const uint32_t kb = sK + st * kBN * kD * 2;
+        // K-steps of 16: four per 64-column half of Q and K
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TM_S + kBN * bb, desc_sw128(sQ + kk * 32, 16, 1024),
-                 desc_sw128(kb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + TM_S + kBN * bb,
+                 desc_sw128(sQ + (kk >> 2) * C::HALF_Q + (kk & 3) * 32, 16, 1024),
+                 desc_sw128(kb + (kk >> 2) * C::HALF_KV + (kk & 3) * 32, 16, 1024), idS,
+                 kk > 0 ? 1u : 0u);
         mma_commit(bar(BAR_S_FULL + bb));
         return true;
       };
@@ -240,8 +268,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
             const uint32_t pcol = kCG == 2 ? (kk >> 1) * 32 + (kk & 1) * 8 : 8 * kk;
+            // V^ MN-major: D / 64 chunks of 64 output columns, C::HALF_KV apart
             mma_ts(tmem + TM_O, tmem + TM_S + kBN * bb + pcol,
-                   desc_sw128(vb + kk * 16 * 128, kBN * kD * 2, 1024), idPV,
+                   desc_sw128(vb + kk * 16 * 128, C::HALF_KV, 1024), idPV,
                    (o_started || kk > 0) ? 1u : 0u);
           }
           o_started = true;
@@ -458,25 +487,28 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (tid == 0 && *abort_flag) atomicExch(&g_device_status, (int)SCREEN_ERR_TIMEOUT);
 }
 
-// One pass over q, k, v (bf16, D = 64; 8 lanes x 16 B per row): the clamped
+// One pass over q, k, v (bf16, D / 8 lanes x 16 B per row): the clamped
 // row norms (written unless the caller gave them), the unit rows
 // V^ = v / |v| (zero for padded keys) that the forward multiplies by alpha,
 // and 1/|k| transposed to [B][H][Tk padded to 64] so a key tile's factors are
 // one contiguous 256-byte run.
+template <int kD>
 __global__ void tc_prep_kernel(Rows q, Rows k, Rows v, int B, int Tq, int Tk, int H, float eps,
                                int norms_given, const uint8_t* kpm, long long kpm_sb,
                                float* __restrict__ nq, float* __restrict__ nk,
                                float* __restrict__ nv, bf16* __restrict__ vhat,
                                float* __restrict__ ikT, int Tkp) {
-  const int sub = threadIdx.x & 7;
+  constexpr int LPR = kD / 8;          // lanes per row (16 bytes each)
+  constexpr int RPS = 256 / LPR;       // rows per block step
+  const int sub = threadIdx.x % LPR;
   const long long rows_q = norms_given ? 0 : (long long)B * Tq * H;
   const long long rows_k = (long long)B * Tk * H;
   const long long total = rows_q + rows_k;
-  // every lane of a warp runs the same number of iterations (32 rows per
-  // block step), so the 8-lane shuffles below always see full groups
-  for (long long base_row = (long long)blockIdx.x * 32; base_row < total;
-       base_row += (long long)gridDim.x * 32) {
-    const long long row = base_row + (threadIdx.x >> 3);
+  // every lane of a warp runs the same number of iterations (RPS rows per
+  // block step), so the LPR-lane shuffles below always see full groups
+  for (long long base_row = (long long)blockIdx.x * RPS; base_row < total;
+       base_row += (long long)gridDim.x * RPS) {
+    const long long row = base_row + (threadIdx.x / LPR);
     const bool valid = row < total;
     const bool isq = row < rows_q;
     const long long rr = !valid ? 0 : (isq ? row : row - rows_q);
@@ -514,7 +546,7 @@ __global__ void tc_prep_kernel(Rows q, Rows k, Rows v, int B, int Tq, int Tk, in
       sc = fmaf(fc.x, fc.x, fmaf(fc.y, fc.y, sc));
     }
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
+    for (int o = 1; o < LPR; o <<= 1) {
       sa += __shfl_xor_sync(0xffffffffu, sa, o);
       sc += __shfl_xor_sync(0xffffffffu, sc, o);
     }
@@ -544,8 +576,6 @@ __global__ void tc_prep_kernel(Rows q, Rows k, Rows v, int B, int Tq, int Tk, in
   }
 }
 
-// zero 1/|k| for the padding keys Tk..Tkp-1, then per 64-key tile the
-// (min, max) of 1/|k| for the forward's trim pre-test
 // per-64-key-tile (min, max) of 1/|k| (zero past Tk, and the padding zeroed):
 // one warp per tile, two keys per lane
 __global__ void tc_ik_meta_kernel(float* __restrict__ ikT, float4* __restrict__ meta, int BH,
@@ -580,35 +610,39 @@ size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace
 
-bool tc_supported(int dtype, int D) { return dtype == SCREEN_BF16 && D == kD; }
+bool tc_supported(int dtype, int D) { return dtype == SCREEN_BF16 && (D == 64 || D == 128); }
 
-size_t tc_fwd_workspace(const AttnShape& s) {
+size_t tc_fwd_workspace(const AttnShape& s, int D) {
   const long long BH = (long long)s.B * s.H, Tkp = tk_pad(s.Tk);
-  return al256((size_t)s.B * s.Tk * s.H * kD * 2) + al256((size_t)BH * Tkp * 4) +
+  return al256((size_t)s.B * s.Tk * s.H * D * 2) + al256((size_t)BH * Tkp * 4) +
          al256((size_t)BH * (Tkp / kBN) * 16) + al256((size_t)BH * ((s.Tq + kBM - 1) / kBM) * 4);
 }
 
-int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
-           cudaStream_t st) {
-  if (s.B == 0 || s.H == 0) return SCREEN_OK;
+namespace {
+template <int D>
+int tc_fwd_d(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
+             cudaStream_t st) {
+  using C = FwdCfg<D>;
   {
-    cudaError_t e = ensure_smem_optin((const void*)tc_fwd_kernel<false>, (int)kSmemBytes);
-    if (e == cudaSuccess) e = ensure_smem_optin((const void*)tc_fwd_kernel<true>, (int)kSmemBytes);
+    cudaError_t e = ensure_smem_optin((const void*)tc_fwd_kernel<false, D>, (int)C::kSmemBytes);
+    if (e == cudaSuccess)
+      e = ensure_smem_optin((const void*)tc_fwd_kernel<true, D>, (int)C::kSmemBytes);
     if (e != cudaSuccess) return record_cuda_error(e);
   }
   const long long BH = (long long)s.B * s.H, Tkp = tk_pad(s.Tk);
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   bf16* vhat = reinterpret_cast<bf16*>(ws);
-  float* ikT = reinterpret_cast<float*>(ws + al256((size_t)s.B * s.Tk * s.H * kD * 2));
+  float* ikT = reinterpret_cast<float*>(ws + al256((size_t)s.B * s.Tk * s.H * D * 2));
   float4* meta = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(ikT) +
                                            al256((size_t)BH * Tkp * 4));
   int* order = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(meta) +
                                       al256((size_t)BH * (Tkp / kBN) * 16));
   const long long rows = (long long)s.B * ((norms_given ? 0 : s.Tq) + s.Tk) * s.H;
   if (rows > 0) {
-    long long blocks = (rows + 31) / 32;
+    constexpr int RPS = 256 / (D / 8);
+    long long blocks = (rows + RPS - 1) / RPS;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    tc_prep_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+    tc_prep_kernel<D><<<(unsigned)blocks, 256, 0, st>>>(
         p.q, p.k, p.v, s.B, s.Tq, s.Tk, s.H, s.eps, norms_given ? 1 : 0, s.kpm, s.kpm_sb,
         const_cast<float*>(p.nq), const_cast<float*>(p.nk), const_cast<float*>(p.nv), vhat, ikT,
         (int)Tkp);
@@ -619,20 +653,28 @@ int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_giv
                                                                    (int)Tkp);
   if (s.Tq == 0) return SCREEN_OK;
   CUtensorMap tq, tk, tv;
-  if (!make_tmap_bthd(&tq, p.q.p, s.B, s.Tq, s.H, p.q.sb, p.q.st, kBM) ||
-      !make_tmap_bthd(&tk, p.k.p, s.B, s.Tk, s.H, p.k.sb, p.k.st, kBN) ||
-      !make_tmap_bthd(&tv, vhat, s.B, s.Tk, s.H, (long long)s.Tk * s.H * kD,
-                      (long long)s.H * kD, kBN))
+  if (!make_tmap_bthd(&tq, p.q.p, s.B, s.Tq, s.H, p.q.sb, p.q.st, kBM, D) ||
+      !make_tmap_bthd(&tk, p.k.p, s.B, s.Tk, s.H, p.k.sb, p.k.st, kBN, D) ||
+      !make_tmap_bthd(&tv, vhat, s.B, s.Tk, s.H, (long long)s.Tk * s.H * D, (long long)s.H * D,
+                      kBN, D))
     return SCREEN_ERR_CUDA;
   const int nqt = (s.Tq + kBM - 1) / kBM;
   tile_order(s, 0, nqt, order, st);
   if (s.drop_thr)
-    tc_fwd_kernel<true><<<(unsigned)(BH * nqt), kThreads, kSmemBytes, st>>>(
+    tc_fwd_kernel<true, D><<<(unsigned)(BH * nqt), kThreads, C::kSmemBytes, st>>>(
         s, p, ikT, meta, (int)Tkp, order, tq, tk, tv);
   else
-    tc_fwd_kernel<false><<<(unsigned)(BH * nqt), kThreads, kSmemBytes, st>>>(
+    tc_fwd_kernel<false, D><<<(unsigned)(BH * nqt), kThreads, C::kSmemBytes, st>>>(
         s, p, ikT, meta, (int)Tkp, order, tq, tk, tv);
   return SCREEN_OK;
+}
+}  // namespace
+
+int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given, int D,
+           cudaStream_t st) {
+  if (s.B == 0 || s.H == 0) return SCREEN_OK;
+  return D == 128 ? tc_fwd_d<128>(s, p, workspace, norms_given, st)
+                  : tc_fwd_d<64>(s, p, workspace, norms_given, st);
 }
 
 

@@ -1128,6 +1128,8 @@ __global__ void __launch_bounds__(256) tc_bwd_dq_finalize_kernel(
                             4 * l) = o;
 }
 
+bool tc_bwd_supported(int dtype, int D) { return dtype == SCREEN_BF16 && D == kD; }
+
 size_t tc_bwd_aux_bytes(const AttnShape& s) {
   const long long BH = (long long)s.B * s.H, Tqp = padT(s.Tq), Tkp = padT(s.Tk);
   return al256(BH * Tqp * 4) + 2 * al256(BH * Tkp * 4) + al256(BH * (Tqp / kBN) * 16) +

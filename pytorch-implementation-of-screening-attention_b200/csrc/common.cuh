@@ -393,16 +393,17 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn_major, 
 }  // namespace screen
 
 // ---------------------------------------------------------------------------
-// Host: TMA descriptor of a bf16 (B, T, H, 64) tensor with element strides
-// sb (batch) and st (time), unit stride over d and 64 over h.  The box is
-// 64 d x 1 head x `rows` times x 1 batch, 128-byte swizzled: in shared memory
+// Host: TMA descriptor of a bf16 (B, T, H, D) tensor with element strides
+// sb (batch) and st (time), unit stride over d and D over h.  The box is
+// 64 d x 1 head x `rows` times x 1 batch (for D = 128 one box per 64-column
+// half, selected by the d coordinate), 128-byte swizzled: in shared memory
 // it lands as `rows` rows of 128 B, 16-byte chunks XOR-swizzled by row % 8,
 // the canonical K-major SW128 layout of the tcgen05 smem descriptors.  Rows
 // at t >= T read as zeros.  The encoder comes from the driver at run time.
 // ---------------------------------------------------------------------------
 namespace screen {
 inline bool make_tmap_bthd(CUtensorMap* map, const void* base, long long B, long long T, int H,
-                           long long sb, long long st, int rows) {
+                           long long sb, long long st, int rows, int D = 64) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -413,9 +414,9 @@ inline bool make_tmap_bthd(CUtensorMap* map, const void* base, long long B, long
     return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }();
   if (!encode) return false;
-  const cuuint64_t dims[4] = {64, (cuuint64_t)H, (cuuint64_t)(T > 0 ? T : 1),
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)(T > 0 ? T : 1),
                               (cuuint64_t)(B > 0 ? B : 1)};
-  const cuuint64_t strides[3] = {64 * 2, (cuuint64_t)st * 2, (cuuint64_t)sb * 2};
+  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)st * 2, (cuuint64_t)sb * 2};
   const cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,

@@ -93,13 +93,15 @@ long long simt_bwd_partials(const AttnShape& s);
 void simt_bwd(int dtype, int D, const AttnShape& s, const BwdPtrs& p, int stages,
               cudaStream_t st);
 
-// tcgen05 / TMEM forward (bf16, D = 64).
+// tcgen05 / TMEM forward (bf16, D = 64 or 128).
 bool tc_supported(int dtype, int D);
-size_t tc_fwd_workspace(const AttnShape& s);
-int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given,
-            cudaStream_t st);
+size_t tc_fwd_workspace(const AttnShape& s, int D);
+int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given, int D,
+           cudaStream_t st);
 int tc_device_status(bool clear);
-// tcgen05 / TMEM backward (bf16, D = 64); aux_ws holds tc_bwd_aux_bytes()
+// tcgen05 / TMEM backward (bf16, D = 64: tc_bwd_supported); aux_ws holds
+// tc_bwd_aux_bytes()
+bool tc_bwd_supported(int dtype, int D);
 size_t tc_bwd_aux_bytes(const AttnShape& s);
 long long tc_bwd_partials(const AttnShape& s);
 // Longest-first launch order of the tcgen05 kernels' CTAs: perm[i] is the

@@ -102,6 +102,10 @@ CASES = [
     (1, 520, 520, 2, 128, True, 0, [50.0, 500.0], [1.2, 1.05], False, 0.4),
     (1, 333, 333, 2, 32, True, 0, [50.0, 500.0], [1.2, 1.05], True, 0.4),
     (1, 200, 200, 2, 16, False, 0, [20.0, 150.0], [1.2, 1.05], False, 0.4),
+    # head dim 128: tensor-core forward (two 64-column operand halves), SIMT backward
+    (2, 200, 333, 2, 128, False, 0, [40.0, 300.0], [1.1, 1.3], True, 0.0),
+    (1, 150, 700, 2, 128, True, 550, [64.0, 700.0], [1.2, 1.05], False, 0.0),
+    (1, 1100, 1100, 3, 128, True, 0, [9.5, 333.0, 1100.0], [1.5, 1.02, 1.3], True, 0.4),
 ]
 
 
@@ -248,3 +252,17 @@ def test_empty_and_masked_everything(ms):
     kv = torch.randn(1, 0, H, D, device=dev)
     y = ms.screening_attention(q, kv, kv, r, w, False)
     assert y.shape == (1, 5, H, D) and torch.count_nonzero(y) == 0
+
+
+def test_head_dim_128_forward_runs_on_tensor_cores(ms):
+    """bf16 D = 128 takes the tcgen05 forward (it reports tile statistics,
+    which only the tensor-core kernel counts)."""
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(7)
+    q, k, v = (torch.randn(1, 300, 2, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    r = torch.tensor([1.2, 1.5], device=dev)
+    w = torch.tensor([50.0, 200.0], device=dev)
+    stats = torch.zeros(2, dtype=torch.int64, device=dev)
+    ms._lib.screen_fwd(q, k, v, r, w, True, tile_stats=stats)
+    torch.cuda.synchronize()
+    assert int(stats[0]) > 0
