@@ -252,7 +252,7 @@ int screen_bwd(const screen_bwd_args* a, screen_stream_t stream) {
             OutRows{a->dq, a->dq_sb, a->dq_st}, OutRows{a->dk, a->dk_sb, a->dk_st},
             OutRows{a->dv, a->dv_sb, a->dv_st}, pr, pw};
   if (use_tc_bwd(a->dtype, a->D)) {
-    if ((st = tc_bwd(sh, p, ws + L.aux_off, stages, s))) return st;
+    if ((st = tc_bwd(sh, p, ws + L.aux_off, stages, a->D, s))) return st;
   } else if (use_mma_drop(a->dtype, a->D, a->dropout_threshold))
     mma_bwd(a->D, sh, p, stages, s);
   else

@@ -87,12 +87,13 @@ __device__ __forceinline__ void store_unit_jacobian(const float (&acc)[64], cons
 // time (scaled by `scale`), in two passes (x . acc, then the output), so at
 // most 32 accumulators and 8 raw values are live.  `ok` false: acc = 0.
 // Warp-collective (tcgen05.ld): call it with the whole warp.
+template <int D = 64>
 __device__ __forceinline__ void store_unit_jacobian_tmem(uint32_t taddr, bool ok, float scale,
                                                          const bf16* xrow, float inv, bf16* out,
                                                          bool store) {
   float dot = 0.f;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
+  for (int h = 0; h < D / 32; ++h) {
     uint32_t u[32];
     if (ok) {
       tmem_ld32(taddr + 32 * h, u);
@@ -117,7 +118,7 @@ __device__ __forceinline__ void store_unit_jacobian_tmem(uint32_t taddr, bool ok
   }
   const float cf = inv * inv * dot * scale;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
+  for (int h = 0; h < D / 32; ++h) {
     uint32_t u[32];
     if (ok) {
       tmem_ld32(taddr + 32 * h, u);
@@ -159,32 +160,50 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&o)[64]) {
 // ===========================================================================
 // dq kernel
 // ===========================================================================
-namespace dq {
-// two CTAs per SM: 3 K/V stages, single S / dP buffers with dS written over
-// the dP columns it came from, dQ accumulator -> 192 of 256 TMEM columns
-constexpr int kNSq = 3;
-constexpr uint32_t TMq_S = 0, TMq_DP = 64, TMq_ACC = 128, TMq_COLS = 256;
-constexpr uint32_t OFF_Q = 0, OFF_GH = TILE_A, OFF_GL = 2 * TILE_A;
-constexpr uint32_t OFF_K = 3 * TILE_A;
-constexpr uint32_t OFF_V = OFF_K + kNSq * TILE_B;
-constexpr uint32_t OFF_COL = OFF_V + kNSq * TILE_B;  // ik | iv | cos | sin [64] + meta
-constexpr uint32_t COLB = 4 * kBN * 4 + 16;
-constexpr uint32_t OFF_TAB = OFF_COL + kNSq * COLB;
-constexpr uint32_t OFF_BAR = OFF_TAB + 2 * kBN * 4;
-constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNSq, BAR_SD = BAR_EMPTY + kNSq,
-              BAR_P = BAR_SD + 1, BAR_DONE = BAR_P + 1;
-constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 16;
-constexpr uint32_t SMEM = OFF_MISC + 64 + 1024;
-static_assert(2 * (SMEM + 1024) <= 228 * 1024, "two CTAs per SM");
-}  // namespace dq
+// Per head dim D (64 or 128): operand tiles are D / 64 column halves of 64
+// elements (128-byte rows, SW128), each one TMA box and one run of 4 K-steps.
+template <int D>
+struct DqCfg {
+  // D = 64: two CTAs per SM; D = 128: one (the 128-row Q / G_hi / G_lo tiles
+  // alone take 96 KB)
+  static constexpr int kNSq = 3, kMinBlocks = D == 64 ? 2 : 1;
+  static constexpr uint32_t TILE_A = kBM * D * 2, TILE_B = kBN * D * 2;
+  static constexpr uint32_t HALF_A = kBM * 128, HALF_B = kBN * 128;
+  // single S / dP buffers with dS written over the dP columns it came from,
+  // dQ accumulator -> 128 + D of 256 TMEM columns
+  static constexpr uint32_t TMq_S = 0, TMq_DP = 64, TMq_ACC = 128, TMq_COLS = 256;
+  static constexpr uint32_t OFF_Q = 0, OFF_GH = TILE_A, OFF_GL = 2 * TILE_A;
+  static constexpr uint32_t OFF_K = 3 * TILE_A;
+  static constexpr uint32_t OFF_V = OFF_K + kNSq * TILE_B;
+  static constexpr uint32_t OFF_COL = OFF_V + kNSq * TILE_B;  // ik | iv | cos | sin [64] + meta
+  static constexpr uint32_t COLB = 4 * kBN * 4 + 16;
+  static constexpr uint32_t OFF_TAB = OFF_COL + kNSq * COLB;
+  static constexpr uint32_t OFF_BAR = OFF_TAB + 2 * kBN * 4;
+  static constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNSq,
+                       BAR_SD = BAR_EMPTY + kNSq, BAR_P = BAR_SD + 1, BAR_DONE = BAR_P + 1;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 16;
+  static constexpr uint32_t SMEM = OFF_MISC + 64 + 1024;
+  static_assert(kMinBlocks * (SMEM + 1024) <= 228 * 1024, "CTAs per SM");
+  static_assert(TMq_ACC + D <= TMq_COLS, "TMEM budget");
+};
 
 // kDrop: attention dropout on alpha (counter-based bits, AttnShape::drop_thr)
-template <bool kDrop>
-__global__ void __launch_bounds__(kThreads, 2)
+template <bool kDrop, int D>
+__global__ void __launch_bounds__(kThreads, DqCfg<D>::kMinBlocks)
     tc_bwd_dq_kernel(AttnShape s, BwdPtrs p, Aux ax, const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV) {
-  using namespace dq;
+  using C = DqCfg<D>;
+  constexpr int kD = D, kNSq = C::kNSq;
+  constexpr uint32_t TILE_A = C::TILE_A, TILE_B = C::TILE_B, HALF_A = C::HALF_A,
+                     HALF_B = C::HALF_B;
+  constexpr uint32_t TMq_S = C::TMq_S, TMq_DP = C::TMq_DP, TMq_ACC = C::TMq_ACC,
+                     TMq_COLS = C::TMq_COLS;
+  constexpr uint32_t OFF_Q = C::OFF_Q, OFF_GH = C::OFF_GH, OFF_GL = C::OFF_GL, OFF_K = C::OFF_K,
+                     OFF_V = C::OFF_V, OFF_COL = C::OFF_COL, COLB = C::COLB, OFF_TAB = C::OFF_TAB,
+                     OFF_BAR = C::OFF_BAR, OFF_MISC = C::OFF_MISC;
+  constexpr int BAR_A = C::BAR_A, BAR_FULL = C::BAR_FULL, BAR_EMPTY = C::BAR_EMPTY,
+                BAR_SD = C::BAR_SD, BAR_P = C::BAR_P, BAR_DONE = C::BAR_DONE;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -238,9 +257,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     // (cos, sin) by rotation
     if (lane == 0) {
       mbar_arrive_expect_tx(bar(BAR_A), 3 * TILE_A);
-      tma_load_4d(base + OFF_Q, &tmQ, 0, h, (int)i0, b, bar(BAR_A));
-      tma_load_4d(base + OFF_GH, &tmG, 0, h, (int)i0, b, bar(BAR_A));
-      tma_load_4d(base + OFF_GL, &tmG, 0, h, (int)i0, b + s.B, bar(BAR_A));
+#pragma unroll
+      for (int hf = 0; hf < kD / 64; ++hf) {
+        tma_load_4d(base + OFF_Q + hf * HALF_A, &tmQ, 64 * hf, h, (int)i0, b, bar(BAR_A));
+        tma_load_4d(base + OFF_GH + hf * HALF_A, &tmG, 64 * hf, h, (int)i0, b, bar(BAR_A));
+        tma_load_4d(base + OFF_GL + hf * HALF_A, &tmG, 64 * hf, h, (int)i0, b + s.B,
+                    bar(BAR_A));
+      }
     }
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -272,8 +295,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane == 0) {
         const uint32_t fb = bar(BAR_FULL + st);
         mbar_arrive_expect_tx(fb, 2 * TILE_B + 2 * kBN * 4 + 16);
-        tma_load_4d(kb, &tmK, 0, h, (int)j0, b, fb);
-        tma_load_4d(vb, &tmV, 0, h, (int)j0, b, fb);
+#pragma unroll
+        for (int hf = 0; hf < kD / 64; ++hf) {
+          tma_load_4d(kb + hf * HALF_B, &tmK, 64 * hf, h, (int)j0, b, fb);
+          tma_load_4d(vb + hf * HALF_B, &tmV, 64 * hf, h, (int)j0, b, fb);
+        }
         bulk_g2s(colb, ikh + j0, kBN * 4, fb);
         bulk_g2s(colb + kBN * 4, ivh + j0, kBN * 4, fb);
         bulk_g2s(colb + 4 * kBN * 4, mh + kt, 16, fb);
@@ -314,18 +340,25 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!mbar_wait(bar(BAR_FULL + st), (jj / kNSq) & 1, abort_flag, kWaitLimitNs)) return false;
         tc_fence_after();
         const uint32_t kb = base + OFF_K + st * TILE_B, vb = base + OFF_V + st * TILE_B;
+        // K-steps of 16 over the D / 64 column halves (four per half)
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TMq_S, desc_sw128(base + OFF_Q + kk * 32, 16, 1024),
-                 desc_sw128(kb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t oa = (kk >> 2) * HALF_A + (kk & 3) * 32, ob = (kk >> 2) * HALF_B + (kk & 3) * 32;
+          mma_ss(tmem + TMq_S, desc_sw128(base + OFF_Q + oa, 16, 1024),
+                 desc_sw128(kb + ob, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TMq_DP, desc_sw128(base + OFF_GH + kk * 32, 16, 1024),
-                 desc_sw128(vb + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t oa = (kk >> 2) * HALF_A + (kk & 3) * 32, ob = (kk >> 2) * HALF_B + (kk & 3) * 32;
+          mma_ss(tmem + TMq_DP, desc_sw128(base + OFF_GH + oa, 16, 1024),
+                 desc_sw128(vb + ob, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TMq_DP, desc_sw128(base + OFF_GL + kk * 32, 16, 1024),
-                 desc_sw128(vb + kk * 32, 16, 1024), idS, 1u);
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t oa = (kk >> 2) * HALF_A + (kk & 3) * 32, ob = (kk >> 2) * HALF_B + (kk & 3) * 32;
+          mma_ss(tmem + TMq_DP, desc_sw128(base + OFF_GL + oa, 16, 1024),
+                 desc_sw128(vb + ob, 16, 1024), idS, 1u);
+        }
         mma_commit(bar(BAR_SD));
         return true;
       };
@@ -341,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
           mma_ts(tmem + TMq_ACC, tmem + TMq_DP + (kk >> 1) * 32 + (kk & 1) * 8,
-                 desc_sw128(kb + kk * 16 * 128, TILE_B, 1024), idQ,
+                 desc_sw128(kb + kk * 16 * 128, HALF_B, 1024), idQ,
                  (started || kk > 0) ? 1u : 0u);
         started = true;
         mma_commit(bar(BAR_EMPTY + st));
@@ -417,10 +450,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         // interior tiles run without the window-edge selects
         auto run = [&](auto edge) {
           constexpr bool EDGE = decltype(edge)::value;
-  #pragma unroll
+#pragma unroll
           for (int q4 = 0; q4 < 8; ++q4) {
             const float4 ikv = ik4[q4], ivv = iv4[q4], ccv = cc4[q4], scv = sc4[q4];
-  #pragma unroll
+#pragma unroll
             for (int hp = 0; hp < 2; ++hp) {
               const int c = 4 * q4 + 2 * hp;
               const float2 ik2 = hp ? make_float2(ikv.z, ikv.w) : make_float2(ikv.x, ikv.y);
@@ -479,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       bf16* orow = reinterpret_cast<bf16*>(p.dq.p) + (long long)b * p.dq.sb + ii * p.dq.st +
                    (long long)h * kD;
       // dS was stored without its 2 r
-      store_unit_jacobian_tmem(tmem + TMq_ACC + lane_off, ok && misc[3],
+      store_unit_jacobian_tmem<kD>(tmem + TMq_ACC + lane_off, ok && misc[3],
                                2.0f * r * (kDrop ? s.drop_scale : 1.0f), qrow, iq,
                                orow, st_row);
     }
@@ -495,44 +528,68 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ===========================================================================
 // dk / dv kernel
 // ===========================================================================
-namespace kv {
-constexpr uint32_t OFF_K = 0, OFF_V = TILE_A;
-constexpr uint32_t OFF_Q = 2 * TILE_A;                 // per stage: Q | G_hi | G_lo (8 KB each)
-constexpr uint32_t STAGE = 3 * TILE_B;
-// dS^T staging for the fused dQ MMA: two buffers, each a pair of query tiles
-// [128 keys][64 queries] bf16 (SW128), 16 KB apart (the operand's LBO)
-constexpr uint32_t OFF_STG = OFF_Q + kNS * STAGE;
-constexpr uint32_t STG_PAIR = 2 * TILE_A;
-// per stage: iq | cos | sin [64] + meta (16 B) + dropout row keys of the 64 queries
-constexpr uint32_t OFF_COL = OFF_STG + 2 * STG_PAIR;
-constexpr uint32_t COLB = 3 * kBN * 4 + 16 + kBN * 4;
-constexpr uint32_t OFF_TAB = OFF_COL + kNS * COLB;
-constexpr uint32_t OFF_RED = OFF_TAB + 2 * kBN * 4;     // [2][8] dr / dw warp sums
-constexpr uint32_t OFF_BAR = OFF_RED + 64 * 4;
-constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNS, BAR_SD = BAR_EMPTY + kNS,
-              BAR_P = BAR_SD + 2, BAR_DONE = BAR_P + 2, BAR_DQF = BAR_DONE + 1,
-              BAR_DQE = BAR_DQF + 2, BAR_SF = BAR_DQE + 2, BAR_COUNT = BAR_SF + 2;
-constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 24;
-static_assert(BAR_COUNT <= 24, "barrier space");
-constexpr uint32_t SMEM = OFF_MISC + 64 + 1024;
-static_assert(SMEM <= 227 * 1024, "shared memory");
-static_assert(OFF_STG % 1024 == 0 && STG_PAIR == 8 * 4096, "dQ drain regions");
-// TMEM: S and dP double-buffered; alpha / dS (bf16) written over the S / dP
-// columns they came from; dV, dK and two dQ accumulators -> 512 columns
-constexpr uint32_t TK_S = 0, TK_DP = 128, TK_ACCV = 256, TK_ACCK = 320, TK_ACCQ = 384;
-}  // namespace kv
+// D = 64: the fused kernel (dQ here too) with a 4-stage ring; D = 128 (and
+// the fixed-order path) without dQ: 3 stages, no dS^T staging, and the dV /
+// dK accumulators take D columns each.
+template <int D, bool kFuse>
+struct KvCfg {
+  static constexpr int kNS = D == 64 ? 4 : 3;
+  static constexpr uint32_t TILE_A = kBM * D * 2, TILE_B = kBN * D * 2;
+  static constexpr uint32_t HALF_A = kBM * 128, HALF_B = kBN * 128;
+  static constexpr uint32_t OFF_K = 0, OFF_V = TILE_A;
+  static constexpr uint32_t OFF_Q = 2 * TILE_A;          // per stage: Q | G_hi | G_lo
+  static constexpr uint32_t STAGE = 3 * TILE_B;
+  // dS^T staging for the fused dQ MMA: two buffers, each a pair of query tiles
+  // [128 keys][64 queries] bf16 (SW128), 16 KB apart (the operand's LBO)
+  static constexpr uint32_t OFF_STG = OFF_Q + kNS * STAGE;
+  static constexpr uint32_t STG_PAIR = 2 * kBM * 64 * 2;
+  // per stage: iq | cos | sin [64] + meta (16 B) + dropout row keys of the 64 queries
+  static constexpr uint32_t OFF_COL = OFF_STG + (kFuse ? 2 * STG_PAIR : 0);
+  static constexpr uint32_t COLB = 3 * kBN * 4 + 16 + kBN * 4;
+  static constexpr uint32_t OFF_TAB = OFF_COL + kNS * COLB;
+  static constexpr uint32_t OFF_RED = OFF_TAB + 2 * kBN * 4;   // [2][8] dr / dw warp sums
+  static constexpr uint32_t OFF_BAR = OFF_RED + 64 * 4;
+  static constexpr int BAR_A = 0, BAR_FULL = 1, BAR_EMPTY = BAR_FULL + kNS,
+                       BAR_SD = BAR_EMPTY + kNS, BAR_P = BAR_SD + 2, BAR_DONE = BAR_P + 2,
+                       BAR_DQF = BAR_DONE + 1, BAR_DQE = BAR_DQF + 2, BAR_SF = BAR_DQE + 2,
+                       BAR_COUNT = BAR_SF + 2;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + 8 * 24;
+  static constexpr uint32_t SMEM = OFF_MISC + 64 + 1024;
+  // TMEM: S and dP double-buffered; alpha / dS (bf16) written over the S / dP
+  // columns they came from; dV, dK (and with kFuse two dQ accumulators)
+  static constexpr uint32_t TK_S = 0, TK_DP = 128, TK_ACCV = 256, TK_ACCK = 256 + D,
+                            TK_ACCQ = 384;
+  static_assert(BAR_COUNT <= 24, "barrier space");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(OFF_STG % 1024 == 0 && STG_PAIR == 8 * 4096, "dQ drain regions");
+  static_assert(TK_ACCK + D <= TM_COLS && (!kFuse || (D == 64 && TK_ACCQ + 128 <= TM_COLS)),
+                "TMEM budget");
+};
 
 // kFuse: dQ is computed here too (dQ += dS K on the tensor cores per pair of
 // query tiles, added into an fp32 accumulator with vector reductions);
 // otherwise tc_bwd_dq_kernel computes it (deterministic order)
 // kDrop: attention dropout on alpha (counter-based bits, AttnShape::drop_thr)
-template <bool kFuse, bool kDrop>
+template <bool kFuse, bool kDrop, int D = 64>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_bwd_kv_kernel(AttnShape s, BwdPtrs p, Aux ax, const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmDQ) {
-  using namespace kv;
+  using C = KvCfg<D, kFuse>;
+  constexpr int kD = D, kNS = C::kNS;
+  constexpr uint32_t TILE_A = C::TILE_A, TILE_B = C::TILE_B, HALF_A = C::HALF_A,
+                     HALF_B = C::HALF_B;
+  constexpr uint32_t OFF_K = C::OFF_K, OFF_V = C::OFF_V, OFF_Q = C::OFF_Q, STAGE = C::STAGE,
+                     OFF_STG = C::OFF_STG, STG_PAIR = C::STG_PAIR, OFF_COL = C::OFF_COL,
+                     COLB = C::COLB, OFF_TAB = C::OFF_TAB, OFF_RED = C::OFF_RED,
+                     OFF_BAR = C::OFF_BAR, OFF_MISC = C::OFF_MISC;
+  constexpr int BAR_A = C::BAR_A, BAR_FULL = C::BAR_FULL, BAR_EMPTY = C::BAR_EMPTY,
+                BAR_SD = C::BAR_SD, BAR_P = C::BAR_P, BAR_DONE = C::BAR_DONE,
+                BAR_DQF = C::BAR_DQF, BAR_DQE = C::BAR_DQE, BAR_SF = C::BAR_SF;
+  constexpr uint32_t TK_S = C::TK_S, TK_DP = C::TK_DP, TK_ACCV = C::TK_ACCV,
+                     TK_ACCK = C::TK_ACCK, TK_ACCQ = C::TK_ACCQ;
+  static_assert(!kFuse || D == 64, "the fused dQ path is built for D = 64");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -601,8 +658,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the column (cos, sin) by rotation
     if (lane == 0) {
       mbar_arrive_expect_tx(bar(BAR_A), 2 * TILE_A);
-      tma_load_4d(base + OFF_K, &tmK, 0, h, (int)j0, b, bar(BAR_A));
-      tma_load_4d(base + OFF_V, &tmV, 0, h, (int)j0, b, bar(BAR_A));
+#pragma unroll
+      for (int hf = 0; hf < kD / 64; ++hf) {
+        tma_load_4d(base + OFF_K + hf * HALF_A, &tmK, 64 * hf, h, (int)j0, b, bar(BAR_A));
+        tma_load_4d(base + OFF_V + hf * HALF_A, &tmV, 64 * hf, h, (int)j0, b, bar(BAR_A));
+      }
     }
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -634,9 +694,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         const uint32_t fb = bar(BAR_FULL + st);
         mbar_arrive_expect_tx(fb, 3 * TILE_B + kBN * 4 + 16);
-        tma_load_4d(sb_, &tmQ, 0, h, (int)iq0, b, fb);
-        tma_load_4d(sb_ + TILE_B, &tmG, 0, h, (int)iq0, b, fb);
-        tma_load_4d(sb_ + 2 * TILE_B, &tmG, 0, h, (int)iq0, b + s.B, fb);
+#pragma unroll
+        for (int hf = 0; hf < kD / 64; ++hf) {
+          tma_load_4d(sb_ + hf * HALF_B, &tmQ, 64 * hf, h, (int)iq0, b, fb);
+          tma_load_4d(sb_ + TILE_B + hf * HALF_B, &tmG, 64 * hf, h, (int)iq0, b, fb);
+          tma_load_4d(sb_ + 2 * TILE_B + hf * HALF_B, &tmG, 64 * hf, h, (int)iq0, b + s.B, fb);
+        }
         bulk_g2s(colb, iqh + iq0, kBN * 4, fb);
         bulk_g2s(colb + 3 * kBN * 4, mh + qt, 16, fb);
       }
@@ -683,7 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dK_k = desc_sw128(base + OFF_K, 16, 1024);       // K-major (S: A = K)
       const uint64_t dV_k = desc_sw128(base + OFF_V, 16, 1024);       // K-major (dP: A = V)
       const uint64_t dQ_k = desc_sw128(base + OFF_Q, 16, 1024);       // stage 0 Q, K-major
-      const uint64_t dQ_mn = desc_sw128(base + OFF_Q, TILE_B, 1024);  // stage 0 Q, MN-major
+      const uint64_t dQ_mn = desc_sw128(base + OFF_Q, HALF_B, 1024);  // stage 0 Q, MN-major
       const uint64_t dStg = desc_sw128(base + OFF_STG, TILE_A, 1024); // dS^T staging, MN-major
       const uint64_t dK_mn = desc_sw128(base + OFF_K, TILE_A, 1024);  // K, MN-major (dQ: B)
       int pair_i = 0;   // pairs of query tiles whose dQ has been issued
@@ -736,15 +799,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         const uint64_t qd = dQ_k + (uint64_t)((st * STAGE) >> 4), ghd = qd + (TILE_B >> 4),
                        gld = qd + (2 * TILE_B >> 4);
-        // S and dP (hi) interleaved, then dP (lo)
+        // S and dP (hi) interleaved, then dP (lo); K-steps of 16 over the
+        // D / 64 column halves (descriptor units of 16 bytes)
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
-          mma_ss(tmem + TK_S + kBN * bb, dK_k + 2 * kk, qd + 2 * kk, idS, kk > 0 ? 1u : 0u);
-          mma_ss(tmem + TK_DP + kBN * bb, dV_k + 2 * kk, ghd + 2 * kk, idS, kk > 0 ? 1u : 0u);
+          const uint64_t oa = ((kk >> 2) * HALF_A + (kk & 3) * 32) >> 4,
+                         ob = ((kk >> 2) * HALF_B + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + TK_S + kBN * bb, dK_k + oa, qd + ob, idS, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + TK_DP + kBN * bb, dV_k + oa, ghd + ob, idS, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tmem + TK_DP + kBN * bb, dV_k + 2 * kk, gld + 2 * kk, idS, 1u);
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint64_t oa = ((kk >> 2) * HALF_A + (kk & 3) * 32) >> 4,
+                         ob = ((kk >> 2) * HALF_B + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + TK_DP + kBN * bb, dV_k + oa, gld + ob, idS, 1u);
+        }
         mma_commit(bar(BAR_SD + bb));
         if (j >= 1) ok = issue_kv(j - 1);
       }
@@ -888,10 +957,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // interior tiles run without the window-edge selects
         auto run = [&](auto edge) {
           constexpr bool EDGE = decltype(edge)::value;
-  #pragma unroll
+#pragma unroll
           for (int q4 = 0; q4 < 8; ++q4) {
             const float4 iqv = iq4[q4], cvv = cv4[q4], svv = sv4[q4];
-  #pragma unroll
+#pragma unroll
             for (int hp = 0; hp < 2; ++hp) {
               const int c = 4 * q4 + 2 * hp;
               const float2 iq2 = hp ? make_float2(iqv.z, iqv.w) : make_float2(iqv.x, iqv.y);
@@ -998,29 +1067,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     // tcgen05.ld is warp-collective: every lane takes the same branch
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    float acc[64];
-    if (ok && misc[3]) {
-      tmem_ld64(tmem + (g == 0 ? TK_ACCK : TK_ACCV) + lane_off, acc);
-    } else {
+    if constexpr (kD == 64) {
+      float acc[64];
+      if (ok && misc[3]) {
+        tmem_ld64(tmem + (g == 0 ? TK_ACCK : TK_ACCV) + lane_off, acc);
+      } else {
 #pragma unroll
-      for (int c = 0; c < 64; ++c) acc[c] = 0.f;
-    }
-    if (ok && valid) {
+        for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+      }
+      if (ok && valid) {
+        if (g == 0) {
+          // dS was stored without this key's 2 r / |v|
+#pragma unroll
+          for (int c = 0; c < 64; ++c) acc[c] *= 2.0f * r * iv * dsc;
+          store_unit_jacobian(acc, kh + jrow * p.k.st, ik,
+                              reinterpret_cast<bf16*>(p.dk.p) + (long long)b * p.dk.sb +
+                                  jrow * p.dk.st + (long long)h * kD);
+        } else {
+          if (kDrop) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) acc[c] *= dsc;
+          }
+          store_unit_jacobian(acc, vh + jrow * p.v.st, iv,
+                              reinterpret_cast<bf16*>(p.dv.p) + (long long)b * p.dv.sb +
+                                  jrow * p.dv.st + (long long)h * kD);
+        }
+      }
+    } else {
+      // D = 128: the accumulator rows are streamed from TMEM 32 columns at
+      // a time through the normalisation Jacobian
+      const bool okacc = ok && misc[3] != 0;
+      const long long jr = valid ? jrow : 0;
       if (g == 0) {
         // dS was stored without this key's 2 r / |v|
-#pragma unroll
-        for (int c = 0; c < 64; ++c) acc[c] *= 2.0f * r * iv * dsc;
-        store_unit_jacobian(acc, kh + jrow * p.k.st, ik,
-                            reinterpret_cast<bf16*>(p.dk.p) + (long long)b * p.dk.sb +
-                                jrow * p.dk.st + (long long)h * kD);
+        store_unit_jacobian_tmem<kD>(tmem + TK_ACCK + lane_off, okacc, 2.0f * r * iv * dsc,
+                                     kh + jr * p.k.st, ik,
+                                     reinterpret_cast<bf16*>(p.dk.p) + (long long)b * p.dk.sb +
+                                         jr * p.dk.st + (long long)h * kD,
+                                     ok && valid);
       } else {
-        if (kDrop) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) acc[c] *= dsc;
-        }
-        store_unit_jacobian(acc, vh + jrow * p.v.st, iv,
-                            reinterpret_cast<bf16*>(p.dv.p) + (long long)b * p.dv.sb +
-                                jrow * p.dv.st + (long long)h * kD);
+        store_unit_jacobian_tmem<kD>(tmem + TK_ACCV + lane_off, okacc, dsc, vh + jr * p.v.st, iv,
+                                     reinterpret_cast<bf16*>(p.dv.p) + (long long)b * p.dv.sb +
+                                         jr * p.dv.st + (long long)h * kD,
+                                     ok && valid);
       }
     }
   }
@@ -1128,7 +1217,7 @@ __global__ void __launch_bounds__(256) tc_bwd_dq_finalize_kernel(
                             4 * l) = o;
 }
 
-bool tc_bwd_supported(int dtype, int D) { return dtype == SCREEN_BF16 && D == kD; }
+bool tc_bwd_supported(int dtype, int D) { return dtype == SCREEN_BF16 && (D == 64 || D == 128); }
 
 size_t tc_bwd_aux_bytes(const AttnShape& s) {
   const long long BH = (long long)s.B * s.H, Tqp = padT(s.Tq), Tkp = padT(s.Tk);
@@ -1141,16 +1230,23 @@ long long tc_bwd_partials(const AttnShape& s) {
   return (long long)s.B * ((s.Tk + kBM - 1) / kBM);
 }
 
-int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st) {
-  if (s.B == 0 || s.H == 0) return SCREEN_OK;
+namespace {
+template <int D>
+int tc_bwd_d(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st) {
   {
-    const void* fns[6] = {(const void*)tc_bwd_dq_kernel<false>, (const void*)tc_bwd_dq_kernel<true>,
-                          (const void*)tc_bwd_kv_kernel<true, false>,
-                          (const void*)tc_bwd_kv_kernel<false, false>,
-                          (const void*)tc_bwd_kv_kernel<true, true>,
-                          (const void*)tc_bwd_kv_kernel<false, true>};
+    // D = 128 has no fused kernel: dq comes from the query-major kernel
+    const void* fns[6] = {(const void*)tc_bwd_dq_kernel<false, D>,
+                          (const void*)tc_bwd_dq_kernel<true, D>,
+                          (const void*)tc_bwd_kv_kernel<false, false, D>,
+                          (const void*)tc_bwd_kv_kernel<false, true, D>,
+                          D == 64 ? (const void*)tc_bwd_kv_kernel<true, false, 64> : nullptr,
+                          D == 64 ? (const void*)tc_bwd_kv_kernel<true, true, 64> : nullptr};
+    const int sm[6] = {(int)DqCfg<D>::SMEM, (int)DqCfg<D>::SMEM, (int)KvCfg<D, false>::SMEM,
+                       (int)KvCfg<D, false>::SMEM, (int)KvCfg<64, true>::SMEM,
+                       (int)KvCfg<64, true>::SMEM};
     for (int i = 0; i < 6; ++i) {
-      const cudaError_t e = ensure_smem_optin(fns[i], i < 2 ? (int)dq::SMEM : (int)kv::SMEM);
+      if (!fns[i]) continue;
+      const cudaError_t e = ensure_smem_optin(fns[i], sm[i]);
       if (e != cudaSuccess) return record_cuda_error(e);
     }
   }
@@ -1180,64 +1276,81 @@ int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaS
   // TMA descriptors: q, k, v as given (raw, strided); G as two stacked
   // planes [2][B][Tq][H][D] (batch b + B is the low plane)
   CUtensorMap tq128, tq64, tg128, tg64, tk128, tk64, tv128, tv64;
-  const long long gsb = (long long)s.Tq * s.H * kD, gst = (long long)s.H * kD;
-  if (!make_tmap_bthd(&tq128, p.q.p, s.B, s.Tq, s.H, p.q.sb, p.q.st, kBM) ||
-      !make_tmap_bthd(&tq64, p.q.p, s.B, s.Tq, s.H, p.q.sb, p.q.st, kBN) ||
-      !make_tmap_bthd(&tg128, p.G, 2LL * s.B, s.Tq, s.H, gsb, gst, kBM) ||
-      !make_tmap_bthd(&tg64, p.G, 2LL * s.B, s.Tq, s.H, gsb, gst, kBN) ||
-      !make_tmap_bthd(&tk128, p.k.p, s.B, s.Tk, s.H, p.k.sb, p.k.st, kBM) ||
-      !make_tmap_bthd(&tk64, p.k.p, s.B, s.Tk, s.H, p.k.sb, p.k.st, kBN) ||
-      !make_tmap_bthd(&tv128, p.v.p, s.B, s.Tk, s.H, p.v.sb, p.v.st, kBM) ||
-      !make_tmap_bthd(&tv64, p.v.p, s.B, s.Tk, s.H, p.v.sb, p.v.st, kBN))
+  const long long gsb = (long long)s.Tq * s.H * D, gst = (long long)s.H * D;
+  if (!make_tmap_bthd(&tq128, p.q.p, s.B, s.Tq, s.H, p.q.sb, p.q.st, kBM, D) ||
+      !make_tmap_bthd(&tq64, p.q.p, s.B, s.Tq, s.H, p.q.sb, p.q.st, kBN, D) ||
+      !make_tmap_bthd(&tg128, p.G, 2LL * s.B, s.Tq, s.H, gsb, gst, kBM, D) ||
+      !make_tmap_bthd(&tg64, p.G, 2LL * s.B, s.Tq, s.H, gsb, gst, kBN, D) ||
+      !make_tmap_bthd(&tk128, p.k.p, s.B, s.Tk, s.H, p.k.sb, p.k.st, kBM, D) ||
+      !make_tmap_bthd(&tk64, p.k.p, s.B, s.Tk, s.H, p.k.sb, p.k.st, kBN, D) ||
+      !make_tmap_bthd(&tv128, p.v.p, s.B, s.Tk, s.H, p.v.sb, p.v.st, kBM, D) ||
+      !make_tmap_bthd(&tv64, p.v.p, s.B, s.Tk, s.H, p.v.sb, p.v.st, kBN, D))
     return SCREEN_ERR_CUDA;
   const bool deterministic = (stages & SCREEN_BWD_DETERMINISTIC) != 0;
-  if (deterministic) {
-    // dq by its own query-major kernel: every sum in a fixed order
-    if (s.Tq > 0 && (stages & 2)) {
+  if (deterministic || D != 64) {
+    // dq by its own query-major kernel: every sum in a fixed order.  Stage
+    // 2 runs it, stage 4 the key-major kernel; at D = 128 (no fused kernel)
+    // stage 4 outside the fixed-order mode runs both
+    const bool run_dq = (stages & 2) || (!deterministic && (stages & 4));
+    if (s.Tq > 0 && run_dq) {
       dim3 g1((s.Tq + kBM - 1) / kBM, s.B * s.H);
       if (s.drop_thr)
-        tc_bwd_dq_kernel<true><<<g1, kThreads, dq::SMEM, st>>>(s, p, ax, tq128, tg128, tk64, tv64);
+        tc_bwd_dq_kernel<true, D><<<g1, kThreads, DqCfg<D>::SMEM, st>>>(s, p, ax, tq128, tg128,
+                                                                        tk64, tv64);
       else
-        tc_bwd_dq_kernel<false><<<g1, kThreads, dq::SMEM, st>>>(s, p, ax, tq128, tg128, tk64, tv64);
+        tc_bwd_dq_kernel<false, D><<<g1, kThreads, DqCfg<D>::SMEM, st>>>(s, p, ax, tq128, tg128,
+                                                                         tk64, tv64);
     }
     if (s.Tk > 0 && (stages & 4)) {
       const int nkt = (s.Tk + kBM - 1) / kBM;
       tile_order(s, 1, nkt, order, st);
       if (s.drop_thr)
-        tc_bwd_kv_kernel<false, true><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(
-            s, p, ax, tq64, tg64, tk128, tv128, tq64);
+        tc_bwd_kv_kernel<false, true, D><<<(unsigned)(BH * nkt), kThreads,
+                                           KvCfg<D, false>::SMEM, st>>>(s, p, ax, tq64, tg64,
+                                                                         tk128, tv128, tq64);
       else
-        tc_bwd_kv_kernel<false, false><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(
-            s, p, ax, tq64, tg64, tk128, tv128, tq64);
+        tc_bwd_kv_kernel<false, false, D><<<(unsigned)(BH * nkt), kThreads,
+                                            KvCfg<D, false>::SMEM, st>>>(s, p, ax, tq64, tg64,
+                                                                          tk128, tv128, tq64);
     }
     return SCREEN_OK;
   }
-  // fused: the key-major kernel also forms dq^ (fp32 vector reductions into
-  // dq_acc), the finalize pass applies the 1/|q| Jacobian; stage 4 runs both
-  // (dq with dk, dv), stage 2 alone runs nothing
-  if (stages & 4) {
-    const size_t acc_bytes = (size_t)BH * s.Tq * kD * 4;
-    if (acc_bytes && cudaMemsetAsync(dq_acc, 0, acc_bytes, st) != cudaSuccess) return SCREEN_ERR_CUDA;
-    BwdPtrs pf = p;
-    pf.dq_acc = dq_acc;
-    if (s.Tk > 0) {
-      const int nkt = (s.Tk + kBM - 1) / kBM;
-      tile_order(s, 1, nkt, order, st);
-      CUtensorMap tdq;
-      if (!make_tmap_dq(&tdq, dq_acc, s.B, s.Tq, s.H)) return SCREEN_ERR_CUDA;
-      if (s.drop_thr)
-        tc_bwd_kv_kernel<true, true><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(
-            s, pf, ax, tq64, tg64, tk128, tv128, tdq);
-      else
-        tc_bwd_kv_kernel<true, false><<<(unsigned)(BH * nkt), kThreads, kv::SMEM, st>>>(
-            s, pf, ax, tq64, tg64, tk128, tv128, tdq);
+  if constexpr (D == 64) {
+    // fused: the key-major kernel also forms dq^ (TMA reduce-adds into
+    // dq_acc), the finalize pass applies the 1/|q| Jacobian; stage 4 runs
+    // both (dq with dk, dv), stage 2 alone runs nothing
+    if (stages & 4) {
+      const size_t acc_bytes = (size_t)BH * s.Tq * kD * 4;
+      if (acc_bytes && cudaMemsetAsync(dq_acc, 0, acc_bytes, st) != cudaSuccess)
+        return SCREEN_ERR_CUDA;
+      BwdPtrs pf = p;
+      pf.dq_acc = dq_acc;
+      if (s.Tk > 0) {
+        const int nkt = (s.Tk + kBM - 1) / kBM;
+        tile_order(s, 1, nkt, order, st);
+        CUtensorMap tdq;
+        if (!make_tmap_dq(&tdq, dq_acc, s.B, s.Tq, s.H)) return SCREEN_ERR_CUDA;
+        if (s.drop_thr)
+          tc_bwd_kv_kernel<true, true><<<(unsigned)(BH * nkt), kThreads, KvCfg<64, true>::SMEM,
+                                         st>>>(s, pf, ax, tq64, tg64, tk128, tv128, tdq);
+        else
+          tc_bwd_kv_kernel<true, false><<<(unsigned)(BH * nkt), kThreads, KvCfg<64, true>::SMEM,
+                                          st>>>(s, pf, ax, tq64, tg64, tk128, tv128, tdq);
+      }
+      const long long rows = BH * s.Tq;
+      if (rows > 0)
+        tc_bwd_dq_finalize_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(
+            dq_acc, p.q, p.nq, p.dq, s.B, s.Tq, s.H);
     }
-    const long long rows = BH * s.Tq;
-    if (rows > 0)
-      tc_bwd_dq_finalize_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(
-          dq_acc, p.q, p.nq, p.dq, s.B, s.Tq, s.H);
   }
   return SCREEN_OK;
+}
+}  // namespace
+
+int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, int D,
+           cudaStream_t st) {
+  if (s.B == 0 || s.H == 0) return SCREEN_OK;
+  return D == 128 ? tc_bwd_d<128>(s, p, aux_ws, stages, st) : tc_bwd_d<64>(s, p, aux_ws, stages, st);
 }
 
 

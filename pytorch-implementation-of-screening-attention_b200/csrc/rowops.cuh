@@ -99,7 +99,7 @@ size_t tc_fwd_workspace(const AttnShape& s, int D);
 int tc_fwd(const AttnShape& s, const FwdPtrs& p, void* workspace, bool norms_given, int D,
            cudaStream_t st);
 int tc_device_status(bool clear);
-// tcgen05 / TMEM backward (bf16, D = 64: tc_bwd_supported); aux_ws holds
+// tcgen05 / TMEM backward (bf16, D = 64 or 128); aux_ws holds
 // tc_bwd_aux_bytes()
 bool tc_bwd_supported(int dtype, int D);
 size_t tc_bwd_aux_bytes(const AttnShape& s);
@@ -109,7 +109,7 @@ long long tc_bwd_partials(const AttnShape& s);
 // count.  kind 0: query tiles of 128 (forward), kind 1: key tiles of 128
 // (key-major backward).  One CTA, counting sort; perm holds B*H*ntiles ints.
 void tile_order(const AttnShape& s, int kind, int ntiles, int* perm, cudaStream_t st);
-int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, cudaStream_t st);
+int tc_bwd(const AttnShape& s, const BwdPtrs& p, void* aux_ws, int stages, int D, cudaStream_t st);
 int tc_bwd_device_status(bool clear);
 
 // bf16 warp-level mma.sync kernels (D = 64).

@@ -157,13 +157,16 @@ def test_t4096_bf16_against_oracle(ms, oracle):
     assert_all_close(got, ref, 2e-2, "T=4096")
 
 
-def test_backward_is_deterministic(ms):
+@pytest.mark.parametrize("D", [64, 128])
+def test_backward_is_deterministic(ms, D):
     """With torch.use_deterministic_algorithms(True) the backward takes the
-    fixed-order path (dq by its own kernel): bitwise reproducible."""
+    fixed-order path (dq by its own kernel): bitwise reproducible.  At
+    D = 128 that is the only tensor-core backward, deterministic or not."""
     prev = torch.are_deterministic_algorithms_enabled()
-    torch.use_deterministic_algorithms(True, warn_only=True)
+    if D == 64:
+        torch.use_deterministic_algorithms(True, warn_only=True)
     try:
-        _backward_twice_equal(ms)
+        _backward_twice_equal(ms, D)
     finally:
         torch.use_deterministic_algorithms(prev)
 
@@ -201,10 +204,10 @@ def test_fused_dq_backward_matches_fixed_order(ms):
     assert ms._lib.device_status() == 0
 
 
-def _backward_twice_equal(ms):
+def _backward_twice_equal(ms, D=64):
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(3)
-    B, T, H, D = 2, 1000, 4, 64
+    B, T, H = 2, 1000, 4
     q = torch.randn(B, T, H, D, device=dev, generator=g).bfloat16()
     k = (q.float() + 0.5 * torch.randn(B, T, H, D, device=dev, generator=g)).bfloat16()
     v = torch.randn(B, T, H, D, device=dev, generator=g).bfloat16()
@@ -266,3 +269,27 @@ def test_head_dim_128_forward_runs_on_tensor_cores(ms):
     ms._lib.screen_fwd(q, k, v, r, w, True, tile_stats=stats)
     torch.cuda.synchronize()
     assert int(stats[0]) > 0
+
+
+def test_head_dim_128_core_long(ms, oracle):
+    """D = 128 forward and backward on the tensor cores at T = 2048 with
+    windows from 40 to 2000, against the fp64 chunked oracle, bf16 contract."""
+    g = torch.Generator().manual_seed(128)
+    B, T, H, D = 1, 2048, 4, 128
+    q = torch.randn(B, T, H, D, generator=g)
+    k = 0.6 * q + torch.randn(B, T, H, D, generator=g)
+    v = torch.randn(B, T, H, D, generator=g)
+    q, k, v = (t.bfloat16().float() for t in (q, k, v))
+    r = torch.tensor([1.02, 1.3, 1.8, 1.1])
+    w = torch.tensor([40.0, 300.0, 2000.0, 900.5])
+    dy = torch.randn(B, T, H, D, generator=g)
+    dev = torch.device("cuda:0")
+    qc, kc, vc = (t.to(dev, torch.bfloat16).requires_grad_(True) for t in (q, k, v))
+    rc, wc = r.to(dev).requires_grad_(True), w.to(dev).requires_grad_(True)
+    y = ms.screening_attention(qc, kc, vc, rc, wc, True)
+    y.backward(dy.to(dev, torch.bfloat16))
+    ref = oracle.windowed_core_grads(q, k, v, r, w, dy.bfloat16().float(), True)
+    got = [t.detach().float().cpu() for t in (y, qc.grad, kc.grad, vc.grad, rc.grad, wc.grad)]
+    for name, a, b in zip(("y", "dq", "dk", "dv", "dr", "dw"), got, ref):
+        assert rel_err(a, b) <= 2e-2, name
+    assert ms._lib.device_status() == 0
