@@ -1,5 +1,5 @@
 // Screening attention forward on the 5th-generation tensor cores (tcgen05,
-// TMEM accumulators), bf16, head dim 64.
+// TMEM accumulators), bf16, head dim 64 or 128 (FwdCfg below).
 //
 // Math: multiscreen/attention.py:156-196 -- S = q^ k^T, a = relu(1-r(1-S)),
 // alpha = a^2 m(rel), o = alpha v^, y = TanhNorm(o) (norm.py:23-25).
@@ -23,8 +23,9 @@
 //   warp 5     MMA issuer (one thread): S_j = Q K_j^T (M=128, N=64, K=64) into
 //              a double-buffered TMEM S, then O += P_{j-1} V^_{j-1} (A from
 //              TMEM, V^ MN-major from shared memory) into the TMEM O.
-// TMEM: S0 [0,64) S1 [64,128) P0 [128,160) P1 [160,192) O [192,256) -> 256
-// columns, so two CTAs share an SM.  Key tiles outside the window are never
+// TMEM (D = 64): a ring of three 64-column S buffers with P written over
+// them, O [192,256) -> 256 columns, so two CTAs share an SM (D = 128: two S
+// buffers and O [128,256)).  Key tiles outside the window are never
 // loaded; a tile whose scores provably all fall under the trim threshold
 // skips the alpha/PV work.  Every wait is bounded by a global-timer limit; on
 // expiry the CTA drains, frees its TMEM and records SCREEN_ERR_TIMEOUT in a

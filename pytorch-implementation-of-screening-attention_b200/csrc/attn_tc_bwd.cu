@@ -1,4 +1,5 @@
-// Screening attention backward on tcgen05 / TMEM (bf16, head dim 64).
+// Screening attention backward on tcgen05 / TMEM (bf16, head dim 64 or 128;
+// at 128 without the fused dQ, see KvCfg / DqCfg).
 //
 // Autograd of multiscreen/attention.py:156-196 (the reference leaves it to
 // PyTorch; its Triton backward, kernels/screening_bwd.py, has no dr / dw):
