@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define SCREEN_ABI_VERSION 4
+#define SCREEN_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define SCREEN_API __attribute__((visibility("default")))
@@ -291,6 +291,37 @@ typedef struct screen_xent_args {
 
 SCREEN_API int screen_cross_entropy_fwd(const screen_xent_args* a, screen_stream_t stream);
 SCREEN_API int screen_cross_entropy_bwd(const screen_xent_args* a, screen_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* RMSNorm of the blocks' pre-norms (torch.nn.RMSNorm in multiscreen/        */
+/* layers.py:35-36,60-76 and model.py:57,98): y = x / sqrt(mean(x^2) + eps)  */
+/* * w over contiguous rows of length D (D % 8 == 0, rows 16-byte aligned),  */
+/* fp32 math.  x and dx: fp32 or bf16; w and dw: fp32 or bf16; y and dy:     */
+/* bf16 or x's dtype (bf16 is what autocast's next Linear would cast the     */
+/* fp32 output to, rounded once).  fwd also writes rstd (rows,) fp32 for the */
+/* backward.  bwd: dx = rstd (g - xh mean(g xh)) with g = dy w, xh = x rstd, */
+/* and dw = sum over rows of dy xh in a fixed order: per-CTA column partials */
+/* in `partials` (screen_rmsnorm_partials(rows) rows of D floats), summed by  */
+/* a second pass.                                                            */
+/* ------------------------------------------------------------------------ */
+typedef struct screen_rmsnorm_args {
+  int64_t rows;
+  int32_t D;
+  int32_t x_dtype, w_dtype, y_dtype;   /* SCREEN_F32 / SCREEN_BF16           */
+  float eps;
+  const void* x;                 /* (rows, D)                                 */
+  const void* w;                 /* (D,)                                      */
+  void* y;                       /* (rows, D) fwd output                      */
+  float* rstd;                   /* (rows,) fwd output, bwd input             */
+  const void* dy;                /* (rows, D) bwd input, y_dtype              */
+  void* dx;                      /* (rows, D) bwd output, x_dtype             */
+  void* dw;                      /* (D,) bwd output, w_dtype                  */
+  float* partials;               /* bwd workspace                             */
+} screen_rmsnorm_args;
+
+SCREEN_API int64_t screen_rmsnorm_partials(int64_t rows);
+SCREEN_API int screen_rmsnorm_fwd(const screen_rmsnorm_args* a, screen_stream_t stream);
+SCREEN_API int screen_rmsnorm_bwd(const screen_rmsnorm_args* a, screen_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Stand-alone TanhNorm (multiscreen/norm.py:8-25) over contiguous rows of   */

@@ -76,6 +76,15 @@ class XentArgs(ctypes.Structure):
     ]
 
 
+class RmsNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", c_int64), ("D", c_int32), ("x_dtype", c_int32), ("w_dtype", c_int32),
+        ("y_dtype", c_int32), ("eps", c_float),
+        ("x", c_void_p), ("w", c_void_p), ("y", c_void_p), ("rstd", c_void_p),
+        ("dy", c_void_p), ("dx", c_void_p), ("dw", c_void_p), ("partials", c_void_p),
+    ]
+
+
 class KVCacheDesc(ctypes.Structure):
     _fields_ = [
         ("k_pages", c_void_p), ("v_pages", c_void_p), ("block_table", c_void_p),
@@ -111,9 +120,10 @@ EXPORTED = (
     "screen_tanhnorm_bwd", "screen_strerror", "screen_version", "screen_sizeof_args",
     "screen_last_cuda_error", "screen_decode_noalloc", "screen_fwd_workspace_size",
     "screen_device_status", "screen_dropout_bits", "screen_rows_linear",
-    "screen_cross_entropy_fwd", "screen_cross_entropy_bwd",
+    "screen_cross_entropy_fwd", "screen_cross_entropy_bwd", "screen_rmsnorm_partials",
+    "screen_rmsnorm_fwd", "screen_rmsnorm_bwd",
 )
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 _lib = None
 
@@ -147,6 +157,10 @@ def load() -> ctypes.CDLL:
     lib.screen_rows_linear.argtypes = [P(RowsLinearArgs), c_void_p]
     lib.screen_cross_entropy_fwd.argtypes = [P(XentArgs), c_void_p]
     lib.screen_cross_entropy_bwd.argtypes = [P(XentArgs), c_void_p]
+    lib.screen_rmsnorm_partials.argtypes = [c_int64]
+    lib.screen_rmsnorm_partials.restype = c_int64
+    lib.screen_rmsnorm_fwd.argtypes = [P(RmsNormArgs), c_void_p]
+    lib.screen_rmsnorm_bwd.argtypes = [P(RmsNormArgs), c_void_p]
     lib.screen_dropout_bits.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.c_uint32]
     lib.screen_dropout_bits.restype = ctypes.c_uint32
@@ -158,7 +172,7 @@ def load() -> ctypes.CDLL:
     if lib.screen_version() != ABI_VERSION:
         raise RuntimeError("libscreening_b200.so ABI version mismatch; rebuild it")
     for i, st in enumerate((FwdArgs, BwdArgs, KVCacheDesc, KVAppendArgs, DecodeArgs,
-                            RowsLinearArgs, XentArgs)):
+                            RowsLinearArgs, XentArgs, RmsNormArgs)):
         if lib.screen_sizeof_args(i) != ctypes.sizeof(st):
             raise RuntimeError(f"struct {st.__name__} size differs from the C header; rebuild")
     _lib = lib
@@ -242,6 +256,37 @@ def cross_entropy_fwd(logits, labels, ignore_index=-100):
                  ld=logits.stride(0), labels=_ptr(labels), lse=_ptr(lse), loss=_ptr(loss))
     _check(load().screen_cross_entropy_fwd(ctypes.byref(a), _stream(logits.device)))
     return lse, loss
+
+
+def rmsnorm_fwd(x, w, eps, out_dtype):
+    """RMSNorm rows of x (.., D) with weight w (D,): returns (y, rstd); y in
+    out_dtype (bf16, or x's dtype), rstd (rows,) fp32."""
+    _require_cuda(x, w)
+    D = x.shape[-1]
+    rows = x.numel() // D
+    y = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+    a = RmsNormArgs(rows=rows, D=D, x_dtype=_dtype_code(x), w_dtype=_dtype_code(w),
+                    y_dtype=_dtype_code(y), eps=float(eps), x=_ptr(x), w=_ptr(w), y=_ptr(y),
+                    rstd=_ptr(rstd))
+    _check(load().screen_rmsnorm_fwd(ctypes.byref(a), _stream(x.device)))
+    return y, rstd
+
+
+def rmsnorm_bwd(x, w, rstd, dy):
+    """Gradients (dx in x's dtype, dw in w's dtype) of rmsnorm_fwd for dy."""
+    D = x.shape[-1]
+    rows = x.numel() // D
+    lib = load()
+    dx = torch.empty_like(x)
+    dw = torch.empty_like(w)
+    part = torch.empty(int(lib.screen_rmsnorm_partials(rows)), D, dtype=torch.float32,
+                       device=x.device)
+    a = RmsNormArgs(rows=rows, D=D, x_dtype=_dtype_code(x), w_dtype=_dtype_code(w),
+                    y_dtype=_dtype_code(dy), x=_ptr(x), w=_ptr(w), rstd=_ptr(rstd),
+                    dy=_ptr(dy), dx=_ptr(dx), dw=_ptr(dw), partials=_ptr(part))
+    _check(lib.screen_rmsnorm_bwd(ctypes.byref(a), _stream(x.device)))
+    return dx, dw
 
 
 def cross_entropy_bwd(logits, labels, lse, dscale, ignore_index=-100):

@@ -140,6 +140,7 @@ int64_t screen_sizeof_args(int which) {
     case 4: return (int64_t)sizeof(screen_decode_args);
     case 5: return (int64_t)sizeof(screen_rows_linear_args);
     case 6: return (int64_t)sizeof(screen_xent_args);
+    case 7: return (int64_t)sizeof(screen_rmsnorm_args);
     default: return -1;
   }
 }

@@ -186,3 +186,52 @@ def tanh_norm(x: torch.Tensor, eps: float = 1e-8) -> torch.Tensor:
     xx = x.float() if x.dtype == torch.float16 else x
     y = TanhNormFn.apply(xx, float(eps))
     return y if y.dtype == out_dtype else y.to(out_dtype)
+
+
+def rms_eps(norm: torch.nn.RMSNorm, x: torch.Tensor) -> float:
+    """nn.RMSNorm's eps.  None means the machine epsilon of the type torch
+    computes in, float32 for bf16 / fp16 / fp32 inputs (not the input
+    dtype's: bf16's would be 2^-7)."""
+    if norm.eps is not None:
+        return float(norm.eps)
+    return float(torch.finfo(torch.float64 if x.dtype == torch.float64 else torch.float32).eps)
+
+
+class RMSNormFn(torch.autograd.Function):
+    """RMSNorm forward / backward on the library's kernels (fp32 math; the
+    weight gradient summed in a fixed order)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps, out_dtype):
+        y, rstd = _lib.rmsnorm_fwd(x, weight, eps, out_dtype)
+        ctx.save_for_backward(x, weight, rstd)
+        ctx.out_dtype = out_dtype
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, rstd = ctx.saved_tensors
+        dx, dw = _lib.rmsnorm_bwd(x, weight, rstd, dy.to(ctx.out_dtype).contiguous())
+        return dx, dw, None, None
+
+
+def rms_norm(norm: torch.nn.RMSNorm, x: torch.Tensor) -> torch.Tensor:
+    """`norm(x)` for the blocks' pre-norms (nn.RMSNorm over the last dim).
+    On CUDA with fp32 / bf16 rows of a length that is a multiple of 8 (up to
+    2048) it runs the fused kernels; under bf16 autocast it returns the bf16
+    row the next Linear would cast the fp32 result to (the same rounding).
+    Other cases (CPU tensors, fp16, other shapes) call the module."""
+    w = norm.weight
+    D = x.shape[-1]
+    if not (x.is_cuda and w is not None and x.dtype in (torch.float32, torch.bfloat16) and
+            w.dtype in (torch.float32, torch.bfloat16) and D % 8 == 0 and D <= 2048 and
+            tuple(norm.normalized_shape) == (D,) and x.is_contiguous() and
+            x.data_ptr() % 16 == 0):
+        return norm(x)
+    if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+        out_dtype = torch.bfloat16
+    else:
+        out_dtype = torch.promote_types(x.dtype, w.dtype)
+        if out_dtype != x.dtype:
+            return norm(x)
+    return RMSNormFn.apply(x, w, rms_eps(norm, x), out_dtype)

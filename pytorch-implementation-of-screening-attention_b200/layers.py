@@ -1,13 +1,15 @@
 """Pre-norm blocks around ScreeningAttention -- drop-ins for
 multiscreen/layers.py:15-144 (same constructor arguments, submodule names
-and therefore state_dict keys).  RMSNorm, the FFN and the residuals stay in
-PyTorch; the attention runs on the fused kernels."""
+and therefore state_dict keys).  The FFN and the residuals stay in
+PyTorch; the attention and the RMSNorms (functional.rms_norm, over the
+nn.RMSNorm modules' weights) run on the library's kernels."""
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
 
 from .attention import ScreeningAttention
+from .functional import rms_norm
 
 
 def _ffn(d_model: int, ffn_dim: int, dropout: float) -> nn.Sequential:
@@ -34,9 +36,9 @@ class MultiscreenBlock(nn.Module):
         self.ffn = _ffn(d_model, ffn_dim, dropout)
 
     def forward(self, x: torch.Tensor, key_padding_mask: torch.Tensor | None = None) -> torch.Tensor:
-        normed = self.norm1(x)
+        normed = rms_norm(self.norm1, x)
         x = x + self.attn(normed, normed, normed, key_padding_mask=key_padding_mask)
-        x = x + self.ffn(self.norm2(x))
+        x = x + self.ffn(rms_norm(self.norm2, x))
         return x
 
 
@@ -60,9 +62,9 @@ class MultiscreenDecoderLayer(nn.Module):
     def forward(self, x: torch.Tensor, memory: torch.Tensor,
                 tgt_key_padding_mask: torch.Tensor | None = None,
                 memory_key_padding_mask: torch.Tensor | None = None) -> torch.Tensor:
-        normed = self.norm1(x)
+        normed = rms_norm(self.norm1, x)
         x = x + self.self_attn(normed, normed, normed, key_padding_mask=tgt_key_padding_mask)
-        normed = self.norm2(x)
+        normed = rms_norm(self.norm2, x)
         x = x + self.cross_attn(normed, memory, memory, key_padding_mask=memory_key_padding_mask)
-        x = x + self.ffn(self.norm3(x))
+        x = x + self.ffn(rms_norm(self.norm3, x))
         return x

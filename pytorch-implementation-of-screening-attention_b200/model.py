@@ -13,7 +13,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib
-from .functional import cross_entropy
+from .functional import cross_entropy, rms_eps, rms_norm
 from .kv_cache import PagedKVCache
 from .layers import MultiscreenBlock
 from .sequence_parallel import current_shard
@@ -34,13 +34,7 @@ def _sharded_mean_ce(logits, labels, shard):
     return (s + (tot[0] - s.detach())) / tot[1]
 
 
-def _rms_eps(norm: nn.RMSNorm, x: torch.Tensor) -> float:
-    """nn.RMSNorm's eps.  None means the machine epsilon of the type torch
-    computes in, float32 for bf16 / fp16 / fp32 inputs (not the input
-    dtype's: bf16's would be 2^-7)."""
-    if norm.eps is not None:
-        return float(norm.eps)
-    return float(torch.finfo(torch.float64 if x.dtype == torch.float64 else torch.float32).eps)
+_rms_eps = rms_eps
 
 
 class MultiscreenLM(nn.Module):
@@ -80,7 +74,7 @@ class MultiscreenLM(nn.Module):
         x = self.emb_dropout(self.token_emb(input_ids) + self.pos_emb(positions))
         for block in self.blocks:
             x = block(x, key_padding_mask=key_padding_mask)
-        x = self.norm(x)
+        x = rms_norm(self.norm, x)
         logits, lpad = self._lm_logits(x)
         result = {"logits": logits}
         if labels is not None:
@@ -139,9 +133,9 @@ class MultiscreenLM(nn.Module):
         positions = torch.arange(off, off + T, device=input_ids.device).unsqueeze(0)
         x = self.emb_dropout(self.token_emb(input_ids) + self.pos_emb(positions))
         for li, blk in enumerate(self.blocks):
-            x = x + blk.attn.prefill(blk.norm1(x), cache, li)
-            x = x + blk.ffn(blk.norm2(x))
-        return self.lm_head(self.norm(x[:, -1:]))[:, -1]
+            x = x + blk.attn.prefill(rms_norm(blk.norm1, x), cache, li)
+            x = x + blk.ffn(rms_norm(blk.norm2, x))
+        return self.lm_head(rms_norm(self.norm, x[:, -1:].contiguous()))[:, -1]
 
     @torch.no_grad()
     def decode_step(self, tokens: torch.Tensor, position, cache: PagedKVCache,

@@ -28,7 +28,7 @@ def test_struct_sizes_and_version(ms):
     assert lib.screen_version() == ms._lib.ABI_VERSION
     L = ms._lib
     mirrors = (L.FwdArgs, L.BwdArgs, L.KVCacheDesc, L.KVAppendArgs, L.DecodeArgs,
-               L.RowsLinearArgs, L.XentArgs)
+               L.RowsLinearArgs, L.XentArgs, L.RmsNormArgs)
     for i, st in enumerate(mirrors):
         assert lib.screen_sizeof_args(i) == ctypes.sizeof(st), st.__name__
     assert lib.screen_sizeof_args(len(mirrors)) == -1
