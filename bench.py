@@ -1182,10 +1182,18 @@ def run_cfg3(args, rank, world, local):
             "kernel_ms": kt, "tflops": tflops,
             "tile_stats": {"fwd_blocks_in_window": visited, "fwd_blocks_live": live},
             "cpu_baseline": cpu,
-            "e2e": {"value": tokens_per_step / (e2e_ms / 1e3), "unit": "tokens/s",
+            # the two input pipelines, each timed over K steps with the copy
+            # and the read-back inside; the line reports the faster (at 8
+            # ranks the copy engine's H2D copy and NCCL's traffic contend,
+            # and the serial order wins)
+            "e2e": {"value": tokens_per_step / (min(e2e_ms, e2e_serial_ms) / 1e3),
+                    "unit": "tokens/s",
                     "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
                     "h2d_gbs_measured": h2d_gbs, "pinned": bool(x_host.is_pinned()),
-                    "input_pipeline": "next step's H2D copy on a copy stream during this step",
+                    "input_pipeline": ("next step's H2D copy on a copy stream during this step"
+                                       if e2e_ms <= e2e_serial_ms else
+                                       "serial: H2D copy, step, loss read-back"),
+                    "pipelined_value": tokens_per_step / (e2e_ms / 1e3),
                     "serial_value": tokens_per_step / (e2e_serial_ms / 1e3)},
             "weak_scaling": weak,
             "clocks": clk.summary(),
