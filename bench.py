@@ -6,9 +6,9 @@ w_h ~ U[256,4096] (seeded).  One step = module forward + backward (q/k/v/out
 projections on cuBLAS, the screening core on this repo's kernels).  With N
 GPUs the global batch of 8 is split over the ranks (8/N sequences each:
 strong scaling, batch sharding) and the projection-weight gradients are
-all-reduced over NCCL in buckets that overlap the backward (DDP), as
-data-parallel training does.  A weak-scaling run (8 sequences per rank) is
-reported beside it.
+averaged over NCCL as data-parallel training does (the out_proj bucket on a
+side stream during the screening backward); the whole step is one CUDA
+graph.  A weak-scaling run (8 sequences per rank) is reported beside it.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload cfg3|decode|prefill|lm|generate]
