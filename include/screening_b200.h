@@ -334,6 +334,20 @@ SCREEN_API int screen_tanhnorm_bwd(int32_t dtype, int64_t rows, int32_t D, float
                         screen_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Per-head parameter transforms of ScreeningAttention, all heads in one     */
+/* launch: r = exp(s_r) + 1 and w = exp(s_v) + 1 (multiscreen/attention.py:   */
+/* 164-165; there they are four PyTorch ops per step, plus the casts of a     */
+/* bf16 module).  s_r, s_v: H values of `dtype`; r, w: H fp32.  The backward  */
+/* writes ds_r = dr exp(s_r), ds_v = dw exp(s_v) in `dtype`; a null dr (dw)   */
+/* leaves ds_r (ds_v) unwritten.                                             */
+/* ------------------------------------------------------------------------ */
+SCREEN_API int screen_head_params_fwd(int32_t dtype, int32_t H, const void* s_r, const void* s_v,
+                                      float* r, float* w, screen_stream_t stream);
+SCREEN_API int screen_head_params_bwd(int32_t dtype, int32_t H, const void* s_r, const void* s_v,
+                                      const float* dr, const float* dw, void* ds_r, void* ds_v,
+                                      screen_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Misc.                                                                     */
 /* ------------------------------------------------------------------------ */
 SCREEN_API const char* screen_strerror(int status);

@@ -121,7 +121,8 @@ EXPORTED = (
     "screen_last_cuda_error", "screen_decode_noalloc", "screen_fwd_workspace_size",
     "screen_device_status", "screen_dropout_bits", "screen_rows_linear",
     "screen_cross_entropy_fwd", "screen_cross_entropy_bwd", "screen_rmsnorm_partials",
-    "screen_rmsnorm_fwd", "screen_rmsnorm_bwd",
+    "screen_rmsnorm_fwd", "screen_rmsnorm_bwd", "screen_head_params_fwd",
+    "screen_head_params_bwd",
 )
 ABI_VERSION = 5
 
@@ -161,6 +162,10 @@ def load() -> ctypes.CDLL:
     lib.screen_rmsnorm_partials.restype = c_int64
     lib.screen_rmsnorm_fwd.argtypes = [P(RmsNormArgs), c_void_p]
     lib.screen_rmsnorm_bwd.argtypes = [P(RmsNormArgs), c_void_p]
+    lib.screen_head_params_fwd.argtypes = [c_int32, c_int32, c_void_p, c_void_p, c_void_p,
+                                           c_void_p, c_void_p]
+    lib.screen_head_params_bwd.argtypes = [c_int32, c_int32, c_void_p, c_void_p, c_void_p,
+                                           c_void_p, c_void_p, c_void_p, c_void_p]
     lib.screen_dropout_bits.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.c_uint32]
     lib.screen_dropout_bits.restype = ctypes.c_uint32
@@ -503,3 +508,32 @@ def screen_tanhnorm_backward(x, dy, eps=1e-8):
     _check(lib.screen_tanhnorm_bwd(_dtype_code(xc), xc.numel() // max(D, 1), D, float(eps),
                                    _ptr(xc), _ptr(dyc), _ptr(dx), _stream(x.device)))
     return dx
+
+
+def head_params_fwd(s_r, s_v):
+    """(r, w) = (exp(s_r) + 1, exp(s_v) + 1) as fp32 (H,) tensors, one launch."""
+    _require_cuda(s_r, s_v)
+    lib = load()
+    sr, sv = s_r.contiguous(), s_v.to(s_r.dtype).contiguous()
+    H = sr.numel()
+    r = torch.empty(H, dtype=torch.float32, device=sr.device)
+    w = torch.empty(H, dtype=torch.float32, device=sr.device)
+    _check(lib.screen_head_params_fwd(_dtype_code(sr), H, _ptr(sr), _ptr(sv), _ptr(r), _ptr(w),
+                                      _stream(sr.device)))
+    return r, w
+
+
+def head_params_bwd(s_r, s_v, dr, dw):
+    """(ds_r, ds_v) = (dr exp(s_r), dw exp(s_v)) in the parameters' dtype; a
+    None gradient in gives None out."""
+    _require_cuda(s_r, s_v)
+    lib = load()
+    sr, sv = s_r.contiguous(), s_v.to(s_r.dtype).contiguous()
+    H = sr.numel()
+    drc = None if dr is None else dr.float().contiguous()
+    dwc = None if dw is None else dw.float().contiguous()
+    ds_r = None if drc is None else torch.empty_like(sr)
+    ds_v = None if dwc is None else torch.empty_like(sr)
+    _check(lib.screen_head_params_bwd(_dtype_code(sr), H, _ptr(sr), _ptr(sv), _ptr(drc),
+                                      _ptr(dwc), _ptr(ds_r), _ptr(ds_v), _stream(sr.device)))
+    return ds_r, ds_v

@@ -17,7 +17,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib
-from .functional import screening_attention, screening_attention_packed
+from .functional import head_params, screening_attention, screening_attention_packed
 from .norm import TanhNorm
 from .sequence_parallel import current_shard, screening_attention_sharded
 
@@ -58,6 +58,11 @@ class ScreeningAttention(nn.Module):
         """r = exp(s_r) + 1 (attention.py:165), float32."""
         return torch.exp(self.s_r.float()) + 1.0
 
+    def _head_params(self):
+        """(r, w) as above, both transforms in one launch (and one in the
+        backward) on CUDA."""
+        return head_params(self.s_r, self.s_v)
+
     def _qkv(self, query, key, value):
         B, Tq, _ = query.shape
         Tk = key.shape[1]
@@ -91,7 +96,7 @@ class ScreeningAttention(nn.Module):
             # causal self-attention of one block of a sequence-sharded input:
             # the K/V halo before the block comes from the previous ranks
             q, k, v = self._qkv(query, key, value)
-            y = screening_attention_sharded(q, k, v, self.sharpness(), self.window(),
+            y = screening_attention_sharded(q, k, v, *self._head_params(),
                                             key_padding_mask=key_padding_mask, eps=self.eps,
                                             shard=shard)
         elif query is key and key is value:
@@ -100,13 +105,13 @@ class ScreeningAttention(nn.Module):
             H, D = self.num_heads, self.head_dim
             wqkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
             qkv = F.linear(query, wqkv).view(B, Tq, 3, H, D)
-            y = screening_attention_packed(qkv, self.sharpness(), self.window(),
+            y = screening_attention_packed(qkv, *self._head_params(),
                                            causal=self.causal,
                                            key_padding_mask=key_padding_mask, eps=self.eps,
                                            dropout_p=p)
         else:
             q, k, v = self._qkv(query, key, value)
-            y = screening_attention(q, k, v, self.sharpness(), self.window(), causal=self.causal,
+            y = screening_attention(q, k, v, *self._head_params(), causal=self.causal,
                                     key_padding_mask=key_padding_mask, eps=self.eps,
                                     dropout_p=p)
         return self.out_proj(y.reshape(B, Tq, self.d_model))
@@ -131,10 +136,10 @@ class ScreeningAttention(nn.Module):
                 pos = torch.full((B,), T - keep, dtype=torch.int32, device=x.device)
                 cache.append(layer, k[:, T - keep:], v[:, T - keep:], pos, eps=self.eps)
         if shard is not None:
-            y = screening_attention_sharded(q, k, v, self.sharpness(), self.window(),
+            y = screening_attention_sharded(q, k, v, *self._head_params(),
                                             eps=self.eps, shard=shard)
         else:
-            y = screening_attention(q, k, v, self.sharpness(), self.window(), causal=True,
+            y = screening_attention(q, k, v, *self._head_params(), causal=True,
                                     eps=self.eps)
         return self.out_proj(y.reshape(B, T, self.d_model))
 

@@ -324,4 +324,25 @@ int screen_tanhnorm_bwd(int32_t dtype, int64_t rows, int32_t D, float eps, const
   return check_launch();
 }
 
+int screen_head_params_fwd(int32_t dtype, int32_t H, const void* s_r, const void* s_v,
+                           float* r, float* w, screen_stream_t stream) {
+  if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;
+  if (H < 0) return SCREEN_ERR_INVALID_ARG;
+  if (H == 0) return SCREEN_OK;
+  if (!s_r || !s_v || !r || !w) return SCREEN_ERR_INVALID_ARG;
+  head_params_fwd(dtype, H, s_r, s_v, r, w, (cudaStream_t)stream);
+  return check_launch();
+}
+
+int screen_head_params_bwd(int32_t dtype, int32_t H, const void* s_r, const void* s_v,
+                           const float* dr, const float* dw, void* ds_r, void* ds_v,
+                           screen_stream_t stream) {
+  if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;
+  if (H < 0) return SCREEN_ERR_INVALID_ARG;
+  if (H == 0 || (!dr && !dw)) return SCREEN_OK;
+  if (!s_r || !s_v || (dr && !ds_r) || (dw && !ds_v)) return SCREEN_ERR_INVALID_ARG;
+  head_params_bwd(dtype, H, s_r, s_v, dr, dw, ds_r, ds_v, (cudaStream_t)stream);
+  return check_launch();
+}
+
 }  // extern "C"

@@ -358,6 +358,51 @@ void reduce_param_grads(const float* part_r, const float* part_w, long long P, i
 }
 
 // ---------------------------------------------------------------------------
+// The module's parameter transforms r = exp(s_r) + 1, w = exp(s_v) + 1
+// (attention.py:164-165) for all heads in one launch, and their backward
+// ds = d exp(s) in the parameters' dtype (one thread per head and parameter).
+// ---------------------------------------------------------------------------
+namespace {
+__device__ __forceinline__ float load_param(const void* p, int dtype, int i) {
+  return dtype == SCREEN_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i])
+                              : reinterpret_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void store_param(void* p, int dtype, int i, float v) {
+  if (dtype == SCREEN_BF16)
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<float*>(p)[i] = v;
+}
+__global__ void head_params_fwd_kernel(int dtype, int H, const void* s_r, const void* s_v,
+                                       float* r, float* w) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < H) r[i] = expf(load_param(s_r, dtype, i)) + 1.0f;
+  else if (i < 2 * H) w[i - H] = expf(load_param(s_v, dtype, i - H)) + 1.0f;
+}
+__global__ void head_params_bwd_kernel(int dtype, int H, const void* s_r, const void* s_v,
+                                       const float* dr, const float* dw, void* ds_r, void* ds_v) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < H) {
+    if (dr) store_param(ds_r, dtype, i, dr[i] * expf(load_param(s_r, dtype, i)));
+  } else if (i < 2 * H) {
+    if (dw) store_param(ds_v, dtype, i - H, dw[i - H] * expf(load_param(s_v, dtype, i - H)));
+  }
+}
+}  // namespace
+
+void head_params_fwd(int dtype, int H, const void* s_r, const void* s_v, float* r, float* w,
+                     cudaStream_t s) {
+  const int n = 2 * H, th = n < 256 ? ((n + 31) / 32) * 32 : 256;
+  head_params_fwd_kernel<<<(n + th - 1) / th, th, 0, s>>>(dtype, H, s_r, s_v, r, w);
+}
+
+void head_params_bwd(int dtype, int H, const void* s_r, const void* s_v, const float* dr,
+                     const float* dw, void* ds_r, void* ds_v, cudaStream_t s) {
+  const int n = 2 * H, th = n < 256 ? ((n + 31) / 32) * 32 : 256;
+  head_params_bwd_kernel<<<(n + th - 1) / th, th, 0, s>>>(dtype, H, s_r, s_v, dr, dw, ds_r, ds_v);
+}
+
+// ---------------------------------------------------------------------------
 // Longest-processing-time-first CTA order.  Under a causal window the CTAs of
 // one launch carry very different numbers of tiles (a head with w = 4096 at
 // the end of the sequence: 66 tiles; a head with w = 256: 6); launched in

@@ -29,6 +29,34 @@ def _dropout_args(p: float, seed: int | None):
     return (_lib.dropout_threshold(p), int(seed))
 
 
+class HeadParamsFn(torch.autograd.Function):
+    """(s_r, s_v) -> (r, w) = (exp(s_r) + 1, exp(s_v) + 1) as fp32, the
+    module's parameter transforms (multiscreen/attention.py:164-165), forward
+    and backward one launch each instead of a cast, an exp and an add per
+    parameter."""
+
+    @staticmethod
+    def forward(ctx, s_r, s_v):
+        r, w = _lib.head_params_fwd(s_r, s_v)
+        ctx.save_for_backward(s_r, s_v)
+        return r, w
+
+    @staticmethod
+    def backward(ctx, dr, dw):
+        s_r, s_v = ctx.saved_tensors
+        ds_r, ds_v = _lib.head_params_bwd(s_r, s_v, dr if ctx.needs_input_grad[0] else None,
+                                          dw if ctx.needs_input_grad[1] else None)
+        return ds_r, ds_v
+
+
+def head_params(s_r: torch.Tensor, s_v: torch.Tensor):
+    """(r, w) for the kernels from the module's s_r, s_v (H,) parameters."""
+    if s_r.is_cuda and s_v.is_cuda and s_r.dtype == s_v.dtype and \
+            s_r.dtype in (torch.float32, torch.bfloat16):
+        return HeadParamsFn.apply(s_r, s_v)
+    return torch.exp(s_r.float()) + 1.0, torch.exp(s_v.float()) + 1.0
+
+
 class ScreenFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, r, w, causal, key_padding_mask, eps, q_offset, dropout=None):

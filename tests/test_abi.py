@@ -71,3 +71,10 @@ def test_validation_before_any_launch(ms):
     assert lib.screen_tanhnorm_fwd(7, 4, 24, 1e-8, None, None, None) == -3
     assert lib.screen_tanhnorm_fwd(L.F32, 4, 0, 1e-8, None, None, None) == -1
     assert lib.screen_tanhnorm_fwd(L.F32, 0, 64, 1e-8, None, None, None) == 0
+    # per-head parameter transforms
+    assert lib.screen_head_params_fwd(7, 4, None, None, None, None, None) == -3
+    assert lib.screen_head_params_fwd(L.BF16, -1, None, None, None, None, None) == -1
+    assert lib.screen_head_params_fwd(L.BF16, 0, None, None, None, None, None) == 0
+    assert lib.screen_head_params_fwd(L.F32, 4, None, None, None, None, None) == -1
+    assert lib.screen_head_params_bwd(L.F32, 4, None, None, None, None, None, None, None) == 0
+    assert lib.screen_head_params_bwd(L.F32, 4, 256, 256, 512, None, None, None, None) == -1
