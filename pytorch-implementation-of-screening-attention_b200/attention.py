@@ -63,16 +63,23 @@ class ScreeningAttention(nn.Module):
         backward) on CUDA."""
         return head_params(self.s_r, self.s_v)
 
-    def _qkv(self, query, key, value):
+    def _wqkv(self, gamma: torch.Tensor | None = None) -> torch.Tensor:
+        """[W_q; W_k; W_v] (3 d_model, d_model), its input columns scaled by
+        `gamma` (an RMSNorm weight absorbed into the projections) if given."""
+        wqkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
+        return wqkv if gamma is None else wqkv * gamma
+
+    def _qkv(self, query, key, value, gamma: torch.Tensor | None = None):
         B, Tq, _ = query.shape
         Tk = key.shape[1]
         H, D = self.num_heads, self.head_dim
         if query is key and key is value:
             # self-attention: one GEMM for the three projections; q, k, v are
             # strided (B,T,H,D) views the kernel reads in place
-            wqkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
-            qkv = F.linear(query, wqkv).view(B, Tq, 3, H, D)
+            qkv = F.linear(query, self._wqkv(gamma)).view(B, Tq, 3, H, D)
             return qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+        if gamma is not None:
+            raise ValueError("an absorbed RMSNorm applies to self-attention only")
         q = self.q_proj(query).view(B, Tq, H, D)
         k = self.k_proj(key).view(B, Tk, H, D)
         v = self.v_proj(value).view(B, Tk, H, D)
@@ -86,47 +93,71 @@ class ScreeningAttention(nn.Module):
                 key_padding_mask: torch.Tensor | None = None) -> torch.Tensor:
         """query (B,T_q,d_model), key/value (B,T_k,d_model),
         key_padding_mask (B,T_k) bool, True = ignore.  Returns (B,T_q,d_model)."""
+        if query is key and key is value:
+            return self._self_attention(query, None, key_padding_mask)
         p = self._dropout_p()
         B, Tq, _ = query.shape
+        q, k, v = self._qkv(query, key, value)
+        y = screening_attention(q, k, v, *self._head_params(), causal=self.causal,
+                                key_padding_mask=key_padding_mask, eps=self.eps,
+                                dropout_p=p)
+        return self.out_proj(y.reshape(B, Tq, self.d_model))
+
+    def forward_rmsnormed(self, x: torch.Tensor, norm: nn.RMSNorm,
+                          key_padding_mask: torch.Tensor | None = None) -> torch.Tensor:
+        """self.forward(n, n, n) with n = norm(x) (the pre-norm blocks'
+        `self.attn(self.norm1(x), ...)`, multiscreen/layers.py:73-74), with the
+        RMSNorm absorbed into the QKV GEMM instead of run as a pass over x.
+
+        RMSNorm multiplies token t's row by rstd_t > 0 and every feature c by
+        weight_c.  rstd_t scales q_t, k_t and v_t of every head alike, and
+        the unit normalisation of each head's rows (attention.py:156-158)
+        divides it out again, so the output only depends on x diag(weight):
+        q, k, v = x (W diag(weight))^T give the same attention, and the same
+        gradients for x, weight and W (the loss does not depend on rstd).
+        The one difference is the eps clamp of that normalisation: a head row
+        whose norm falls below eps (1e-8) is scaled differently."""
+        return self._self_attention(x, norm.weight, key_padding_mask)
+
+    def _self_attention(self, x, gamma, key_padding_mask):
+        p = self._dropout_p()
+        B, Tq, _ = x.shape
         shard = current_shard() if self.causal else None
-        if shard is not None and query is key and key is value:
+        if shard is not None:
             if p > 0:
                 raise NotImplementedError(
                     "attention dropout with a sequence-sharded input is not implemented")
             # causal self-attention of one block of a sequence-sharded input:
             # the K/V halo before the block comes from the previous ranks
-            q, k, v = self._qkv(query, key, value)
+            q, k, v = self._qkv(x, x, x, gamma)
             y = screening_attention_sharded(q, k, v, *self._head_params(),
                                             key_padding_mask=key_padding_mask, eps=self.eps,
                                             shard=shard)
-        elif query is key and key is value:
-            # self-attention: one GEMM for the three projections; the kernels
-            # read q, k, v in place and write their gradients into one buffer
+        else:
+            # one GEMM for the three projections; the kernels read q, k, v in
+            # place and write their gradients into one buffer
             H, D = self.num_heads, self.head_dim
-            wqkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
-            qkv = F.linear(query, wqkv).view(B, Tq, 3, H, D)
+            qkv = F.linear(x, self._wqkv(gamma)).view(B, Tq, 3, H, D)
             y = screening_attention_packed(qkv, *self._head_params(),
                                            causal=self.causal,
                                            key_padding_mask=key_padding_mask, eps=self.eps,
                                            dropout_p=p)
-        else:
-            q, k, v = self._qkv(query, key, value)
-            y = screening_attention(q, k, v, *self._head_params(), causal=self.causal,
-                                    key_padding_mask=key_padding_mask, eps=self.eps,
-                                    dropout_p=p)
         return self.out_proj(y.reshape(B, Tq, self.d_model))
 
     # ------------------------------------------------------------------
     # KV-cached inference (used by MultiscreenLM.generate)
     # ------------------------------------------------------------------
     @torch.no_grad()
-    def prefill(self, x: torch.Tensor, cache, layer: int) -> torch.Tensor:
+    def prefill(self, x: torch.Tensor, cache, layer: int,
+                norm: nn.RMSNorm | None = None) -> torch.Tensor:
         """Causal self-attention over a whole prompt x (B,T,d) that also
         writes the prompt's last `cache.keep` unit keys/values into `cache`
         (cache None: attention only).  Inside sequence_parallel(), x is this
-        rank's block of a sharded prompt."""
+        rank's block of a sharded prompt.  With `norm`, the attention is that
+        of norm(x), the RMSNorm absorbed as in forward_rmsnormed (the cache
+        holds unit rows, which the RMSNorm's row scale does not change)."""
         B, T, _ = x.shape
-        q, k, v = self._qkv(x, x, x)
+        q, k, v = self._qkv(x, x, x, None if norm is None else norm.weight)
         shard = current_shard()
         if cache is not None:
             if shard is not None and shard.world > 1:

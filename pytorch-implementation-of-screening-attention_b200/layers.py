@@ -2,7 +2,10 @@
 multiscreen/layers.py:15-144 (same constructor arguments, submodule names
 and therefore state_dict keys).  The FFN and the residuals stay in
 PyTorch; the attention and the RMSNorms (functional.rms_norm, over the
-nn.RMSNorm modules' weights) run on the library's kernels."""
+nn.RMSNorm modules' weights) run on the library's kernels, except the norm
+in front of each self-attention, which the attention absorbs into its QKV
+GEMM (ScreeningAttention.forward_rmsnormed: the unit normalisation of q, k,
+v divides out its per-token scale)."""
 from __future__ import annotations
 
 import torch
@@ -36,8 +39,8 @@ class MultiscreenBlock(nn.Module):
         self.ffn = _ffn(d_model, ffn_dim, dropout)
 
     def forward(self, x: torch.Tensor, key_padding_mask: torch.Tensor | None = None) -> torch.Tensor:
-        normed = rms_norm(self.norm1, x)
-        x = x + self.attn(normed, normed, normed, key_padding_mask=key_padding_mask)
+        # self.attn(norm1(x), ...) with the RMSNorm absorbed into the QKV GEMM
+        x = x + self.attn.forward_rmsnormed(x, self.norm1, key_padding_mask=key_padding_mask)
         x = x + self.ffn(rms_norm(self.norm2, x))
         return x
 
@@ -62,8 +65,8 @@ class MultiscreenDecoderLayer(nn.Module):
     def forward(self, x: torch.Tensor, memory: torch.Tensor,
                 tgt_key_padding_mask: torch.Tensor | None = None,
                 memory_key_padding_mask: torch.Tensor | None = None) -> torch.Tensor:
-        normed = rms_norm(self.norm1, x)
-        x = x + self.self_attn(normed, normed, normed, key_padding_mask=tgt_key_padding_mask)
+        x = x + self.self_attn.forward_rmsnormed(x, self.norm1,
+                                                 key_padding_mask=tgt_key_padding_mask)
         normed = rms_norm(self.norm2, x)
         x = x + self.cross_attn(normed, memory, memory, key_padding_mask=memory_key_padding_mask)
         x = x + self.ffn(rms_norm(self.norm3, x))

@@ -133,7 +133,7 @@ class MultiscreenLM(nn.Module):
         positions = torch.arange(off, off + T, device=input_ids.device).unsqueeze(0)
         x = self.emb_dropout(self.token_emb(input_ids) + self.pos_emb(positions))
         for li, blk in enumerate(self.blocks):
-            x = x + blk.attn.prefill(rms_norm(blk.norm1, x), cache, li)
+            x = x + blk.attn.prefill(x, cache, li, norm=blk.norm1)
             x = x + blk.ffn(rms_norm(blk.norm2, x))
         return self.lm_head(rms_norm(self.norm, x[:, -1:].contiguous()))[:, -1]
 
