@@ -145,6 +145,33 @@ int check_launch();
 // SCREEN_ERR_CUDA on error, SCREEN_OK otherwise (defined in api.cu).
 int record_cuda_error(cudaError_t e);
 
+// Programmatic dependent launch for the chains of short kernels of a decode
+// step: a kernel launched with launch_pdl may start while the previous
+// kernel on the stream is still running; it reads nothing the previous
+// kernels write (and writes nothing) before pdl_wait(), which returns once
+// they have completed and their memory is visible.  pdl_trigger() lets the
+// next kernel start early (its CTAs are placed once every CTA of this one has
+// started).  Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Raise kernel `fn`'s dynamic shared-memory limit to `bytes` on the current
 // device.  The attribute is per device, so the call is made once per
 // (device, kernel, size) under a lock; later calls return the cached result.

@@ -56,6 +56,8 @@ __device__ __forceinline__ long long page_row(const screen_kv_cache& c, int b, i
 // ---------------------------------------------------------------------------
 template <typename T, int D>
 __global__ void kv_append_kernel(screen_kv_append_args a) {
+  pdl_wait();      // reads the previous kernels' outputs from here on
+  pdl_trigger();
   constexpr int G = D / 4;
   constexpr int RPB = 256 / G;
   const long long row = (long long)blockIdx.x * RPB + threadIdx.x / G;
@@ -128,6 +130,8 @@ __device__ __forceinline__ void store_split(const screen_decode_args& a, float* 
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_split_kernel(screen_decode_args a,
                                                            float* __restrict__ part) {
+  pdl_wait();      // reads the previous kernels' outputs from here on
+  pdl_trigger();
   constexpr int VEC = Vec16<T>::N;
   constexpr int LPK = D / VEC;      // lanes per key row
   constexpr int KPW = 32 / LPK;     // keys per warp step
@@ -293,6 +297,8 @@ __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t u) {
 template <typename T, int D>
 __global__ void __launch_bounds__(32 * (kDecConsumers + 1)) decode_bulk_kernel(
     screen_decode_args a, float* __restrict__ part, int nstages, int sk) {
+  pdl_wait();      // reads the previous kernels' outputs from here on
+  pdl_trigger();
   using namespace sm100;
   constexpr int NW = kDecConsumers;
   constexpr int SZ = (int)sizeof(T);
@@ -526,6 +532,8 @@ __global__ void __launch_bounds__(32 * (kDecConsumers + 1)) decode_bulk_kernel(
 template <typename T, int D>
 __global__ void __launch_bounds__(256) decode_finish_kernel(screen_decode_args a,
                                                             const float* __restrict__ part) {
+  pdl_wait();      // reads the previous kernels' outputs from here on
+  pdl_trigger();
   constexpr int NG = 256 / D;
   __shared__ float acc[NG][D];
   __shared__ float red[D];
@@ -561,7 +569,7 @@ void launch_append(const screen_kv_append_args& a, cudaStream_t s) {
   const long long rows = (long long)a.B * a.n_new * a.H;
   if (rows == 0) return;
   dim3 grid((unsigned)((rows + RPB - 1) / RPB), 2);
-  kv_append_kernel<T, D><<<grid, 256, 0, s>>>(a);
+  launch_pdl(kv_append_kernel<T, D>, grid, dim3(256), 0, s, a);
 }
 template <typename T, int D>
 void launch_decode(const screen_decode_args& a, float* part, cudaStream_t s) {
@@ -583,11 +591,13 @@ void launch_decode(const screen_decode_args& a, float* part, cudaStream_t s) {
     // the opt-in is per device; on failure the error stays in
     // cudaGetLastError for the entry point's launch check
     if (ensure_smem_optin((const void*)decode_bulk_kernel<T, D>, 200 << 10) != cudaSuccess) return;
-    decode_bulk_kernel<T, D><<<grid, 32 * (kDecConsumers + 1), smem, s>>>(a, part, nstages, sk);
+    launch_pdl(decode_bulk_kernel<T, D>, grid, dim3(32 * (kDecConsumers + 1)), smem, s, a, part,
+               nstages, sk);
   } else {
-    decode_split_kernel<T, D><<<grid, 128, 0, s>>>(a, part);
+    launch_pdl(decode_split_kernel<T, D>, grid, dim3(128), 0, s, a, part);
   }
-  if (a.num_splits > 1) decode_finish_kernel<T, D><<<a.B * a.H, 256, 0, s>>>(a, part);
+  if (a.num_splits > 1)
+    launch_pdl(decode_finish_kernel<T, D>, dim3(a.B * a.H), dim3(256), 0, s, a, part);
 }
 
 }  // namespace

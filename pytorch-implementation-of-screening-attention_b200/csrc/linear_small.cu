@@ -48,6 +48,10 @@ __global__ void __launch_bounds__(kWarps * 32) rows_linear_kernel(screen_rows_li
                                     : make_uint4(0, 0, 0, 0);
     }
   }
+  // the weights are not written by the kernels before this one; the input
+  // rows and the residual are
+  pdl_wait();
+  pdl_trigger();
   const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(a.x);
   const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
   // ---- stage the input rows (RMSNorm'ed when norm_w is given)
@@ -188,7 +192,9 @@ int launch_rows_linear_r(const screen_rows_linear_args& a, cudaStream_t st) {
   }
   const long long per_cta = (long long)kWarps * R;
   const unsigned grid = (unsigned)((a.N + per_cta - 1) / per_cta);
-  rows_linear_kernel<M, R><<<grid, kWarps * 32, smem, st>>>(a);
+  const cudaError_t e = launch_pdl(rows_linear_kernel<M, R>, dim3(grid), dim3(kWarps * 32), smem,
+                                   st, a);
+  if (e != cudaSuccess) return record_cuda_error(e);
   return check_launch();
 }
 
