@@ -192,9 +192,8 @@ int launch_rows_linear_r(const screen_rows_linear_args& a, cudaStream_t st) {
   }
   const long long per_cta = (long long)kWarps * R;
   const unsigned grid = (unsigned)((a.N + per_cta - 1) / per_cta);
-  const cudaError_t e = launch_pdl(rows_linear_kernel<M, R>, dim3(grid), dim3(kWarps * 32), smem,
-                                   st, a);
-  if (e != cudaSuccess) return record_cuda_error(e);
+  // a failed launch leaves its error for check_launch
+  launch_pdl(rows_linear_kernel<M, R>, dim3(grid), dim3(kWarps * 32), smem, st, a);
   return check_launch();
 }
 
