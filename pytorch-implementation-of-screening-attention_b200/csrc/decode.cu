@@ -336,6 +336,10 @@ __global__ void __launch_bounds__(32 * (kDecConsumers + 1)) decode_bulk_kernel(
     abort_s = 0;
     fence_proxy_async_smem();
   }
+  // per-head parameters and the sequence length are requested together with
+  // the query (independent loads, one memory round trip)
+  const float r = a.r[h], w = a.w[h];
+  const long long t = (long long)a.seq_lens[b] - 1;
   const T* qraw = reinterpret_cast<const T*>(a.q) + (long long)b * a.q_sb + (long long)h * D;
   float* qf = reinterpret_cast<float*>(&qc[0][0]);
   float ssq = 0.f;
@@ -350,9 +354,7 @@ __global__ void __launch_bounds__(32 * (kDecConsumers + 1)) decode_bulk_kernel(
   if (lane == 0) qsum[warp] = ssq;
   __syncthreads();
 
-  const float r = a.r[h], w = a.w[h];
   const int dmax = window_dmax(w);
-  const long long t = (long long)a.seq_lens[b] - 1;
   long long lo = t - dmax;
   if (lo < 0) lo = 0;
   const bool any = dmax >= 0 && t >= 0;
