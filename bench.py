@@ -45,10 +45,11 @@ D_MODEL, HEADS, HEAD_DIM, BATCH, SEQ = 1024, 16, 64, 8, 4096
 METRIC = "screening-attn fwd+bwd tokens/s (ScreeningAttention d=1024 H=16 D=64 causal T=4096, bf16)"
 WORKLOAD = ("cfg3: isolated ScreeningAttention d_model=1024, 16 heads x 64, causal, global batch 8 "
             "split over the GPUs, T=4096, bf16, r~U[1,2], w~U[256,4096], fwd+bwd")
-# this repo's kernels launched per cfg3 step: forward (prep, k meta, CTA
-# order, attention), backward (TanhNorm-grad prologue, aux norms, CTA order,
-# fused attention, dq finalize, dr/dw reduction)
-LAUNCHES_PER_STEP = 10
+# this repo's kernels launched per cfg3 step: forward (r / w transforms,
+# prep, k meta, CTA order, attention), backward (TanhNorm-grad prologue, aux
+# norms, CTA order, fused attention, dq finalize, dr/dw reduction, r / w
+# gradients)
+LAUNCHES_PER_STEP = 12
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
