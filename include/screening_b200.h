@@ -348,6 +348,19 @@ SCREEN_API int screen_head_params_bwd(int32_t dtype, int32_t H, const void* s_r,
                                       screen_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Backward of Y = W diag(g): a pre-attention RMSNorm weight g folded into    */
+/* the columns of the QKV projection W (rows x D, row-major).  The RMSNorm    */
+/* in front of self-attention (multiscreen/layers.py:73-74) needs no pass of  */
+/* its own: its per-token scale cancels in the unit normalisation of q, k, v  */
+/* (attention.py:156-158), so q, k, v = x (W diag(g))^T.  Writes              */
+/* dW = dY diag(g) and dg[c] = sum_o dY[o, c] W[o, c] (fixed order); a null   */
+/* dw or dg is not written.  dy, w, g, dw, dg all of `dtype`.                 */
+/* ------------------------------------------------------------------------ */
+SCREEN_API int screen_col_scale_bwd(int32_t dtype, int64_t rows, int32_t D, const void* dy,
+                                    const void* w, const void* g, void* dw, void* dg,
+                                    screen_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Misc.                                                                     */
 /* ------------------------------------------------------------------------ */
 SCREEN_API const char* screen_strerror(int status);

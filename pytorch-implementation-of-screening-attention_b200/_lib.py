@@ -122,7 +122,7 @@ EXPORTED = (
     "screen_device_status", "screen_dropout_bits", "screen_rows_linear",
     "screen_cross_entropy_fwd", "screen_cross_entropy_bwd", "screen_rmsnorm_partials",
     "screen_rmsnorm_fwd", "screen_rmsnorm_bwd", "screen_head_params_fwd",
-    "screen_head_params_bwd",
+    "screen_head_params_bwd", "screen_col_scale_bwd",
 )
 ABI_VERSION = 5
 
@@ -166,6 +166,8 @@ def load() -> ctypes.CDLL:
                                            c_void_p, c_void_p]
     lib.screen_head_params_bwd.argtypes = [c_int32, c_int32, c_void_p, c_void_p, c_void_p,
                                            c_void_p, c_void_p, c_void_p, c_void_p]
+    lib.screen_col_scale_bwd.argtypes = [c_int32, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_void_p]
     lib.screen_dropout_bits.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.c_uint32]
     lib.screen_dropout_bits.restype = ctypes.c_uint32
@@ -537,3 +539,19 @@ def head_params_bwd(s_r, s_v, dr, dw):
     _check(lib.screen_head_params_bwd(_dtype_code(sr), H, _ptr(sr), _ptr(sv), _ptr(drc),
                                       _ptr(dwc), _ptr(ds_r), _ptr(ds_v), _stream(sr.device)))
     return ds_r, ds_v
+
+
+def col_scale_bwd(dy, w, g, need_dw=True, need_dg=True):
+    """Gradients of W diag(g) (W: rows x D, g: D) for dy: (dW, dg) in the
+    common dtype of the three (None where not needed)."""
+    _require_cuda(dy, w, g)
+    lib = load()
+    dt = w.dtype
+    dyc, wc, gc = dy.to(dt).contiguous(), w.contiguous(), g.to(dt).contiguous()
+    D = wc.shape[-1]
+    rows = wc.numel() // D
+    dw = torch.empty_like(wc) if need_dw else None
+    dg = torch.empty(D, dtype=dt, device=wc.device) if need_dg else None
+    _check(lib.screen_col_scale_bwd(_dtype_code(wc), rows, D, _ptr(dyc), _ptr(wc), _ptr(gc),
+                                    _ptr(dw), _ptr(dg), _stream(wc.device)))
+    return dw, dg

@@ -17,7 +17,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib
-from .functional import head_params, screening_attention, screening_attention_packed
+from .functional import col_scale, head_params, screening_attention, screening_attention_packed
 from .norm import TanhNorm
 from .sequence_parallel import current_shard, screening_attention_sharded
 
@@ -67,7 +67,7 @@ class ScreeningAttention(nn.Module):
         """[W_q; W_k; W_v] (3 d_model, d_model), its input columns scaled by
         `gamma` (an RMSNorm weight absorbed into the projections) if given."""
         wqkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
-        return wqkv if gamma is None else wqkv * gamma
+        return wqkv if gamma is None else col_scale(wqkv, gamma)
 
     def _qkv(self, query, key, value, gamma: torch.Tensor | None = None):
         B, Tq, _ = query.shape

@@ -324,6 +324,16 @@ int screen_tanhnorm_bwd(int32_t dtype, int64_t rows, int32_t D, float eps, const
   return check_launch();
 }
 
+int screen_col_scale_bwd(int32_t dtype, int64_t rows, int32_t D, const void* dy, const void* w,
+                         const void* g, void* dw, void* dg, screen_stream_t stream) {
+  if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;
+  if (rows < 0 || D <= 0) return SCREEN_ERR_INVALID_ARG;
+  if ((!dw && !dg) || (rows == 0 && !dg)) return SCREEN_OK;
+  if (!dy || !g || (dg && !w)) return SCREEN_ERR_INVALID_ARG;
+  col_scale_bwd(dtype, rows, D, dy, w, g, dw, dg, (cudaStream_t)stream);
+  return check_launch();
+}
+
 int screen_head_params_fwd(int32_t dtype, int32_t H, const void* s_r, const void* s_v,
                            float* r, float* w, screen_stream_t stream) {
   if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;

@@ -159,13 +159,32 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(screen_rmsnorm
   }
 }
 
+// dw[d] = sum of the nblk partial rows: CTA = 32 columns x 8 row slices
+// (slice s sums partial rows s, s + 8, ...), the slices added in order, so
+// the result is deterministic and the 600-odd partial rows are read by 8
+// independent streams per column instead of one
 template <typename TW>
-__global__ void rmsnorm_dw_kernel(screen_rmsnorm_args a, int nblk) {
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d >= a.D) return;
-  float t = 0.f;
-  for (int b = 0; b < nblk; ++b) t += a.partials[(long long)b * a.D + d];
-  reinterpret_cast<TW*>(a.dw)[d] = from_f<TW>(t);
+__global__ void __launch_bounds__(256) rmsnorm_dw_kernel(screen_rmsnorm_args a, int nblk) {
+  __shared__ float red[8][33];
+  const int c = threadIdx.x & 31, sl = threadIdx.x >> 5;
+  const int d = blockIdx.x * 32 + c;
+  float t0 = 0.f, t1 = 0.f;
+  if (d < a.D) {
+    int b = sl;
+    for (; b + 8 < nblk; b += 16) {
+      t0 += a.partials[(long long)b * a.D + d];
+      t1 += a.partials[(long long)(b + 8) * a.D + d];
+    }
+    if (b < nblk) t0 += a.partials[(long long)b * a.D + d];
+  }
+  red[sl][c] = t0 + t1;
+  __syncthreads();
+  if (sl == 0 && d < a.D) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][c];
+    reinterpret_cast<TW*>(a.dw)[d] = from_f<TW>(t);
+  }
 }
 
 int grid_for(long long rows) {
@@ -204,7 +223,7 @@ int run(const screen_rmsnorm_args& a, bool bwd, cudaStream_t st) {
     if (e != cudaSuccess) return record_cuda_error(e);
   }
   rmsnorm_bwd_kernel<TX, TW, TY, NCH><<<grid, kWarps * 32, smem, st>>>(a);
-  rmsnorm_dw_kernel<TW><<<(a.D + 255) / 256, 256, 0, st>>>(a, grid);
+  rmsnorm_dw_kernel<TW><<<(a.D + 31) / 32, 256, 0, st>>>(a, grid);
   return check_launch();
 }
 

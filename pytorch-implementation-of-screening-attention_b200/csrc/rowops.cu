@@ -396,6 +396,54 @@ void head_params_fwd(int dtype, int H, const void* s_r, const void* s_v, float* 
   head_params_fwd_kernel<<<(n + th - 1) / th, th, 0, s>>>(dtype, H, s_r, s_v, r, w);
 }
 
+// ---------------------------------------------------------------------------
+// Backward of Y = W diag(g) (a norm weight g folded into the columns of a
+// projection W of `rows` x D): dW = dY diag(g), dg[c] = sum_o dY[o, c] W[o, c].
+// CTA = 32 columns x 8 row slices, slices added in a fixed order.
+// ---------------------------------------------------------------------------
+namespace {
+template <typename T>
+__global__ void __launch_bounds__(256) col_scale_bwd_kernel(long long rows, int D, const T* dy,
+                                                            const T* w, const T* g, T* dw, T* dg) {
+  __shared__ float red[8][33];
+  const int c = threadIdx.x & 31, sl = threadIdx.x >> 5;
+  const int d = blockIdx.x * 32 + c;
+  float acc = 0.f;
+  if (d < D) {
+    const float gc = to_f(g[d]);
+    for (long long o = sl; o < rows; o += 8) {
+      const long long at = o * D + d;
+      const float v = to_f(dy[at]);
+      if (dg) acc = fmaf(v, to_f(w[at]), acc);
+      if (dw) dw[at] = from_f<T>(v * gc);
+    }
+  }
+  red[sl][c] = acc;
+  __syncthreads();
+  if (dg && sl == 0 && d < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][c];
+    dg[d] = from_f<T>(t);
+  }
+}
+}  // namespace
+
+void col_scale_bwd(int dtype, long long rows, int D, const void* dy, const void* w,
+                   const void* g, void* dw, void* dg, cudaStream_t s) {
+  const unsigned grid = (unsigned)((D + 31) / 32);
+  if (dtype == SCREEN_BF16) {
+    typedef __nv_bfloat16 bf;
+    col_scale_bwd_kernel<bf><<<grid, 256, 0, s>>>(
+        rows, D, static_cast<const bf*>(dy), static_cast<const bf*>(w), static_cast<const bf*>(g),
+        static_cast<bf*>(dw), static_cast<bf*>(dg));
+  } else {
+    col_scale_bwd_kernel<float><<<grid, 256, 0, s>>>(
+        rows, D, static_cast<const float*>(dy), static_cast<const float*>(w),
+        static_cast<const float*>(g), static_cast<float*>(dw), static_cast<float*>(dg));
+  }
+}
+
 void head_params_bwd(int dtype, int H, const void* s_r, const void* s_v, const float* dr,
                      const float* dw, void* ds_r, void* ds_v, cudaStream_t s) {
   const int n = 2 * H, th = n < 256 ? ((n + 31) / 32) * 32 : 256;

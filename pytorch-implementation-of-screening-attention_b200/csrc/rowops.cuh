@@ -30,6 +30,10 @@ void tanhnorm_grad_from_y(int dtype, int D, const void* y, const float* no, cons
                           int H, float eps, cudaStream_t s);
 void reduce_param_grads(const float* part_r, const float* part_w, long long P, int H,
                         const float* w, float* dr, float* dw, cudaStream_t s);
+// backward of W diag(g): dW = dY diag(g) and dg = column sums of dY * W
+// (dw or dg null: not written); rows x D row-major, all of one dtype
+void col_scale_bwd(int dtype, long long rows, int D, const void* dy, const void* w,
+                   const void* g, void* dw, void* dg, cudaStream_t s);
 // r = exp(s_r) + 1, w = exp(s_v) + 1 per head; backward ds = d exp(s) (dr or
 // dw null: that gradient is not written)
 void head_params_fwd(int dtype, int H, const void* s_r, const void* s_v, float* r, float* w,

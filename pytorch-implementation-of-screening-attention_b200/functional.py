@@ -57,6 +57,37 @@ def head_params(s_r: torch.Tensor, s_v: torch.Tensor):
     return torch.exp(s_r.float()) + 1.0, torch.exp(s_v.float()) + 1.0
 
 
+class ColScaleFn(torch.autograd.Function):
+    """W diag(g) with its backward in one launch (dW = dY diag(g) and the
+    column sums dg = sum_o dY W): the RMSNorm weight g folded into the QKV
+    projection.  PyTorch's own backward of the broadcast product reduces the
+    columns with a two-CTA kernel (tens of microseconds per layer)."""
+
+    @staticmethod
+    def forward(ctx, w, g):
+        ctx.save_for_backward(w, g)
+        return w * g
+
+    @staticmethod
+    def backward(ctx, dy):
+        w, g = ctx.saved_tensors
+        dw, dg = _lib.col_scale_bwd(dy, w, g, ctx.needs_input_grad[0], ctx.needs_input_grad[1])
+        if dw is not None and dw.dtype != w.dtype:
+            dw = dw.to(w.dtype)
+        if dg is not None and dg.dtype != g.dtype:
+            dg = dg.to(g.dtype)
+        return dw, dg
+
+
+def col_scale(w: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+    """w * g (g over the last dimension of w)."""
+    if w.is_cuda and g.is_cuda and w.dtype == g.dtype and w.dtype in (torch.float32,
+                                                                     torch.bfloat16) \
+            and w.dim() == 2 and g.dim() == 1 and w.shape[1] == g.shape[0]:
+        return ColScaleFn.apply(w, g)
+    return w * g
+
+
 class ScreenFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, r, w, causal, key_padding_mask, eps, q_offset, dropout=None):

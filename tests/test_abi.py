@@ -78,3 +78,8 @@ def test_validation_before_any_launch(ms):
     assert lib.screen_head_params_fwd(L.F32, 4, None, None, None, None, None) == -1
     assert lib.screen_head_params_bwd(L.F32, 4, None, None, None, None, None, None, None) == 0
     assert lib.screen_head_params_bwd(L.F32, 4, 256, 256, 512, None, None, None, None) == -1
+    # folded-norm column scale backward
+    assert lib.screen_col_scale_bwd(7, 4, 8, None, None, None, None, None, None) == -3
+    assert lib.screen_col_scale_bwd(L.F32, 4, 0, None, None, None, None, None, None) == -1
+    assert lib.screen_col_scale_bwd(L.F32, 4, 8, None, None, None, None, None, None) == 0
+    assert lib.screen_col_scale_bwd(L.F32, 4, 8, None, None, None, 256, None, None) == -1

@@ -57,3 +57,22 @@ def test_prefill_absorbed_norm_matches_forward(ms):
         n = blk.norm1(x)
         b = blk.attn(n, n, n)
     assert _rel(a, b) <= 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows,D", [(768, 256), (3072, 1024), (5, 40)])
+def test_col_scale_backward_matches_torch(ms, dtype, rows, D):
+    dev = torch.device("cuda:0")
+    g0 = torch.Generator().manual_seed(rows + D)
+    w = torch.randn(rows, D, generator=g0).to(dev, dtype).requires_grad_(True)
+    g = (torch.rand(D, generator=g0) + 0.5).to(dev, dtype).requires_grad_(True)
+    dy = torch.randn(rows, D, generator=g0).to(dev, dtype)
+    y = ms.functional.col_scale(w, g)
+    y.backward(dy)
+    got = (y.detach(), w.grad.clone(), g.grad.clone())
+    w.grad = g.grad = None
+    (w.float() * g.float()).backward(dy.float())
+    tol = 1e-5 if dtype == torch.float32 else 8e-3
+    assert _rel(got[0], (w.float() * g.float()).detach()) <= tol
+    assert _rel(got[1], w.grad) <= tol
+    assert _rel(got[2], g.grad) <= tol
