@@ -226,6 +226,17 @@ SCREEN_API size_t screen_decode_workspace_size(const screen_decode_args* a);
  * then not read). */
 SCREEN_API int screen_decode(const screen_decode_args* a, screen_stream_t stream);
 
+/* screen_kv_append of one new row per sequence (ap->n_new == 1) followed by
+ * screen_decode over the same cache, as one launch where the decode kernel
+ * streams the cache pages by bulk copies: the CTA whose pages hold
+ * positions[b] writes the unit k / v rows (the same arithmetic as
+ * screen_kv_append) before it reads the page.  The per-token step of
+ * generate() (multiscreen/model.py:131-133 recomputes the whole prefix
+ * instead).  ap->cache and a->cache must be the same descriptor; the new
+ * token is normally at positions[b] == seq_lens[b] - 1. */
+SCREEN_API int screen_decode_append(const screen_kv_append_args* ap, const screen_decode_args* a,
+                                    screen_stream_t stream);
+
 /* Bytes of the static device scratch array used by screen_decode_noalloc. */
 #define SCREEN_DECODE_NOALLOC_SCRATCH_BYTES (4u << 20)
 

@@ -122,7 +122,7 @@ EXPORTED = (
     "screen_device_status", "screen_dropout_bits", "screen_rows_linear",
     "screen_cross_entropy_fwd", "screen_cross_entropy_bwd", "screen_rmsnorm_partials",
     "screen_rmsnorm_fwd", "screen_rmsnorm_bwd", "screen_head_params_fwd",
-    "screen_head_params_bwd", "screen_col_scale_bwd",
+    "screen_head_params_bwd", "screen_col_scale_bwd", "screen_decode_append",
 )
 ABI_VERSION = 5
 
@@ -168,6 +168,7 @@ def load() -> ctypes.CDLL:
                                            c_void_p, c_void_p, c_void_p, c_void_p]
     lib.screen_col_scale_bwd.argtypes = [c_int32, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_void_p]
+    lib.screen_decode_append.argtypes = [P(KVAppendArgs), P(DecodeArgs), c_void_p]
     lib.screen_dropout_bits.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.c_uint32]
     lib.screen_dropout_bits.restype = ctypes.c_uint32
@@ -486,6 +487,41 @@ def screen_decode(q, seq_lens, r, w, k_pages, v_pages, block_table, eps=1e-8, nu
     a.workspace = workspace.data_ptr()
     a.workspace_bytes = workspace.numel()
     _check(lib.screen_decode(ctypes.byref(a), _stream(dev)))
+    return y, no
+
+
+def screen_decode_append(k, v, positions, q, seq_lens, r, w, k_pages, v_pages, block_table,
+                         eps=1e-8, num_splits=1, workspace=None):
+    """screen_kv_append of one new raw k, v row per sequence (B,1,H,D) at
+    positions[b], then screen_decode of q (B,H,D) over the same cache, in one
+    launch.  Returns y (B,H,D), no (B,H)."""
+    _require_cuda(k, v, positions, q, seq_lens, r, w, k_pages, v_pages, block_table)
+    lib = load()
+    k, v = _bthd(k), _bthd(v)
+    if k.shape[1] != 1:
+        raise ValueError("screen_decode_append appends one row per sequence")
+    if k_pages.dtype != k.dtype or q.dtype != k.dtype:
+        raise TypeError("cache dtype must match q / k / v")
+    if q.stride(-1) != 1 or q.stride(-2) != q.shape[-1] or q.stride(0) % 4 or q.data_ptr() % 16:
+        q = q.contiguous()
+    B, H, D = q.shape
+    dev = q.device
+    cache = kv_desc(k_pages, v_pages, block_table)
+    ap = KVAppendArgs(dtype=_dtype_code(k), B=B, H=H, D=D, n_new=1, eps=float(eps),
+                      k=_ptr(k), k_sb=k.stride(0), k_st=k.stride(1),
+                      v=_ptr(v), v_sb=v.stride(0), v_st=v.stride(1),
+                      positions=_ptr(positions), cache=cache)
+    y = torch.empty((B, H, D), dtype=q.dtype, device=dev)
+    no = torch.empty((B, H), dtype=torch.float32, device=dev)
+    a = DecodeArgs(dtype=_dtype_code(q), B=B, H=H, D=D, num_splits=int(num_splits), eps=float(eps),
+                   q=_ptr(q), q_sb=q.stride(0), seq_lens=_ptr(seq_lens), r=_ptr(r), w=_ptr(w),
+                   cache=cache, y=_ptr(y), no=_ptr(no))
+    need = int(lib.screen_decode_workspace_size(ctypes.byref(a)))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    a.workspace = workspace.data_ptr()
+    a.workspace_bytes = workspace.numel()
+    _check(lib.screen_decode_append(ctypes.byref(ap), ctypes.byref(a), _stream(dev)))
     return y, no
 
 

@@ -195,8 +195,8 @@ class ScreeningAttention(nn.Module):
         B = qkv.shape[0]
         H, D = self.num_heads, self.head_dim
         qkv = qkv.reshape(B, 1, 3, H, D)
-        cache.append(layer, qkv[:, :, 1], qkv[:, :, 2], positions, eps=self.eps)
-        y, _ = cache.decode(layer, qkv[:, 0, 0], seq_lens,
-                            self.sharpness() if r is None else r,
-                            self.window() if w is None else w, eps=self.eps)
+        # the new token's unit k / v rows are written by the decode launch itself
+        y, _ = cache.append_decode(layer, qkv[:, :, 1], qkv[:, :, 2], positions, qkv[:, 0, 0],
+                                   seq_lens, self.sharpness() if r is None else r,
+                                   self.window() if w is None else w, eps=self.eps)
         return y.reshape(B, self.d_model)

@@ -302,6 +302,32 @@ int screen_decode(const screen_decode_args* a, screen_stream_t stream) {
   return check_launch();
 }
 
+int screen_decode_append(const screen_kv_append_args* ap, const screen_decode_args* a,
+                         screen_stream_t stream) {
+  if (!ap || !a) return SCREEN_ERR_INVALID_ARG;
+  int st = common_checks(a->dtype, a->B, a->H, 0, 0, a->D);
+  if (st) return st;
+  if (ap->n_new != 1 || ap->dtype != a->dtype || ap->B != a->B || ap->H != a->H ||
+      ap->D != a->D || a->num_splits < 1)
+    return SCREEN_ERR_INVALID_ARG;
+  // one cache: the rows are appended where the decode reads them
+  if (memcmp(&ap->cache, &a->cache, sizeof(screen_kv_cache)) != 0) return SCREEN_ERR_INVALID_ARG;
+  if ((long long)a->B * a->H == 0) return SCREEN_OK;
+  if (!a->q || !a->seq_lens || !a->r || !a->w || !a->y || !a->cache.k_pages ||
+      !a->cache.v_pages || !a->cache.block_table || a->cache.page_size <= 0 ||
+      a->cache.max_blocks <= 0 || !ap->k || !ap->v || !ap->positions)
+    return SCREEN_ERR_INVALID_ARG;
+  if (!al16(a->q) || !al16(a->cache.k_pages) || !al16(a->cache.v_pages) || !al16(a->workspace) ||
+      !al16(ap->k) || !al16(ap->v))
+    return SCREEN_ERR_ALIGNMENT;
+  if (a->q_sb % 4 != 0) return SCREEN_ERR_ALIGNMENT;
+  if (!strides_ok(ap->k_sb, ap->k_st) || !strides_ok(ap->v_sb, ap->v_st)) return SCREEN_ERR_ALIGNMENT;
+  const size_t need = screen_decode_workspace_size(a);
+  if (!a->workspace || a->workspace_bytes < need) return SCREEN_ERR_WORKSPACE;
+  decode_append(*ap, *a, reinterpret_cast<float*>(a->workspace), (cudaStream_t)stream);
+  return check_launch();
+}
+
 int screen_tanhnorm_fwd(int32_t dtype, int64_t rows, int32_t D, float eps, const void* x,
                         void* y, screen_stream_t stream) {
   if (!dtype_ok(dtype)) return SCREEN_ERR_DTYPE;

@@ -296,7 +296,8 @@ __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t u) {
 
 template <typename T, int D>
 __global__ void __launch_bounds__(32 * (kDecConsumers + 1)) decode_bulk_kernel(
-    screen_decode_args a, float* __restrict__ part, int nstages, int sk) {
+    screen_decode_args a, float* __restrict__ part, int nstages, int sk,
+    screen_kv_append_args ap, int do_append) {
   pdl_wait();      // reads the previous kernels' outputs from here on
   pdl_trigger();
   using namespace sm100;
@@ -367,6 +368,40 @@ __global__ void __launch_bounds__(32 * (kDecConsumers + 1)) decode_bulk_kernel(
   if (b1 > bhi) b1 = bhi;
   const int npages = any && b1 >= b0 ? (int)(b1 - b0 + 1) : 0;
   const int nunits = npages * subs;
+
+  if (do_append) {
+    // the newest token's unit k / v rows (the one new row of ap) go into the
+    // cache first, written by the split whose pages hold that position (the
+    // first split when the window is empty), with the arithmetic of
+    // kv_append_kernel: groups of D / 4 lanes, K rows then V rows
+    const int wsplit = any ? (int)((bhi - blo) / per) : 0;
+    constexpr int G = D / 4;
+    constexpr int NT = 2 * G < 32 ? 32 : 2 * G;   // whole warps take part in the shuffles
+    if (split == wsplit && tid < NT) {
+      const bool valid = tid < 2 * G;
+      const bool isv = tid >= G;
+      const int gl = tid % G;
+      const T* src = reinterpret_cast<const T*>(isv ? ap.v : ap.k) +
+                     (long long)b * (isv ? ap.v_sb : ap.k_sb) + (long long)h * D + gl * 4;
+      float x[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[e] = valid ? to_f(src[e]) : 0.f;
+      float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o, G);
+      const float nrm = fmaxf(sqrtf(ss), ap.eps);
+      const long long dst = valid ? page_row(ap.cache, b, ap.H, h, (long long)ap.positions[b], D)
+                                  : -1;
+      if (dst >= 0) {
+        T* out = reinterpret_cast<T*>(isv ? ap.cache.v_pages : ap.cache.k_pages) + dst + gl * 4;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) out[e] = from_f<T>(x[e] / nrm);
+      }
+      // the rows are read back below by bulk copies (the async proxy)
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
+    __syncthreads();
+  }
 
   float acc[EPL];
 #pragma unroll
@@ -573,9 +608,16 @@ void launch_append(const screen_kv_append_args& a, cudaStream_t s) {
   dim3 grid((unsigned)((rows + RPB - 1) / RPB), 2);
   launch_pdl(kv_append_kernel<T, D>, grid, dim3(256), 0, s, a);
 }
+// ap: one new k / v row per (b, h) to append before the decode (nullptr:
+// none).  The bulk-copy kernel writes it itself; the fallback path launches
+// the append kernel first.
 template <typename T, int D>
-void launch_decode(const screen_decode_args& a, float* part, cudaStream_t s) {
-  if (a.B == 0 || a.H == 0) return;
+void launch_decode(const screen_decode_args& a, float* part, cudaStream_t s,
+                   const screen_kv_append_args* ap = nullptr) {
+  if (a.B == 0 || a.H == 0) {
+    if (ap) launch_append<T, D>(*ap, s);
+    return;
+  }
   dim3 grid(a.num_splits, a.B * a.H);
   // sub-runs of sk keys: the largest power of two <= 32 dividing page_size
   int sk = 1;
@@ -594,8 +636,9 @@ void launch_decode(const screen_decode_args& a, float* part, cudaStream_t s) {
     // cudaGetLastError for the entry point's launch check
     if (ensure_smem_optin((const void*)decode_bulk_kernel<T, D>, 200 << 10) != cudaSuccess) return;
     launch_pdl(decode_bulk_kernel<T, D>, grid, dim3(32 * (kDecConsumers + 1)), smem, s, a, part,
-               nstages, sk);
+               nstages, sk, ap ? *ap : screen_kv_append_args{}, ap ? 1 : 0);
   } else {
+    if (ap) launch_append<T, D>(*ap, s);
     launch_pdl(decode_split_kernel<T, D>, grid, dim3(128), 0, s, a, part);
   }
   if (a.num_splits > 1)
@@ -639,6 +682,11 @@ int decode_device_status(bool clear) {
 void decode(const screen_decode_args& a, float* part, cudaStream_t s) {
   const int dtype = a.dtype, D = a.D;
   DEC_DISPATCH(launch_decode, a, part, s);
+}
+void decode_append(const screen_kv_append_args& ap, const screen_decode_args& a, float* part,
+                   cudaStream_t s) {
+  const int dtype = a.dtype, D = a.D;
+  DEC_DISPATCH(launch_decode, a, part, s, &ap);
 }
 
 }  // namespace screen

@@ -64,6 +64,19 @@ class PagedKVCache:
         _lib.screen_kv_append(k.to(dt), v.to(dt), positions, self.k_pages[layer],
                               self.v_pages[layer], self.block_table, eps)
 
+    def append_decode(self, layer: int, k: torch.Tensor, v: torch.Tensor,
+                      positions: torch.Tensor, q: torch.Tensor, seq_lens: torch.Tensor,
+                      r: torch.Tensor, w: torch.Tensor, eps: float = 1e-8):
+        """append(layer, k, v, positions) of one new row per sequence, then
+        decode(layer, q, ...), in one launch."""
+        dt = self.k_pages[layer].dtype
+        if self._workspace is None:
+            need = self.batch * self.num_heads * self.num_splits * self.head_dim * 4
+            self._workspace = torch.empty(need + 256, dtype=torch.uint8, device=q.device)
+        return _lib.screen_decode_append(k.to(dt), v.to(dt), positions, q.to(dt), seq_lens, r, w,
+                                         self.k_pages[layer], self.v_pages[layer],
+                                         self.block_table, eps, self.num_splits, self._workspace)
+
     def decode(self, layer: int, q: torch.Tensor, seq_lens: torch.Tensor, r: torch.Tensor,
                w: torch.Tensor, eps: float = 1e-8):
         """Screening decode of raw q (B,H,D) for the newest token of each sequence."""
