@@ -116,3 +116,28 @@ def test_kv_cache_ring_layout(ms):
             pages = [int(t[b, lb]) for lb in blocks]
             assert len(set(pages)) == len(pages)
             assert all(b * c.pages_per_seq <= p < (b + 1) * c.pages_per_seq for p in pages)
+
+
+def test_head_params_and_col_scale_host_forms(ms):
+    """The module's r / w transforms and the folded norm weight give the
+    reference's formulas (attention.py:164-165; RMSNorm weight times the
+    projection's columns) when no kernel can run (CPU parameters)."""
+    a = ms.ScreeningAttention(64, 4)
+    with torch.no_grad():
+        a.s_r.copy_(torch.tensor([-1.0, 0.0, 0.5, 2.0]))
+    r, w = a._head_params()
+    torch.testing.assert_close(r, torch.exp(a.s_r) + 1.0)
+    torch.testing.assert_close(w, torch.exp(a.s_v) + 1.0)
+    torch.testing.assert_close(r, a.sharpness())
+    g = torch.rand(64) + 0.5
+    wq = a._wqkv(g)
+    ref = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0) * g
+    torch.testing.assert_close(wq, ref)
+    assert a._wqkv().shape == (192, 64)
+
+
+def test_absorbed_norm_rejects_cross_attention(ms):
+    a = ms.ScreeningAttention(64, 4)
+    x, m = torch.randn(1, 3, 64), torch.randn(1, 5, 64)
+    with pytest.raises(ValueError):
+        a._qkv(x, m, m, torch.ones(64))
