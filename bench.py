@@ -81,6 +81,21 @@ def windowed_pairs(w: torch.Tensor, T: int, causal=True) -> float:
     return float(tot)
 
 
+def bwd_executed_tiles(w: torch.Tensor, T: int) -> int:
+    """Tiles of 128 keys x 64 queries the fused causal backward runs per
+    sequence: each key tile [j0, j0 + 127] walks the 64-query tiles from the
+    one holding j0 to the one holding min(T - 1, j0 + 127 + ceil(w) - 1)."""
+    tot = 0
+    for wh in w.tolist():
+        dmax = math.ceil(wh) - 1
+        if dmax < 0:
+            continue
+        for j0 in range(0, T, 128):
+            ihi = min(T - 1, j0 + 127 + dmax)
+            tot += ihi // 64 - j0 // 64 + 1
+    return tot
+
+
 class ClockSampler:
     """nvidia-smi sampling during the timed region."""
 
@@ -1089,6 +1104,12 @@ def run_cfg3(args, rank, world, local):
         "windowed": 7 * gemm * pairs_w / step_s / 1e12 * world,
         "fwd_executed_fraction_of_windowed": fwd_exec / (2 * gemm * pairs_w),
     }
+    # the fused backward as executed: its tiles x 6 MMA products of 128 x 64 x
+    # D (S, dP from the G hi and lo planes, dV, dK, dQ) -- beside the
+    # algorithmic 5 GEMMs per in-window pair of the roofline line
+    bwd_exec = bwd_executed_tiles(ww.cpu(), SEQ) * B * 6 * 128 * 64 * gemm
+    tflops["bwd_executed_tile"] = bwd_exec / (kt["bwd"] / 1e3) / 1e12
+    tflops["bwd_executed_tile_frac_of_peak"] = tflops["bwd_executed_tile"] / peak
     traffic = None
     tfile = REPO / "profiles" / f"{dom}_traffic.txt"
     if tfile.exists() and B == BATCH:
